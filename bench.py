@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""Benchmark of one SandMuon optimizer step on B200 (config 1 of the baseline).
+
+Workload: the 9-layer x 768 GPT matrix set -- per layer
+q/k/v/o 768x768, mlp.c_fc 3072x768, mlp.c_proj 768x3072, 54 matrices,
+63,700,992 FP32 parameters -- under RankOneAWeightedPE.  Gradients ~ N(0,
+1e-4^2), weights ~ N(0, 0.02^2), and the hook statistics of 8 microbatches x
+16384 rows (drawn like config 0) are injected as accumulated sums.  A step =
+statistics finish + Nesterov momentum + whitening + 5-stage S8 + mapback +
+graft + update (+ the statistic all-reduce and the weight all-gather when
+N > 1).  The sums are refilled before every step with one device copy (the
+step zeroes them, as in training).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  value = device ms per step, max over ranks;
+e2e = the same through the public API with pinned-host gradients/statistics
+copied in and the updated weights copied out inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SandMuon step ms & S8 GEMM TFLOP/s, 9L×768 GPT matrices, 1/2/4/8 B200"
+UNIT = "ms/step"
+LAYERS, WIDTH, HIDDEN = 9, 768, 3072
+ROWS = 8 * 16 * 1024
+LR = 1e-2
+SEED = 1337
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
+    return ap.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
+            float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def workload_config(world, partition):
+    return {
+        "workload": "cfg1: 9Lx768 GPT matrix set (54 matrices, 63.7M FP32 params), RankOneAWeightedPE step, "
+                    "statistics of 8x16384 rows injected",
+        "matrices": LAYERS * 6,
+        "params": LAYERS * (4 * WIDTH * WIDTH + 2 * WIDTH * HIDDEN),
+        "s8_precision": "stages 1-4 compensated bf16 (hi/lo, 3 products), stage 5 bf16, fp32 accumulate",
+        "l2": "no flush: each step streams ~1 GB of FP32 state (> 126 MB L2)",
+        "parallelism": f"matrix-sharded ({partition}) x{world}" if world > 1 else "single GPU",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons (one GPU)."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.samples = []
+        self.windows = []
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.monotonic(), line.strip()))
+
+    def mark(self, start, end):
+        self.windows.append((start, end))
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.2)
+        self.proc.terminate()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        inside, reasons, maxes, power = [], set(), [], []
+        for t, line in self.samples:
+            if not any(a <= t <= b for a, b in self.windows):
+                continue
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                inside.append(float(parts[0]))
+                maxes.append(float(parts[1]))
+                power.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(inside) if inside else None,
+                "sm_max_mhz": max(maxes) if maxes else None,
+                "power_w_max": max(power) if power else None,
+                "reasons": sorted(reasons), "samples": len(inside)}
+
+
+# -------------------------------------------------------------- workload
+
+def build(device, group, partition):
+    from sandmuon_b200 import RankOneAWeightedPE
+    from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    torch.manual_seed(SEED)
+    rng = np.random.default_rng(SEED)
+    model = gpt_matrix_model(LAYERS, WIDTH, HIDDEN)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
+    model.to(device)
+    opt = RankOneAWeightedPE(model, lr=LR, process_group=group, partition=partition)
+    grads_host = {}
+    for n, p in opt.named_matrices.items():
+        g = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
+        grads_host[n] = torch.from_numpy(g).pin_memory()
+        p.grad = grads_host[n].to(device)
+    stats = synth_gpt_statistics(opt, rng, count=ROWS, inject=False)
+    # every statistic sum lives in one flat buffer so a refill is one copy
+    order = []
+    for n, entry in stats.items():
+        for key in ("a_sum", "a_first_sum", "b_sum"):
+            if key in entry:
+                order.append((n, key, entry[key]))
+    total = sum(a.size for _, _, a in order)
+    flat = torch.empty(total, dtype=torch.float32, device=device)
+    src_host = torch.empty(total, dtype=torch.float32).pin_memory()
+    off = 0
+    for n, key, arr in order:
+        src_host[off:off + arr.size].copy_(torch.from_numpy(arr))
+        opt.state[opt.named_matrices[n]][key] = flat[off:off + arr.size]
+        off += arr.size
+    src_dev = src_host.to(device)
+    counts = [(opt.state[opt.named_matrices[n]], key.replace("_sum", "_count").replace("a_first_count", "a_count"))
+              for n, key, _ in order]
+
+    def refill(from_host=False):
+        flat.copy_(src_host if from_host else src_dev, non_blocking=True)
+        for st, key in counts:
+            st[key] = ROWS
+
+    return model, opt, grads_host, refill, flat.numel() * 4
+
+
+def time_steps(opt, refill, steps, device):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        refill()
+        opt.step()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / steps
+
+
+def cpu_baseline_sample(seconds=10.0):
+    """The numpy oracle on one of the nine layers (6 of 54 matrices), repeated
+    for ~`seconds`; the median is scaled by 9 to a full config-1 step."""
+    from oracle import sandmuon_oracle as orc
+    rng = np.random.default_rng(SEED)
+    shapes = {f"transformer.h.0.attn.{p}.weight": (WIDTH, WIDTH) for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
+    shapes["transformer.h.0.mlp.c_fc.weight"] = (HIDDEN, WIDTH)
+    shapes["transformer.h.0.mlp.c_proj.weight"] = (WIDTH, HIDDEN)
+    source = {n: n.replace("k_proj", "q_proj").replace("v_proj", "q_proj") for n in shapes}
+    weights = {n: (rng.standard_normal(s) * 0.02).astype(np.float32) for n, s in shapes.items()}
+    grads = {n: (rng.standard_normal(s) * 1e-4).astype(np.float32) for n, s in shapes.items()}
+    stats = {}
+    for n, (d_out, d_in) in shapes.items():
+        e = {"b_sum": (ROWS * (1e-3 * np.exp(rng.normal(0, .5, d_out))) ** 2).astype(np.float32), "b_count": ROWS}
+        if source[n] == n:
+            mean, std = rng.normal(.1, .05, d_in), np.exp(rng.normal(0, .5, d_in))
+            e.update(a_sum=(ROWS * (mean ** 2 + std ** 2)).astype(np.float32),
+                     a_first_sum=(ROWS * mean).astype(np.float32), a_count=ROWS)
+        stats[n] = e
+    opt = orc.OracleSandMuon(shapes, source, rank_one_a=True, lr=LR)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 2:
+        for n, e in stats.items():
+            opt.inject(n, **e)
+        t0 = time.perf_counter()
+        opt.step(weights, grads)
+        times.append(time.perf_counter() - t0)
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) if threadpool_info() else os.cpu_count()
+    except Exception:
+        cores = os.cpu_count()
+    return statistics.median(times[1:] if len(times) > 2 else times) * 9 * 1e3, cores, len(times)
+
+
+# ------------------------------------------------------------------- main
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    value, cores, reps = None, None, 0
+    samples = []
+    for _ in range(args.warmup):
+        cpu_baseline_sample(seconds=0.0)
+    for _ in range(args.steps):
+        v, cores, _ = cpu_baseline_sample(seconds=0.0)
+        samples.append(v)
+    value = statistics.median(samples)
+    sample = ("numpy port of the reference's eager FP32 step (oracle/sandmuon_oracle.py) on 1 of the 9 layers "
+              "(6 of 54 matrices) per step, scaled x9")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": workload_config(args.gpus, args.partition),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch.distributed as dist
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+        group = dist.group.WORLD
+    model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition)
+    sampler = ClockSampler(local)
+    for _ in range(max(args.warmup, 3)):
+        refill()
+        opt.step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    t0 = time.monotonic()
+    ms = time_steps(opt, refill, args.steps, device)
+    sampler.mark(t0, time.monotonic())
+    if world > 1:
+        dist.barrier()
+    plan = opt._last_plan
+    launches = plan.launches_per_step()
+
+    # per-launch CUDA events on the launching stream: GEMM time and FLOPs
+    plan.set_timing(True)
+    t0 = time.monotonic()
+    time_steps(opt, refill, args.steps, device)
+    sampler.mark(t0, time.monotonic())
+    timing = plan.read_timing()
+    plan.set_timing(False)
+
+    # end to end through the public API with host buffers
+    params = list(opt.named_matrices.values())
+    host_w = [torch.empty(tuple(p.shape), dtype=torch.float32).pin_memory() for p in params]
+    host_g = [grads_host[n] for n in opt.named_matrices]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.monotonic()
+    start.record()
+    for _ in range(args.steps):
+        for p, hg in zip(params, host_g):
+            p.grad.copy_(hg, non_blocking=True)
+        refill(from_host=True)
+        opt.step()
+        for p, hw in zip(params, host_w):
+            hw.copy_(p.detach(), non_blocking=True)
+    end.record()
+    torch.cuda.synchronize(device)
+    sampler.mark(t0, time.monotonic())
+    e2e_ms = start.elapsed_time(end) / args.steps
+
+    # keep the GPU under the same load for ~1 s more so clocks are sampled
+    t0 = time.monotonic()
+    while time.monotonic() - t0 < 1.0:
+        time_steps(opt, refill, 5, device)
+    sampler.mark(t0, time.monotonic())
+    clocks = sampler.summary()
+
+    vals = torch.tensor([ms, e2e_ms, timing["ms"]["gemm"], timing["gemm_flops"]], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals[:3], op=dist.ReduceOp.MAX)
+        dist.all_reduce(vals[3:], op=dist.ReduceOp.SUM)
+    ms, e2e_ms, gemm_ms, gemm_flops = vals.tolist()
+    gemm_ms /= args.steps
+    gemm_flops /= args.steps
+    peak, peak_sustained, hbm, peak_kind = peaks()
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
+    h2d = sum(g.numel() * 4 for g in host_g) + stat_bytes
+    d2h = sum(p.numel() * 4 for p in params)
+
+    if rank == 0:
+        cpu_ms, cores, reps = cpu_baseline_sample(10.0) if world == 1 else (None, None, 0)
+        line = {
+            "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 tensor cores (stages 1-4 compensated hi/lo) / fp32 state",
+            "data": "synthetic (seeded; random-init weights, N(0,1e-4) grads, injected statistics)",
+            "config": workload_config(world, args.partition),
+            "s8_gemm_tflops": round(achieved, 1),
+            "s8_gemm_ms_per_step": round(gemm_ms, 4),
+            "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_kind": f"{peak_kind} burst bf16 (sustained {peak_sustained})",
+                         "kernel": "k_gemm_bf16 (all S8 GEMM launches of a step)"},
+            "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches * args.steps),
+            "launches_per_step": launches,
+            "clocks": clocks,
+        }
+        if cpu_ms is not None:
+            line["cpu_baseline"] = {"value": round(cpu_ms, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                                    "sample": f"numpy oracle, 1 of 9 layers (6 of 54 matrices), median of {reps} "
+                                              "runs over ~10 s, scaled x9"}
+        print(json.dumps(line), flush=True)
+    opt.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,231 @@
+/*
+ * sandmuon_b200.h -- C-ABI of libsandmuon_b200.so, the B200 (sm_100a) engine
+ * behind the drop-in `sandmuon_b200` optimizer package.
+ *
+ * Conventions
+ *   - Every entry point is `extern "C"`, takes plain pointers / sizes / POD
+ *     structs, and returns an int status: 0 = success, otherwise one of the
+ *     SM_ERR_* codes below.  `sm_last_error()` returns a thread-local message
+ *     describing the last failure on the calling thread.
+ *   - Every device operation is stream-ordered on the caller-supplied
+ *     `stream` (a cudaStream_t passed as void*; NULL = legacy default stream).
+ *   - The library never allocates device memory.  The caller (PyTorch in the
+ *     Python package) allocates every tensor and workspace and passes them in.
+ *     The library keeps no references to caller memory after a call returns,
+ *     except inside an `SmPlan`, which records the pointers given at creation
+ *     and must be destroyed (or rebuilt) when any of them is freed.
+ *   - Entry points are reentrant; a plan must not be stepped concurrently from
+ *     two threads.
+ *
+ * Reference interfaces replaced (paths within the SandMuon project):
+ *   sm_stats_accumulate  <- forward hook `a_sum += x^2.sum(0)`, `a_first_sum += x.sum(0)`
+ *                           (sandmuon/optimizer.py:151-168) and the cotangent hook
+ *                           `b_sum += delta^2.sum(0)` (sandmuon/optimizer.py:170-179)
+ *   sm_plan_*            <- DiagonalWeightedPE.step matrix path
+ *                           (sandmuon/optimizer.py:224-266, 283-316) including
+ *                           _finish_a / _finish_b (:182-222), rank1_whiten (:38-45),
+ *                           _s8_fp32 (:69-93), rank1_mapback (:48-60),
+ *                           _graft_direction (:63-66)
+ *   sm_s8_polar          <- _s8_fp32 (sandmuon/optimizer.py:69-93) on a batch
+ *   sm_adamw_multi       <- auxiliary AdamW loop (sandmuon/optimizer.py:268-281)
+ *   sm_gemm_bf16         <- the dense products inside _s8_fp32 (x @ x.mT, gram @ gram,
+ *                           p @ x; sandmuon/optimizer.py:79-91); exported for unit tests
+ */
+#ifndef SANDMUON_B200_H
+#define SANDMUON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SM_ABI_VERSION 1
+
+/* status codes */
+#define SM_OK 0
+#define SM_ERR_ARG 1          /* invalid argument (shape, dtype, alignment, null) */
+#define SM_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define SM_ERR_WORKSPACE 3    /* workspace too small */
+#define SM_ERR_UNSUPPORTED 4  /* device is not sm_100 or feature unavailable */
+#define SM_ERR_DEVICE 5       /* a kernel reported a device-side error (timeout) */
+
+/* element types accepted by sm_stats_accumulate */
+#define SM_DTYPE_F32 0
+#define SM_DTYPE_BF16 1
+#define SM_DTYPE_F16 2
+#define SM_DTYPE_F64 3
+
+/* ---------------------------------------------------------------- basics */
+
+/* ABI version (SM_ABI_VERSION). */
+int sm_version(void);
+
+/* Thread-local text of the last error reported on this thread ("" if none). */
+const char* sm_last_error(void);
+
+/* Checks the current device is a B200-class sm_100 GPU and warms the library's
+ * kernels (sets their shared-memory attributes).  Returns SM_ERR_UNSUPPORTED
+ * on other devices. */
+int sm_init_device(void);
+
+/* Reads and clears the device-side status word that bounded waits inside the
+ * library's kernels set on timeout (0 = no error).  Synchronises `stream`. */
+int sm_device_status(int* status_out, void* stream);
+
+/* --------------------------------------------------- N1: hook statistics */
+
+/* Bytes of workspace sm_stats_accumulate needs for an [n_rows, n_cols] input. */
+size_t sm_stats_workspace_bytes(int64_t n_rows, int64_t n_cols);
+
+/* Column statistics of a 2-D row block, accumulated in place:
+ *   sum_sq[c] += sum_r float(x[r, c])^2
+ *   sum[c]    += sum_r float(x[r, c])        (skipped when sum == NULL)
+ * x[r, c] lives at rows + (r * row_stride + c * col_stride) * elem_size.
+ * Deterministic: a fixed two-pass reduction order, no float atomics.
+ * Replaces the forward hook (sandmuon/optimizer.py:156-168) and the cotangent
+ * hook (sandmuon/optimizer.py:170-179). */
+int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_cols,
+                        int64_t row_stride, int64_t col_stride, float* sum_sq, float* sum,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------ optimizer plan */
+
+/* One selected weight matrix (a torch Linear weight, shape [d_out, d_in],
+ * FP32, row-major and contiguous) and its persistent state. */
+typedef struct {
+    float* weight;        /* [d_out, d_in] updated in place                  */
+    float* momentum;      /* [d_out, d_in] FP32 momentum_buffer              */
+    int32_t d_out;
+    int32_t d_in;
+    int32_t a_stat;       /* index into the A-statistic table (shared q/k/v)  */
+    int32_t b_stat;       /* index into the B-statistic table                 */
+} SmMatrixSpec;
+
+/* One activation (A) or cotangent (B) statistic vector and its EMA state. */
+typedef struct {
+    float* sum;           /* a_sum / b_sum  [n] (zeroed by the step)          */
+    float* first_sum;     /* a_first_sum [n] (rank-one A only, else NULL)     */
+    float* ema;           /* a_ema / b_ema [n]                                */
+    float* mean_ema;      /* a_mean_ema [n] (rank-one A only, else NULL)      */
+    int32_t n;            /* vector length                                    */
+    int32_t kind;         /* SM_STAT_A_DIAG, SM_STAT_A_RANK1 or SM_STAT_B     */
+} SmStatSpec;
+
+#define SM_STAT_A_DIAG 0
+#define SM_STAT_A_RANK1 1
+#define SM_STAT_B 2
+
+typedef struct {
+    const SmMatrixSpec* matrices;
+    int32_t n_matrices;
+    const SmStatSpec* stats;
+    int32_t n_stats;
+    float statistic_beta;    /* 0.97 (sandmuon/optimizer.py:123)            */
+    float momentum;          /* 0.8  (sandmuon/optimizer.py:139)            */
+} SmPlanSpec;
+
+typedef struct SmPlan SmPlan;
+
+/* Per-step dynamic inputs. Arrays are host memory, indexed like the spec. */
+typedef struct {
+    const float* const* grads;   /* [n_matrices] device pointers to FP32 grads, same
+                                    layout as the weight                           */
+    const float* lrs;            /* [n_matrices] learning rate of each matrix      */
+    const int64_t* counts;       /* [n_stats] rows accumulated into each statistic */
+    const int32_t* ema_init;     /* [n_stats] 1 = first step: EMA <- value (copy)  */
+} SmStepArgs;
+
+/* Workspace bytes a plan needs (256-byte aligned pointer required). */
+int sm_plan_workspace_bytes(const SmPlanSpec* spec, size_t* bytes_out);
+
+/* Builds a plan: groups matrices by oriented S8 shape (rows <= cols), lays the
+ * workspace out, zeroes its padding on `stream`, and encodes TMA descriptors. */
+int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_bytes,
+                   void* stream, SmPlan** plan_out);
+
+/* One optimizer step for every matrix of the plan:
+ *   finish statistics (EMA, inverse square roots, rank-one factors; sums zeroed)
+ *   -> Nesterov momentum -> two-sided whitening -> 5-stage S8 polynomial
+ *   (stages 1-4 compensated BF16 -- hi/lo operand planes, three products --
+ *   and stage 5 plain BF16, FP32 accumulation throughout, on tcgen05)
+ *   -> mapback -> Frobenius graft to sqrt(d_out) -> W -= lr * direction. */
+int sm_plan_step(SmPlan* plan, const SmStepArgs* args, void* stream);
+
+/* Optional per-kernel-class timing with CUDA events (for the benchmark).
+ * When enabled, sm_plan_step records an event pair around each launch;
+ * sm_plan_timing_read synchronises, returns totals in ms per class and the
+ * launch counts, and resets the accumulators.  Classes: see SM_TCLASS_*. */
+#define SM_TCLASS_GEMM 0
+#define SM_TCLASS_ELEMWISE 1
+#define SM_TCLASS_STATS 2
+#define SM_TCLASS_COUNT 3
+int sm_plan_set_timing(SmPlan* plan, int enabled);
+int sm_plan_timing_read(SmPlan* plan, double* ms_out, int64_t* launches_out,
+                        double* gemm_flops_out);
+
+/* Number of kernels one sm_plan_step launches. */
+int sm_plan_launches_per_step(const SmPlan* plan, int64_t* out);
+
+int sm_plan_destroy(SmPlan* plan);
+
+/* --------------------------------------------------------- S8 (batch) */
+
+/* Workspace for sm_s8_polar on a batch of `batch` [rows, cols] matrices. */
+size_t sm_s8_workspace_bytes(int32_t batch, int32_t rows, int32_t cols);
+
+/* out[b] = S8(x[b]) for a contiguous FP32 batch [batch, rows, cols]; the same
+ * oriented pipeline the plan runs (transposes when rows > cols). All-zero
+ * matrices give exact zeros.  Replaces _s8_fp32 (sandmuon/optimizer.py:69-93). */
+int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t cols,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- N8: auxiliary AdamW */
+
+typedef struct {
+    float* param;
+    const float* grad;
+    float* exp_avg;
+    float* exp_avg_sq;
+    int64_t numel;
+    float bias_correction1;   /* 1 - beta1^step, computed on the host in double */
+    float bias_correction2;   /* 1 - beta2^step                                  */
+} SmAdamTensor;
+
+/* One fused multi-tensor AdamW update (sandmuon/optimizer.py:268-281):
+ *   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g^2
+ *   u = (m / bc1) / (sqrt(v / bc2) + eps) ; p *= decay_factor ; p -= lr * u
+ * decay_factor = 1 - lr * weight_decay (host-computed). */
+int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float beta1,
+                   float beta2, float eps, float decay_factor, void* stream);
+
+/* ------------------------------------------------- GEMM (unit testing) */
+
+#define SM_EPI_F32 0        /* C = alpha * acc (FP32)                          */
+#define SM_EPI_BF16 1       /* C = bf16(alpha * acc)                           */
+#define SM_EPI_HILO 2       /* C_hi = bf16(alpha*acc), C_lo = bf16(rest)       */
+#define SM_EPI_F32_NORM 3   /* FP32 store + per-tile sum of squares partials  */
+#define SM_EPI_POLY 4       /* C = bf16(pa*I + pb*aux + pc*acc)                */
+#define SM_EPI_POLY_HILO 5  /* P = pa*I + pb*(aux + aux_lo) + pc*acc -> hi/lo  */
+
+/* Batched C[b] = A[b] * op(B[b]) on tcgen05 tensor cores.
+ *   A: [batch, M, K] BF16 row-major (K contiguous); a_lo != NULL selects the
+ *      compensated 3-product mode (a_hi*b_lo + a_lo*b_hi + a_hi*b_hi), which
+ *      then also needs b_lo.
+ *   B: b_kmajor = 1 -> [batch, N, K] (C = A B^T);  0 -> [batch, K, N] (C = A B).
+ *   M % 128 == 0, N % 128 == 0, K % 64 == 0.
+ *   out0/out1: outputs [batch, M, N] (out1 = lo plane for SM_EPI_HILO).
+ *   alpha: device [batch] FP32 scales or NULL (1).  aux (and aux_lo for the
+ *   hi/lo polynomial): BF16 [batch, M, N] for SM_EPI_POLY / SM_EPI_POLY_HILO.
+ *   partials: device FP32 [batch, (M/128)*(N/BN)*4] for SM_EPI_F32_NORM. */
+int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo,
+                 int b_kmajor, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
+                 void* out0, void* out1, const float* alpha, const void* aux, const void* aux_lo,
+                 float pa, float pb, float pc, float* partials, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SANDMUON_B200_H */

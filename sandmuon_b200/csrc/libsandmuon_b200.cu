@@ -1,0 +1,1133 @@
+// libsandmuon_b200.cu -- host runtime and C-ABI of the SandMuon B200 engine.
+//
+// One translation unit: the kernels (sm_gemm.cuh, sm_kernels.cuh), the plan
+// executor that sequences a whole optimizer step from a single C call, and the
+// extern "C" entry points declared in include/sandmuon_b200.h.
+//
+// Memory: the library allocates nothing on the device.  Callers pass every
+// buffer; a plan carves its workspace into per-shape-group buffers:
+//   xh|xl  BF16 [B, rp, cp] x2  hi/lo planes of the S8 iterate: stages 1, 3, 5
+//                               read it (stage 5 reads the hi plane only)
+//   xa|xb  BF16 [B, rp, cp] x2  hi/lo planes of the iterate of stages 2 and 4;
+//                               the final FP32 S8 output Q [B, rp, cp] reuses
+//                               these bytes
+//   gh, gl BF16 [B, rp, rp]     gram hi/lo (stage 1: P hi/lo in place after);
+//                               stage 5: gh = gram, gl = polynomial P
+//   g2     FP32 [B, rp, rp]     stage-1 gram^2; stages 2-4: P hi/lo planes
+//   + per-row float2 statistics, per-tile partial sums, per-matrix scalars.
+// rp, cp are the oriented rows/cols (rows <= cols) padded to multiples of 128;
+// padding is zeroed at plan creation and stays zero through every stage.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "sm_common.cuh"
+#include "sm_gemm.cuh"
+#include "sm_kernels.cuh"
+
+namespace smb {
+
+// S8 constants (sandmuon/coefficients.py:3-10).
+constexpr float kS8Margin = 1.35f;
+constexpr double kS8Coeff[5][3] = {
+    {11.062126275847973, -56.051653229128085, 72.32081107619855},
+    {4.100720073616268, -2.9324183165353577, 0.5339692084282731},
+    {3.930310192522361, -2.873509793709714, 0.5366557527206212},
+    {3.280567968245866, -2.414925589994015, 0.48635134757825227},
+    {2.282741575232451, -1.6302296637355072, 0.40275720810675486},
+};
+
+thread_local std::string t_last_error;
+
+static int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+#define SM_CUDA(call)                                                                       \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(SM_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define SM_LAUNCHED()                                                                        \
+  do {                                                                                       \
+    cudaError_t e_ = cudaGetLastError();                                                     \
+    if (e_ != cudaSuccess) return fail(SM_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define SM_TRY(expr)          \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != SM_OK) return rc_; \
+  } while (0)
+
+static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+static inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+// ------------------------------------------------------------ device info
+
+struct DeviceInfo {
+  int sms = 0;
+  bool attrs_set = false;
+};
+static std::mutex g_dev_mutex;
+static DeviceInfo g_dev[64];
+
+static int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    int major = 0, minor = 0;
+    SM_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    SM_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      return fail(SM_ERR_UNSUPPORTED, "libsandmuon_b200 requires an sm_100 (B200) GPU; found sm_" +
+                                          std::to_string(major) + std::to_string(minor));
+    SM_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  *out = &d;
+  return SM_OK;
+}
+
+// ------------------------------------------------------------- tensor maps
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encode(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  static std::once_flag once;
+  static int status = SM_OK;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      status = SM_ERR_UNSUPPORTED;
+    } else {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (status != SM_OK) return fail(status, "cuTensorMapEncodeTiled is unavailable");
+  *out = g_encode;
+  return SM_OK;
+}
+
+// 3-D BF16 tensor [batch, outer, inner] (inner contiguous), box {64, box_outer, 1},
+// 128-byte swizzle.  inner * 2 bytes must be a multiple of 16.
+static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t batch,
+                    uint32_t box_outer) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  SM_TRY(get_encode(&enc));
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(SM_ERR_ARG, "TMA base not 16-byte aligned");
+  if ((inner * 2) % 16 != 0) return fail(SM_ERR_ARG, "TMA row stride not a multiple of 16 bytes");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner * 2), static_cast<cuuint64_t>(inner * outer * 2)};
+  cuuint32_t box[3] = {64, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SM_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return SM_OK;
+}
+
+// ------------------------------------------------------------ GEMM launch
+
+template <int BN, bool COMP, bool B_MN, int EPI>
+static int launch_gemm_t(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+                         const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
+  constexpr int STAGES = COMP ? (BN == 256 ? 2 : 3) : (BN == 256 ? 4 : 6);
+  using L = GemmSmem<BN, COMP, STAGES>;
+  static_assert(L::kTotal <= 232448, "shared memory budget");
+  auto kern = k_gemm_bf16<BN, COMP, B_MN, STAGES, EPI>;
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  // The attribute is per function and device; set it once per device.
+  static bool attr_done[64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    attr_done[dev] = true;
+  }
+  const int total = a.tiles_m * a.tiles_n * a.batch;
+  if (total == 0) return SM_OK;
+  const int grid = std::min(total, di->sms);
+  kern<<<grid, kGemmThreads, L::kTotal, st>>>(ah, al, bh, bl, a);
+  SM_LAUNCHED();
+  return SM_OK;
+}
+
+template <int BN>
+static int dispatch_gemm_bn(bool comp, bool b_mn, int epi, const CUtensorMap& ah, const CUtensorMap& al,
+                            const CUtensorMap& bh, const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
+  if (!comp) {
+    if (!b_mn) {
+      switch (epi) {
+        case kEpiF32: return launch_gemm_t<BN, false, false, kEpiF32>(ah, al, bh, bl, a, st);
+        case kEpiBF16: return launch_gemm_t<BN, false, false, kEpiBF16>(ah, al, bh, bl, a, st);
+        case kEpiPoly: return launch_gemm_t<BN, false, false, kEpiPoly>(ah, al, bh, bl, a, st);
+        default: break;
+      }
+    } else {
+      switch (epi) {
+        case kEpiF32: return launch_gemm_t<BN, false, true, kEpiF32>(ah, al, bh, bl, a, st);
+        case kEpiBF16: return launch_gemm_t<BN, false, true, kEpiBF16>(ah, al, bh, bl, a, st);
+        default: break;
+      }
+    }
+  } else {
+    if (!b_mn) {
+      switch (epi) {
+        case kEpiF32: return launch_gemm_t<BN, true, false, kEpiF32>(ah, al, bh, bl, a, st);
+        case kEpiBF16: return launch_gemm_t<BN, true, false, kEpiBF16>(ah, al, bh, bl, a, st);
+        case kEpiHiLo: return launch_gemm_t<BN, true, false, kEpiHiLo>(ah, al, bh, bl, a, st);
+        case kEpiF32Norm: return launch_gemm_t<BN, true, false, kEpiF32Norm>(ah, al, bh, bl, a, st);
+        case kEpiPolyHiLo: return launch_gemm_t<BN, true, false, kEpiPolyHiLo>(ah, al, bh, bl, a, st);
+        default: break;
+      }
+    } else {
+      switch (epi) {
+        case kEpiF32: return launch_gemm_t<BN, true, true, kEpiF32>(ah, al, bh, bl, a, st);
+        case kEpiBF16: return launch_gemm_t<BN, true, true, kEpiBF16>(ah, al, bh, bl, a, st);
+        case kEpiHiLo: return launch_gemm_t<BN, true, true, kEpiHiLo>(ah, al, bh, bl, a, st);
+        default: break;
+      }
+    }
+  }
+  return fail(SM_ERR_ARG, "unsupported GEMM mode combination (compensated=" + std::to_string(comp) +
+                              ", b_mn_major=" + std::to_string(b_mn) + ", epilogue=" + std::to_string(epi) + ")");
+}
+
+static int dispatch_gemm(int bn, bool comp, bool b_mn, int epi, const CUtensorMap& ah, const CUtensorMap& al,
+                         const CUtensorMap& bh, const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
+  if (bn == 256) return dispatch_gemm_bn<256>(comp, b_mn, epi, ah, al, bh, bl, a, st);
+  if (bn == 128) return dispatch_gemm_bn<128>(comp, b_mn, epi, ah, al, bh, bl, a, st);
+  return fail(SM_ERR_ARG, "BN must be 128 or 256");
+}
+
+static inline int pick_bn(int64_t n) { return (n % 256 == 0) ? 256 : 128; }
+
+// ------------------------------------------------------------------- timing
+
+struct Timer {
+  bool enabled = false;
+  std::vector<cudaEvent_t> pool;
+  struct Rec {
+    int cls;
+    cudaEvent_t a, b;
+    double flops;
+  };
+  std::vector<Rec> recs;
+  size_t next = 0;
+
+  // Records the opening event; *idx = record index (or -1 when disabled).
+  int begin(int cls, double flops, cudaStream_t st, long* idx) {
+    *idx = -1;
+    if (!enabled) return SM_OK;
+    while (pool.size() < next + 2) {
+      cudaEvent_t e;
+      SM_CUDA(cudaEventCreate(&e));
+      pool.push_back(e);
+    }
+    Rec r{cls, pool[next], pool[next + 1], flops};
+    next += 2;
+    SM_CUDA(cudaEventRecord(r.a, st));
+    recs.push_back(r);
+    *idx = static_cast<long>(recs.size()) - 1;
+    return SM_OK;
+  }
+  int end(long idx, cudaStream_t st) {
+    if (idx < 0) return SM_OK;
+    SM_CUDA(cudaEventRecord(recs[idx].b, st));
+    return SM_OK;
+  }
+};
+
+// Runs `body` bracketed by timing events of class `cls` when timing is on.
+#define SM_TIMED(timer, cls, flops, stream, body)        \
+  do {                                                   \
+    long rec_ = -1;                                      \
+    if ((timer) != nullptr) SM_TRY((timer)->begin((cls), (flops), (stream), &rec_)); \
+    SM_TRY(body);                                        \
+    if ((timer) != nullptr) SM_TRY((timer)->end(rec_, (stream))); \
+  } while (0)
+
+// ------------------------------------------------------------------ groups
+
+struct Group {
+  int r = 0, c = 0;      // oriented shape, r <= c
+  int rp = 0, cp = 0;    // padded to multiples of 128
+  int bn_r = 0, bn_c = 0;
+  int batch = 0;
+  int mat_off = 0;       // first descriptor of this group in the MatDev table
+  bool rank1 = false;
+  int dmax = 0;          // leading dimension of the per-row statistic arrays
+  __nv_bfloat16 *xh = nullptr, *xl = nullptr, *xa = nullptr, *xb = nullptr, *gh = nullptr, *gl = nullptr;
+  __nv_bfloat16 *ph = nullptr, *pl = nullptr;
+  float *q = nullptr, *g2 = nullptr, *partials = nullptr;
+  float *inv_norm = nullptr, *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
+  float2 *rs_white = nullptr, *rs_map = nullptr;
+  CUtensorMap xh_A, xl_A, xh_Bk, xl_Bk, xh_Bmn, xl_Bmn;
+  CUtensorMap gh_A, gl_A, gh_Bk, gl_Bk;
+  CUtensorMap xa_A, xa_Bk, xa_Bmn, xb_A, xb_Bk, xb_Bmn;
+  CUtensorMap ph_A, pl_A;
+};
+
+// Bump allocator over a caller workspace (or a null base to measure).
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = round_up(static_cast<int64_t>(off), 256);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+static void carve_group(Carver& cv, Group& g) {
+  const size_t xs = static_cast<size_t>(g.batch) * g.rp * g.cp;
+  const size_t gs = static_cast<size_t>(g.batch) * g.rp * g.rp;
+  g.xh = cv.take<__nv_bfloat16>(2 * xs);  // xh | xl contiguous
+  g.xl = g.xh ? g.xh + xs : nullptr;
+  g.xa = cv.take<__nv_bfloat16>(2 * xs);  // xa | xb contiguous; q aliases both planes
+  g.xb = g.xa ? g.xa + xs : nullptr;
+  g.q = reinterpret_cast<float*>(g.xa);
+  g.gh = cv.take<__nv_bfloat16>(gs);
+  g.gl = cv.take<__nv_bfloat16>(gs);
+  g.g2 = cv.take<float>(gs);
+  g.ph = reinterpret_cast<__nv_bfloat16*>(g.g2);  // P hi | P lo in the g2 bytes
+  g.pl = g.ph ? g.ph + gs : nullptr;
+  const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * 4;
+  g.partials = cv.take<float>(static_cast<size_t>(g.batch) * per_mat);
+  g.inv_norm = cv.take<float>(g.batch);
+  g.s = cv.take<float>(g.batch);
+  g.s_inv = cv.take<float>(g.batch);
+  g.gamma = cv.take<float>(g.batch);
+  g.rs_white = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
+  g.rs_map = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
+}
+
+static int encode_group_maps(Group& g) {
+  SM_TRY(make_map(&g.xh_A, g.xh, g.cp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.xl_A, g.xl, g.cp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.xh_Bk, g.xh, g.cp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.xl_Bk, g.xl, g.cp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.xh_Bmn, g.xh, g.cp, g.rp, g.batch, 64));
+  SM_TRY(make_map(&g.xl_Bmn, g.xl, g.cp, g.rp, g.batch, 64));
+  SM_TRY(make_map(&g.gh_A, g.gh, g.rp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.gl_A, g.gl, g.rp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.gh_Bk, g.gh, g.rp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.gl_Bk, g.gl, g.rp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.xa_A, g.xa, g.cp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.xa_Bk, g.xa, g.cp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.xa_Bmn, g.xa, g.cp, g.rp, g.batch, 64));
+  SM_TRY(make_map(&g.xb_A, g.xb, g.cp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.xb_Bk, g.xb, g.cp, g.rp, g.batch, g.bn_r));
+  SM_TRY(make_map(&g.xb_Bmn, g.xb, g.cp, g.rp, g.batch, 64));
+  SM_TRY(make_map(&g.ph_A, g.ph, g.rp, g.rp, g.batch, kGemmBM));
+  SM_TRY(make_map(&g.pl_A, g.pl, g.rp, g.rp, g.batch, kGemmBM));
+  return SM_OK;
+}
+
+static void init_group_shape(Group& g, int r, int c, int batch) {
+  g.r = r;
+  g.c = c;
+  g.rp = static_cast<int>(round_up(r, 128));
+  g.cp = static_cast<int>(round_up(c, 128));
+  g.bn_r = pick_bn(g.rp);
+  g.bn_c = pick_bn(g.cp);
+  g.batch = batch;
+  g.dmax = c;
+}
+
+static GemmArgs gemm_args(int m, int n, int k, int batch, int bn) {
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.batch = batch;
+  a.tiles_m = m / kGemmBM;
+  a.tiles_n = n / bn;
+  return a;
+}
+
+static double gemm_flops(const GemmArgs& a, bool comp) {
+  return 2.0 * a.m * a.n * static_cast<double>(a.k) * a.batch * (comp ? 3.0 : 1.0);
+}
+
+// Stage schedule of the S8 polynomial: stages 1-4 compensated (hi/lo operand
+// planes, three BF16 products, FP32 accumulation), stage 5 plain BF16.
+// Keeping stage 2-4 iterates at ~16 significant bits holds the map within
+// 1e-2 relative Frobenius error of the FP32 reference even for rank-deficient
+// inputs, whose near-zero singular values the later stages amplify ~120x.
+constexpr int kCompensatedStages = 4;
+
+// The five-stage S8 polynomial on the group's stage-1 planes xh/xl (already
+// normalised, oriented, zero-padded).  Result: FP32 Q [B, rp, cp] in g.q.
+// Mirrors _s8_fp32 (sandmuon/optimizer.py:79-91).
+static int run_s8(const Group& g, cudaStream_t st, Timer* tm, int64_t* launches) {
+  const int rp = g.rp, cp = g.cp, B = g.batch;
+  // stage 1: G = X X^T (hi/lo), G2 = G G (FP32 + norm partials)
+  {
+    GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
+    a.out0 = g.gh;
+    a.out1 = g.gl;
+    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+             dispatch_gemm(g.bn_r, true, false, kEpiHiLo, g.xh_A, g.xl_A, g.xh_Bk, g.xl_Bk, a, st));
+    ++*launches;
+  }
+  {
+    GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
+    a.out0 = g.g2;
+    a.partials = g.partials;
+    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+             dispatch_gemm(g.bn_r, true, false, kEpiF32Norm, g.gh_A, g.gl_A, g.gh_Bk, g.gl_Bk, a, st));
+    ++*launches;
+  }
+  {
+    const int per_mat = (rp / kGemmBM) * (rp / g.bn_r) * 4;
+    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+               k_reduce_s8scale<<<B, 256, 0, st>>>(g.partials, per_mat, kS8Margin, g.s, g.s_inv);
+               SM_LAUNCHED();
+               return SM_OK;
+             }()));
+    const int64_t per = static_cast<int64_t>(rp) * rp;
+    const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 2, 256), 512));
+    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+               k_poly_stage1<<<dim3(blocks, B), 256, 0, st>>>(g.gh, g.gl, g.g2, g.s, rp, (float)kS8Coeff[0][0],
+                                                               (float)kS8Coeff[0][1], (float)kS8Coeff[0][2]);
+               SM_LAUNCHED();
+               return SM_OK;
+             }()));
+    *launches += 2;
+  }
+  {
+    // X2 = (P X) / s, emitted as hi/lo planes into xa|xb
+    GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
+    a.out0 = g.xa;
+    a.out1 = g.xb;
+    a.alpha = g.s_inv;
+    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+             dispatch_gemm(g.bn_c, true, true, kEpiHiLo, g.gh_A, g.gl_A, g.xh_Bmn, g.xl_Bmn, a, st));
+    ++*launches;
+  }
+  // stages 2..5: the iterate alternates between the xa|xb and xh|xl pairs
+  for (int stage = 1; stage < 5; ++stage) {
+    const bool in_a = (stage % 2) == 1;  // stages 2 and 4 read xa|xb
+    const bool comp = stage < kCompensatedStages;
+    const bool next_comp = stage + 1 < kCompensatedStages;
+    const bool last = stage == 4;
+    const CUtensorMap& xA_h = in_a ? g.xa_A : g.xh_A;
+    const CUtensorMap& xA_l = in_a ? g.xb_A : g.xl_A;
+    const CUtensorMap& xBk_h = in_a ? g.xa_Bk : g.xh_Bk;
+    const CUtensorMap& xBk_l = in_a ? g.xb_Bk : g.xl_Bk;
+    const CUtensorMap& xBmn_h = in_a ? g.xa_Bmn : g.xh_Bmn;
+    const CUtensorMap& xBmn_l = in_a ? g.xb_Bmn : g.xl_Bmn;
+    __nv_bfloat16* out_h = in_a ? g.xh : g.xa;
+    __nv_bfloat16* out_l = in_a ? g.xl : g.xb;
+    const float pa = static_cast<float>(kS8Coeff[stage][0]);
+    const float pb = static_cast<float>(kS8Coeff[stage][1]);
+    const float pc = static_cast<float>(kS8Coeff[stage][2]);
+    if (comp) {
+      {  // G = X X^T as hi/lo
+        GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
+        a.out0 = g.gh;
+        a.out1 = g.gl;
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+                 dispatch_gemm(g.bn_r, true, false, kEpiHiLo, xA_h, xA_l, xBk_h, xBk_l, a, st));
+      }
+      {  // P = a I + b G + c G G as hi/lo (into the g2 bytes)
+        GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
+        a.out0 = g.ph;
+        a.out1 = g.pl;
+        a.aux = g.gh;
+        a.aux_lo = g.gl;
+        a.pa = pa;
+        a.pb = pb;
+        a.pc = pc;
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+                 dispatch_gemm(g.bn_r, true, false, kEpiPolyHiLo, g.gh_A, g.gl_A, g.gh_Bk, g.gl_Bk, a, st));
+      }
+      {  // X' = P X (hi/lo for a compensated next stage, else BF16)
+        GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
+        a.out0 = out_h;
+        a.out1 = out_l;
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
+                 dispatch_gemm(g.bn_c, true, true, next_comp ? kEpiHiLo : kEpiBF16, g.ph_A, g.pl_A, xBmn_h,
+                               xBmn_l, a, st));
+      }
+    } else {
+      {  // G = X X^T (BF16)
+        GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
+        a.out0 = g.gh;
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
+                 dispatch_gemm(g.bn_r, false, false, kEpiBF16, xA_h, xA_h, xBk_h, xBk_h, a, st));
+      }
+      {  // P = a I + b G + c G G (BF16)
+        GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
+        a.out0 = g.gl;
+        a.aux = g.gh;
+        a.pa = pa;
+        a.pb = pb;
+        a.pc = pc;
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
+                 dispatch_gemm(g.bn_r, false, false, kEpiPoly, g.gh_A, g.gh_A, g.gh_Bk, g.gh_Bk, a, st));
+      }
+      {  // X' = P X; the last stage writes FP32 Q over the xa|xb bytes
+        GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
+        if (last && in_a) return fail(SM_ERR_ARG, "stage schedule would overwrite the last iterate");
+        a.out0 = last ? static_cast<void*>(g.q) : static_cast<void*>(out_h);
+        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
+                 dispatch_gemm(g.bn_c, false, true, last ? kEpiF32 : kEpiBF16, g.gl_A, g.gl_A, xBmn_h, xBmn_h, a,
+                               st));
+      }
+    }
+    *launches += 3;
+  }
+  return SM_OK;
+}
+
+// Whitening / normalisation front end for one group (N3 passes 1 and 2).
+static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float mom_omb, bool vec4,
+                     cudaStream_t st, Timer* tm, int64_t* launches) {
+  const int B = g.batch;
+  const int ld = g.dmax;
+  const MatDev* mats = d_mats + g.mat_off;
+  SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
+             if (g.rank1) {
+               if (vec4) k_whiten_rowstats<4, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
+               else k_whiten_rowstats<1, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
+             } else {
+               if (vec4) k_whiten_rowstats<4, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
+               else k_whiten_rowstats<1, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
+             }
+             SM_LAUNCHED();
+             k_reduce_invnorm<<<B, 256, 0, st>>>(mats, g.rs_white, ld, g.inv_norm);
+             SM_LAUNCHED();
+             return SM_OK;
+           }()));
+  SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), B);
+             if (g.rank1) {
+               if (vec4) k_whiten_write<true, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
+               else k_whiten_write<true, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
+             } else {
+               if (vec4) k_whiten_write<false, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
+               else k_whiten_write<false, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
+             }
+             SM_LAUNCHED();
+             return SM_OK;
+           }()));
+  *launches += 3;
+  return SM_OK;
+}
+
+// Mapback + graft + update back end for one group (N7 passes 1 and 2).
+static int run_back(const Group& g, const MatDev* d_mats, bool has_trans, bool has_plain, cudaStream_t st,
+                    Timer* tm, int64_t* launches) {
+  const int B = g.batch;
+  const int ld = g.dmax;
+  const MatDev* mats = d_mats + g.mat_off;
+  SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+             if (has_plain) {
+               dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
+               if (g.rank1) k_mapback_rowstats_rows<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+               else k_mapback_rowstats_rows<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+               SM_LAUNCHED();
+             }
+             if (has_trans) {
+               dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 256)), B);
+               if (g.rank1) k_mapback_rowstats_cols<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+               else k_mapback_rowstats_cols<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+               SM_LAUNCHED();
+             }
+             k_reduce_graft<<<B, 256, 0, st>>>(mats, g.rs_map, ld, g.gamma);
+             SM_LAUNCHED();
+             return SM_OK;
+           }()));
+  SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), B);
+             if (g.rank1) k_mapback_apply<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+             else k_mapback_apply<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+             SM_LAUNCHED();
+             return SM_OK;
+           }()));
+  *launches += (has_plain ? 1 : 0) + (has_trans ? 1 : 0) + 2;
+  return SM_OK;
+}
+
+}  // namespace smb
+
+using namespace smb;
+
+// ==================================================================== plan
+
+struct SmPlan {
+  int device = 0;
+  std::vector<SmMatrixSpec> mats;
+  std::vector<SmStatSpec> stats;
+  std::vector<Group> groups;
+  std::vector<int> order;        // table position -> matrix index
+  std::vector<int> mat_group;    // matrix index -> group
+  std::vector<int> mat_slot;     // matrix index -> slot within group
+  float stat_beta = 0.97f, stat_omb = 0.03f;
+  float mom_beta = 0.8f, mom_omb = 0.2f;
+  MatDev* d_mats = nullptr;
+  StatDev* d_stats = nullptr;
+  size_t table_bytes = 0;
+  std::vector<uint8_t> h_table;
+  // per-stat outputs
+  std::vector<float*> s_inv, s_z, s_zeta, s_scal;
+  std::vector<uint8_t> group_has_trans, group_has_plain;
+  Timer timer;
+  int64_t launches_last = 0;
+};
+
+namespace smb {
+
+__global__ void k_fill(float* p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+
+static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* bytes) {
+  if (spec == nullptr || spec->n_matrices < 0 || spec->n_stats < 0)
+    return fail(SM_ERR_ARG, "null or negative plan spec");
+  Carver cv(ws);
+  const int nm = spec->n_matrices, ns = spec->n_stats;
+  // group discovery (oriented shape, first-appearance order)
+  std::vector<std::pair<int, int>> shapes;
+  std::vector<int> mg(nm), slot(nm);
+  std::vector<int> counts;
+  for (int i = 0; i < nm; ++i) {
+    const SmMatrixSpec& m = spec->matrices[i];
+    if (m.d_out <= 0 || m.d_in <= 0) return fail(SM_ERR_ARG, "matrix with empty shape");
+    if (m.a_stat < 0 || m.a_stat >= ns || m.b_stat < 0 || m.b_stat >= ns)
+      return fail(SM_ERR_ARG, "matrix statistic index out of range");
+    const SmStatSpec& sa = spec->stats[m.a_stat];
+    const SmStatSpec& sb = spec->stats[m.b_stat];
+    if (sa.kind == SM_STAT_B || sb.kind != SM_STAT_B) return fail(SM_ERR_ARG, "statistic kinds do not match sides");
+    if (sa.n != m.d_in || sb.n != m.d_out) return fail(SM_ERR_ARG, "statistic length does not match matrix shape");
+    const int r = std::min(m.d_out, m.d_in), c = std::max(m.d_out, m.d_in);
+    int g = -1;
+    for (size_t k = 0; k < shapes.size(); ++k)
+      if (shapes[k].first == r && shapes[k].second == c) g = static_cast<int>(k);
+    if (g < 0) {
+      g = static_cast<int>(shapes.size());
+      shapes.push_back({r, c});
+      counts.push_back(0);
+    }
+    mg[i] = g;
+    slot[i] = counts[g]++;
+  }
+  std::vector<Group> groups(shapes.size());
+  int off = 0;
+  for (size_t g = 0; g < shapes.size(); ++g) {
+    init_group_shape(groups[g], shapes[g].first, shapes[g].second, counts[g]);
+    groups[g].mat_off = off;
+    off += counts[g];
+    bool any_r1 = false, any_diag = false;
+    for (int i = 0; i < nm; ++i) {
+      if (mg[i] != static_cast<int>(g)) continue;
+      const int kind = spec->stats[spec->matrices[i].a_stat].kind;
+      if (kind == SM_STAT_A_RANK1) any_r1 = true;
+      else any_diag = true;
+    }
+    if (any_r1 && any_diag) return fail(SM_ERR_ARG, "a shape group mixes rank-one and diagonal A statistics");
+    groups[g].rank1 = any_r1;
+  }
+  MatDev* d_mats = cv.take<MatDev>(nm);
+  StatDev* d_stats = cv.take<StatDev>(ns);
+  std::vector<float*> s_inv(ns), s_z(ns), s_zeta(ns), s_scal(ns);
+  for (int s = 0; s < ns; ++s) {
+    const SmStatSpec& st = spec->stats[s];
+    if (st.n <= 0) return fail(SM_ERR_ARG, "statistic with empty length");
+    s_inv[s] = cv.take<float>(st.n);
+    s_z[s] = st.kind == SM_STAT_A_RANK1 ? cv.take<float>(st.n) : nullptr;
+    s_zeta[s] = st.kind == SM_STAT_A_RANK1 ? cv.take<float>(st.n) : nullptr;
+    s_scal[s] = cv.take<float>(4);
+  }
+  for (auto& g : groups) carve_group(cv, g);
+  *bytes = round_up(static_cast<int64_t>(cv.off), 256);
+  if (plan != nullptr) {
+    plan->mats.assign(spec->matrices, spec->matrices + nm);
+    plan->stats.assign(spec->stats, spec->stats + ns);
+    plan->groups = groups;
+    plan->mat_group = mg;
+    plan->mat_slot = slot;
+    plan->order.assign(nm, 0);
+    for (int i = 0; i < nm; ++i) plan->order[groups[mg[i]].mat_off + slot[i]] = i;
+    plan->d_mats = d_mats;
+    plan->d_stats = d_stats;
+    plan->table_bytes = reinterpret_cast<uint8_t*>(d_stats + ns) - reinterpret_cast<uint8_t*>(d_mats);
+    plan->s_inv = s_inv;
+    plan->s_z = s_z;
+    plan->s_zeta = s_zeta;
+    plan->s_scal = s_scal;
+    plan->group_has_trans.assign(groups.size(), 0);
+    plan->group_has_plain.assign(groups.size(), 0);
+    for (int i = 0; i < nm; ++i) {
+      const bool tr = spec->matrices[i].d_out > spec->matrices[i].d_in;
+      (tr ? plan->group_has_trans : plan->group_has_plain)[mg[i]] = 1;
+    }
+  }
+  return SM_OK;
+}
+
+static int stats_splits(int64_t n_rows, int64_t n_cols, int vec, int sms) {
+  const int64_t col_blocks = cdiv(n_cols, 32 * vec);
+  int64_t splits = cdiv(4 * static_cast<int64_t>(sms), col_blocks);
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, cdiv(n_rows, 32)));
+  const int64_t rps = cdiv(n_rows, splits);
+  return static_cast<int>(cdiv(n_rows, rps));
+}
+
+template <typename T>
+static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
+                        float* sum, void* ws, size_t ws_bytes, cudaStream_t st, int sms) {
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec_ok = cs == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                      ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
+  const int vec = vec_ok ? kVec : 1;
+  const int splits = stats_splits(n_rows, n_cols, vec, sms);
+  const int64_t rps = cdiv(n_rows, splits);
+  const size_t need = static_cast<size_t>(splits) * n_cols * (sum ? 2 : 1) * sizeof(float);
+  if (ws == nullptr || ws_bytes < need) return fail(SM_ERR_WORKSPACE, "statistics workspace too small");
+  float* part_sq = static_cast<float*>(ws);
+  float* part_s = sum ? part_sq + static_cast<size_t>(splits) * n_cols : nullptr;
+  dim3 grid(static_cast<unsigned>(cdiv(n_cols, 32 * vec)), splits);
+  if (vec_ok) {
+    if (sum) k_colstats_partial<T, kVec, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+    else k_colstats_partial<T, kVec, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+  } else {
+    if (sum) k_colstats_partial<T, 1, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+    else k_colstats_partial<T, 1, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+  }
+  SM_LAUNCHED();
+  const int fin_blocks = static_cast<int>(std::min<int64_t>(cdiv(n_cols, 256), 4 * sms));
+  k_colstats_finish<<<fin_blocks, 256, 0, st>>>(part_sq, part_s, splits, n_cols, sum_sq, sum);
+  SM_LAUNCHED();
+  return SM_OK;
+}
+
+// Layout: Group buffers, then MatDev table [batch], ones [max(rows, cols)].
+static int s8_layout(int32_t batch, int32_t rows, int32_t cols, void* ws, Group* g, MatDev** d_mats, float** ones,
+                     size_t* bytes) {
+  Carver cv(ws);
+  init_group_shape(*g, std::min(rows, cols), std::max(rows, cols), batch);
+  g->rank1 = false;
+  g->mat_off = 0;
+  *d_mats = cv.take<MatDev>(batch);
+  *ones = cv.take<float>(std::max(rows, cols));
+  carve_group(cv, *g);
+  *bytes = round_up(static_cast<int64_t>(cv.off), 256);
+  return SM_OK;
+}
+
+}  // namespace smb
+
+// =============================================================== C-ABI
+
+extern "C" {
+
+int sm_version(void) { return SM_ABI_VERSION; }
+
+const char* sm_last_error(void) { return t_last_error.c_str(); }
+
+int sm_init_device(void) {
+  DeviceInfo* di;
+  return current_device_info(&di);
+}
+
+int sm_device_status(int* status_out, void* stream) {
+  if (status_out == nullptr) return fail(SM_ERR_ARG, "null status_out");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0, zero = 0;
+  SM_CUDA(cudaMemcpyFromSymbolAsync(&v, g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+  SM_CUDA(cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
+  SM_CUDA(cudaStreamSynchronize(st));
+  *status_out = v;
+  return SM_OK;
+}
+
+// ------------------------------------------------------------ N1 stats
+
+size_t sm_stats_workspace_bytes(int64_t n_rows, int64_t n_cols) {
+  if (n_rows <= 0 || n_cols <= 0) return 0;
+  int sms = 148;
+  DeviceInfo* di;
+  if (current_device_info(&di) == SM_OK) sms = di->sms;
+  int splits = 0;
+  for (int vec : {1, 2, 4, 8}) splits = std::max(splits, stats_splits(n_rows, n_cols, vec, sms));
+  return static_cast<size_t>(splits) * n_cols * 2 * sizeof(float);
+}
+
+int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_cols, int64_t row_stride,
+                        int64_t col_stride, float* sum_sq, float* sum, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (n_rows < 0 || n_cols < 0) return fail(SM_ERR_ARG, "negative shape");
+  if (n_rows == 0 || n_cols == 0) return SM_OK;
+  if (rows == nullptr || sum_sq == nullptr) return fail(SM_ERR_ARG, "null input or output");
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SM_DTYPE_F32:
+      return stats_launch(static_cast<const float*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq, sum,
+                          workspace, workspace_bytes, st, di->sms);
+    case SM_DTYPE_BF16:
+      return stats_launch(static_cast<const __nv_bfloat16*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
+                          sum, workspace, workspace_bytes, st, di->sms);
+    case SM_DTYPE_F16:
+      return stats_launch(static_cast<const __half*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq, sum,
+                          workspace, workspace_bytes, st, di->sms);
+    case SM_DTYPE_F64:
+      return stats_launch(static_cast<const double*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq, sum,
+                          workspace, workspace_bytes, st, di->sms);
+    default:
+      return fail(SM_ERR_ARG, "unsupported dtype code " + std::to_string(dtype));
+  }
+}
+
+// ------------------------------------------------------------------ plan
+
+int sm_plan_workspace_bytes(const SmPlanSpec* spec, size_t* bytes_out) {
+  if (bytes_out == nullptr) return fail(SM_ERR_ARG, "null bytes_out");
+  return plan_layout(spec, nullptr, nullptr, bytes_out);
+}
+
+int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_bytes, void* stream,
+                   SmPlan** plan_out) {
+  if (plan_out == nullptr) return fail(SM_ERR_ARG, "null plan_out");
+  *plan_out = nullptr;
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(SM_ERR_ARG, "workspace must be a 256-byte aligned device pointer");
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  for (int i = 0; i < spec->n_matrices; ++i) {
+    const SmMatrixSpec& m = spec->matrices[i];
+    if (m.weight == nullptr || m.momentum == nullptr) return fail(SM_ERR_ARG, "null weight or momentum");
+  }
+  for (int s = 0; s < spec->n_stats; ++s) {
+    const SmStatSpec& st = spec->stats[s];
+    if (st.sum == nullptr || st.ema == nullptr) return fail(SM_ERR_ARG, "null statistic buffer");
+    if (st.kind == SM_STAT_A_RANK1 && (st.first_sum == nullptr || st.mean_ema == nullptr))
+      return fail(SM_ERR_ARG, "rank-one statistic without first-moment buffers");
+  }
+  size_t need = 0;
+  SM_TRY(plan_layout(spec, nullptr, nullptr, &need));
+  if (workspace_bytes < need) return fail(SM_ERR_WORKSPACE, "plan workspace too small");
+  SmPlan* p = new SmPlan();
+  int rc = plan_layout(spec, workspace, p, &need);
+  if (rc == SM_OK) {
+    SM_CUDA(cudaGetDevice(&p->device));
+    p->stat_beta = spec->statistic_beta;
+    p->stat_omb = static_cast<float>(1.0 - static_cast<double>(spec->statistic_beta));
+    p->mom_beta = spec->momentum;
+    p->mom_omb = static_cast<float>(1.0 - static_cast<double>(spec->momentum));
+    // Zero the whole workspace once: padding of every S8 plane must be zero.
+    cudaError_t e = cudaMemsetAsync(workspace, 0, need, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+    for (auto& g : p->groups) {
+      if (rc != SM_OK) break;
+      rc = encode_group_maps(g);
+    }
+    p->h_table.resize(p->table_bytes);
+  }
+  if (rc != SM_OK) {
+    delete p;
+    return rc;
+  }
+  *plan_out = p;
+  return SM_OK;
+}
+
+int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
+  if (p == nullptr || args == nullptr || args->grads == nullptr || args->lrs == nullptr || args->counts == nullptr ||
+      args->ema_init == nullptr)
+    return fail(SM_ERR_ARG, "null plan or step argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nm = static_cast<int>(p->mats.size());
+  const int ns = static_cast<int>(p->stats.size());
+  Timer* tm = p->timer.enabled ? &p->timer : nullptr;
+  int64_t launches = 0;
+
+  // ---- host table: per-matrix descriptors in group/slot order + statistics
+  MatDev* hm = reinterpret_cast<MatDev*>(p->h_table.data());
+  StatDev* hs = reinterpret_cast<StatDev*>(p->h_table.data() +
+                                          (reinterpret_cast<uint8_t*>(p->d_stats) - reinterpret_cast<uint8_t*>(p->d_mats)));
+  std::vector<uint8_t> vec4(p->groups.size(), 1);
+  for (int t = 0; t < nm; ++t) {
+    const int i = p->order[t];
+    const SmMatrixSpec& m = p->mats[i];
+    if (args->grads[i] == nullptr) return fail(SM_ERR_ARG, "null gradient for matrix " + std::to_string(i));
+    MatDev& d = hm[t];
+    memset(&d, 0, sizeof(d));
+    d.grad = args->grads[i];
+    d.mom = m.momentum;
+    d.weight = m.weight;
+    d.inv_a = p->s_inv[m.a_stat];
+    d.z_a = p->s_z[m.a_stat];
+    d.zeta_a = p->s_zeta[m.a_stat];
+    d.scal_a = p->s_scal[m.a_stat];
+    d.inv_b = p->s_inv[m.b_stat];
+    d.d_out = m.d_out;
+    d.d_in = m.d_in;
+    d.transposed = m.d_out > m.d_in ? 1 : 0;
+    d.slot = p->mat_slot[i];
+    d.lr = args->lrs[i];
+    d.sqrt_rows = static_cast<float>(std::sqrt(static_cast<double>(m.d_out)));
+    const bool aligned = (m.d_in % 4 == 0) && (reinterpret_cast<uintptr_t>(d.grad) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(d.mom) % 16 == 0);
+    if (!aligned) vec4[p->mat_group[i]] = 0;
+  }
+  for (int s = 0; s < ns; ++s) {
+    const SmStatSpec& sp = p->stats[s];
+    if (args->counts[s] < 1) return fail(SM_ERR_ARG, "statistic " + std::to_string(s) + " has no rows");
+    StatDev& d = hs[s];
+    memset(&d, 0, sizeof(d));
+    d.sum = sp.sum;
+    d.first_sum = sp.first_sum;
+    d.ema = sp.ema;
+    d.mean_ema = sp.mean_ema;
+    d.inv = p->s_inv[s];
+    d.z = p->s_z[s];
+    d.zeta = p->s_zeta[s];
+    d.scal = p->s_scal[s];
+    d.count = args->counts[s];
+    d.n = sp.n;
+    d.kind = sp.kind;
+    d.init = args->ema_init[s] ? 1 : 0;
+  }
+  // Pageable source: the runtime stages it before returning, so h_table may
+  // be rewritten by the next step immediately.
+  SM_CUDA(cudaMemcpyAsync(p->d_mats, p->h_table.data(), p->table_bytes, cudaMemcpyHostToDevice, st));
+
+  SM_TIMED(tm, SM_TCLASS_STATS, 0.0, st, ([&]() -> int {
+             if (ns > 0) {
+               k_stats_finish<<<ns, 256, 0, st>>>(p->d_stats, p->stat_beta, p->stat_omb);
+               SM_LAUNCHED();
+             }
+             return SM_OK;
+           }()));
+  ++launches;
+  for (size_t gi = 0; gi < p->groups.size(); ++gi) {
+    const Group& g = p->groups[gi];
+    SM_TRY(run_front(g, p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
+    SM_TRY(run_s8(g, st, tm, &launches));
+    SM_TRY(run_back(g, p->d_mats, p->group_has_trans[gi] != 0, p->group_has_plain[gi] != 0, st, tm, &launches));
+  }
+  p->launches_last = launches;
+  return SM_OK;
+}
+
+int sm_plan_set_timing(SmPlan* p, int enabled) {
+  if (p == nullptr) return fail(SM_ERR_ARG, "null plan");
+  p->timer.enabled = enabled != 0;
+  return SM_OK;
+}
+
+int sm_plan_timing_read(SmPlan* p, double* ms_out, int64_t* launches_out, double* gemm_flops_out) {
+  if (p == nullptr || ms_out == nullptr || launches_out == nullptr) return fail(SM_ERR_ARG, "null argument");
+  for (int c = 0; c < SM_TCLASS_COUNT; ++c) {
+    ms_out[c] = 0.0;
+    launches_out[c] = 0;
+  }
+  double flops = 0.0;
+  if (!p->timer.recs.empty()) SM_CUDA(cudaEventSynchronize(p->timer.recs.back().b));
+  for (const auto& r : p->timer.recs) {
+    float ms = 0.f;
+    SM_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+    ms_out[r.cls] += ms;
+    launches_out[r.cls] += 1;
+    flops += r.flops;
+  }
+  if (gemm_flops_out != nullptr) *gemm_flops_out = flops;
+  p->timer.recs.clear();
+  p->timer.next = 0;
+  return SM_OK;
+}
+
+int sm_plan_launches_per_step(const SmPlan* p, int64_t* out) {
+  if (p == nullptr || out == nullptr) return fail(SM_ERR_ARG, "null argument");
+  *out = p->launches_last;
+  return SM_OK;
+}
+
+int sm_plan_destroy(SmPlan* p) {
+  if (p == nullptr) return SM_OK;
+  for (cudaEvent_t e : p->timer.pool) cudaEventDestroy(e);
+  delete p;
+  return SM_OK;
+}
+
+// -------------------------------------------------------------- S8 batch
+
+size_t sm_s8_workspace_bytes(int32_t batch, int32_t rows, int32_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  Group g;
+  MatDev* dm;
+  float* ones;
+  size_t bytes = 0;
+  s8_layout(batch, rows, cols, nullptr, &g, &dm, &ones, &bytes);
+  return bytes;
+}
+
+int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t cols, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 0) return fail(SM_ERR_ARG, "negative shape");
+  if (batch == 0 || rows == 0 || cols == 0) return SM_OK;
+  if (x == nullptr || out == nullptr) return fail(SM_ERR_ARG, "null input or output");
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(SM_ERR_ARG, "workspace must be a 256-byte aligned device pointer");
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Group g;
+  MatDev* d_mats;
+  float* ones;
+  size_t need = 0;
+  s8_layout(batch, rows, cols, nullptr, &g, &d_mats, &ones, &need);
+  if (workspace_bytes < need) return fail(SM_ERR_WORKSPACE, "S8 workspace too small");
+  s8_layout(batch, rows, cols, workspace, &g, &d_mats, &ones, &need);
+  SM_TRY(encode_group_maps(g));
+  SM_CUDA(cudaMemsetAsync(workspace, 0, need, st));
+  const int64_t nmax = std::max(rows, cols);
+  k_fill<<<static_cast<unsigned>(cdiv(nmax, 256)), 256, 0, st>>>(ones, nmax, 1.0f);
+  SM_LAUNCHED();
+  k_fill<<<1, 256, 0, st>>>(g.gamma, batch, 1.0f);
+  SM_LAUNCHED();
+  std::vector<MatDev> hm(batch);
+  const int64_t per = static_cast<int64_t>(rows) * cols;
+  bool vec4 = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  for (int b = 0; b < batch; ++b) {
+    MatDev& d = hm[b];
+    memset(&d, 0, sizeof(d));
+    d.grad = x + b * per;
+    d.mom = nullptr;  // S8 input is used as is (no momentum)
+    d.weight = out + b * per;
+    d.inv_a = ones;
+    d.inv_b = ones;
+    d.d_out = rows;
+    d.d_in = cols;
+    d.transposed = rows > cols ? 1 : 0;
+    d.slot = b;
+    d.lr = -1.0f;  // out = 0 - (-1) * 1 * Q
+    d.sqrt_rows = 1.0f;
+  }
+  SM_CUDA(cudaMemcpyAsync(d_mats, hm.data(), sizeof(MatDev) * batch, cudaMemcpyHostToDevice, st));
+  int64_t launches = 0;
+  SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, st, nullptr, &launches));
+  SM_TRY(run_s8(g, st, nullptr, &launches));
+  SM_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * per, st));
+  {
+    dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), batch);
+    k_mapback_apply<false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
+    SM_LAUNCHED();
+  }
+  return SM_OK;
+}
+
+// ------------------------------------------------------------------ AdamW
+
+int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float beta1, float beta2, float eps,
+                   float decay_factor, void* stream) {
+  if (count < 0 || (count > 0 && tensors == nullptr)) return fail(SM_ERR_ARG, "bad tensor list");
+  if (count == 0) return SM_OK;
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float omb1 = static_cast<float>(1.0 - static_cast<double>(beta1));
+  const float omb2 = static_cast<float>(1.0 - static_cast<double>(beta2));
+  for (int start = 0; start < count; start += kAdamMaxTensors) {
+    AdamBatch b;
+    memset(&b, 0, sizeof(b));
+    b.count = std::min(kAdamMaxTensors, count - start);
+    b.chunk_start[0] = 0;
+    for (int t = 0; t < b.count; ++t) {
+      const SmAdamTensor& s = tensors[start + t];
+      if (s.numel < 0 || (s.numel > 0 && (s.param == nullptr || s.grad == nullptr || s.exp_avg == nullptr ||
+                                          s.exp_avg_sq == nullptr)))
+        return fail(SM_ERR_ARG, "bad AdamW tensor " + std::to_string(start + t));
+      b.param[t] = s.param;
+      b.grad[t] = s.grad;
+      b.m1[t] = s.exp_avg;
+      b.m2[t] = s.exp_avg_sq;
+      b.numel[t] = s.numel;
+      b.bc1[t] = s.bias_correction1;
+      b.bc2[t] = s.bias_correction2;
+      b.chunk_start[t + 1] = b.chunk_start[t] + cdiv(s.numel, kAdamChunk);
+    }
+    const int64_t chunks = b.chunk_start[b.count];
+    if (chunks == 0) continue;
+    const int grid = static_cast<int>(std::min<int64_t>(chunks, 8 * di->sms));
+    k_adamw_multi<<<grid, 256, 0, st>>>(b, lr, beta1, omb1, beta2, omb2, eps, decay_factor);
+    SM_LAUNCHED();
+  }
+  return SM_OK;
+}
+
+// ------------------------------------------------------------------- GEMM
+
+int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int b_kmajor, int32_t batch,
+                 int32_t m, int32_t n, int32_t k, int epilogue, void* out0, void* out1, const float* alpha,
+                 const void* aux, const void* aux_lo, float pa, float pb, float pc, float* partials,
+                 void* stream) {
+  if (batch <= 0 || m <= 0 || n <= 0 || k <= 0) return fail(SM_ERR_ARG, "empty GEMM");
+  if (m % 128 != 0 || n % 128 != 0 || k % 64 != 0) return fail(SM_ERR_ARG, "GEMM needs M%128, N%128, K%64 == 0");
+  if (a_hi == nullptr || b_hi == nullptr || out0 == nullptr) return fail(SM_ERR_ARG, "null operand");
+  const bool comp = a_lo != nullptr;
+  if (comp && b_lo == nullptr) return fail(SM_ERR_ARG, "compensated mode needs both lo planes");
+  if (epilogue == SM_EPI_HILO && out1 == nullptr) return fail(SM_ERR_ARG, "hi/lo epilogue needs out1");
+  if (epilogue == SM_EPI_POLY && aux == nullptr) return fail(SM_ERR_ARG, "poly epilogue needs aux");
+  if (epilogue == SM_EPI_POLY_HILO && (aux == nullptr || aux_lo == nullptr || out1 == nullptr))
+    return fail(SM_ERR_ARG, "hi/lo poly epilogue needs aux, aux_lo and out1");
+  if (epilogue == SM_EPI_HILO && out1 == nullptr) return fail(SM_ERR_ARG, "hi/lo epilogue needs out1");
+  if (epilogue == SM_EPI_F32_NORM && partials == nullptr) return fail(SM_ERR_ARG, "norm epilogue needs partials");
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  const int bn = pick_bn(n);
+  CUtensorMap ah, al, bh, bl;
+  SM_TRY(make_map(&ah, a_hi, k, m, batch, kGemmBM));
+  al = ah;
+  if (comp) SM_TRY(make_map(&al, a_lo, k, m, batch, kGemmBM));
+  if (b_kmajor) {
+    SM_TRY(make_map(&bh, b_hi, k, n, batch, bn));
+    bl = bh;
+    if (comp) SM_TRY(make_map(&bl, b_lo, k, n, batch, bn));
+  } else {
+    SM_TRY(make_map(&bh, b_hi, n, k, batch, 64));
+    bl = bh;
+    if (comp) SM_TRY(make_map(&bl, b_lo, n, k, batch, 64));
+  }
+  GemmArgs a = gemm_args(m, n, k, batch, bn);
+  a.out0 = out0;
+  a.out1 = out1;
+  a.alpha = alpha;
+  a.aux = static_cast<const __nv_bfloat16*>(aux);
+  a.aux_lo = static_cast<const __nv_bfloat16*>(aux_lo);
+  a.pa = pa;
+  a.pb = pb;
+  a.pc = pc;
+  a.partials = partials;
+  return dispatch_gemm(bn, comp, !b_kmajor, epilogue, ah, al, bh, bl, a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

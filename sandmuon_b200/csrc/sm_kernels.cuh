@@ -1,0 +1,734 @@
+// sm_kernels.cuh -- HBM-bound kernels of the SandMuon step on sm_100a.
+//
+//   N1  k_colstats_partial / k_colstats_finish : hook column statistics
+//   N2  k_stats_finish                         : EMA + inverse square roots
+//   N3  k_whiten_rowstats / k_whiten_write     : Nesterov momentum, two-sided
+//                                                whitening, stage-1 hi/lo split
+//   N5  k_poly_stage1                          : first S8 polynomial (hi/lo)
+//   N7  k_mapback_rowstats_* / k_mapback_apply : mapback, graft, weight update
+//   N8  k_adamw_multi                          : auxiliary AdamW
+//   --  k_reduce_*                             : per-matrix scalar reductions
+//
+// All reductions use a fixed order (no float atomics) so results are
+// bit-reproducible run to run.
+#pragma once
+
+#include "sm_common.cuh"
+
+namespace smb {
+
+// ============================================================ N1: statistics
+// sum_sq[c] += sum_r x[r,c]^2 ; sum[c] += sum_r x[r,c]
+// (sandmuon/optimizer.py:156-168 forward hook, :170-178 cotangent hook).
+// Pass 1: grid (column blocks of 32*VEC, row splits), 8 warps per CTA, warp w
+// walks rows r = begin + w, begin + w + 8, ...; lane l owns VEC consecutive
+// columns loaded as one 16-byte vector.  Partials [split][col] go to the
+// workspace; pass 2 sums them in split order (FP64) into the accumulators.
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<double>(double v) { return static_cast<float>(v); }
+
+template <typename T, int VEC>
+__device__ __forceinline__ void load_vec(const T* p, int64_t cs, float (&out)[VEC]) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) out[i] = to_f32<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) out[i] = to_f32<T>(p[i * cs]);
+  }
+}
+
+template <typename T, int VEC, bool FIRST>
+__global__ void __launch_bounds__(256)
+    k_colstats_partial(const T* __restrict__ x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs,
+                       int64_t rows_per_split, float* __restrict__ part_sq, float* __restrict__ part_sum) {
+  __shared__ float sh_sq[8][32 * VEC];
+  __shared__ float sh_s[FIRST ? 8 : 1][FIRST ? 32 * VEC : 1];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * 32 * VEC + lane * VEC;
+  const int64_t r_begin = static_cast<int64_t>(blockIdx.y) * rows_per_split;
+  const int64_t r_end = min(r_begin + rows_per_split, n_rows);
+  float acc_sq[VEC], acc_s[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc_sq[i] = acc_s[i] = 0.0f;
+  // Vector path requires n_cols % VEC == 0 (host-checked), so a lane's VEC
+  // columns are either all in range or all out.
+  if (col0 < n_cols) {
+    const T* base = x + col0 * cs;
+    int64_t r = r_begin + warp;
+    for (; r + 24 < r_end; r += 32) {
+      float v0[VEC], v1[VEC], v2[VEC], v3[VEC];
+      load_vec<T, VEC>(base + r * rs, cs, v0);
+      load_vec<T, VEC>(base + (r + 8) * rs, cs, v1);
+      load_vec<T, VEC>(base + (r + 16) * rs, cs, v2);
+      load_vec<T, VEC>(base + (r + 24) * rs, cs, v3);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        acc_sq[i] += v0[i] * v0[i];
+        acc_sq[i] += v1[i] * v1[i];
+        acc_sq[i] += v2[i] * v2[i];
+        acc_sq[i] += v3[i] * v3[i];
+        if (FIRST) acc_s[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
+      }
+    }
+    for (; r < r_end; r += 8) {
+      float v[VEC];
+      load_vec<T, VEC>(base + r * rs, cs, v);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        acc_sq[i] += v[i] * v[i];
+        if (FIRST) acc_s[i] += v[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    sh_sq[warp][lane * VEC + i] = acc_sq[i];
+    if (FIRST) sh_s[warp][lane * VEC + i] = acc_s[i];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < 32 * VEC; c += blockDim.x) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * 32 * VEC + c;
+    if (col >= n_cols) continue;
+    float s2 = 0.0f, s1 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      s2 += sh_sq[w][c];
+      if (FIRST) s1 += sh_s[w][c];
+    }
+    part_sq[static_cast<int64_t>(blockIdx.y) * n_cols + col] = s2;
+    if (FIRST) part_sum[static_cast<int64_t>(blockIdx.y) * n_cols + col] = s1;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    k_colstats_finish(const float* __restrict__ part_sq, const float* __restrict__ part_sum, int splits,
+                      int64_t n_cols, float* __restrict__ sum_sq, float* __restrict__ sum) {
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < n_cols;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    double s2 = 0.0, s1 = 0.0;
+    for (int p = 0; p < splits; ++p) {
+      s2 += part_sq[p * n_cols + c];
+      if (sum != nullptr) s1 += part_sum[p * n_cols + c];
+    }
+    sum_sq[c] += static_cast<float>(s2);
+    if (sum != nullptr) sum[c] += static_cast<float>(s1);
+  }
+}
+
+// ====================================================== N2: statistics finish
+// One CTA per statistic vector; kind-specific arithmetic of
+//   _finish_a + diagonal_inverse_sqrt / rank1_inverse_sqrt
+//   (sandmuon/optimizer.py:182-207, :19-35) and
+//   _finish_b (sandmuon/optimizer.py:209-222).
+
+struct StatDev {
+  float* sum;
+  float* first_sum;
+  float* ema;
+  float* mean_ema;
+  float* inv;     // out [n]
+  float* z;       // out [n] (rank-one)
+  float* zeta;    // out [n] = inv * z (rank-one)
+  float* scal;    // out [4]: {coefficient, sum(zeta^2), sum(z^2), 0}
+  int64_t count;
+  int32_t n;
+  int32_t kind;
+  int32_t init;
+  int32_t pad;
+};
+
+template <int NT>
+__device__ __forceinline__ double block_sum_d(double v, double* sh) {
+  v = warp_sum_d(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) t += sh[w];
+  return t;
+}
+
+constexpr float kFltTiny = 1.17549435e-38f;  // torch.finfo(torch.float32).tiny
+
+__global__ void __launch_bounds__(256) k_stats_finish(const StatDev* __restrict__ stats, float beta, float omb) {
+  __shared__ double sh[8];
+  const StatDev d = stats[blockIdx.x];
+  const int n = d.n;
+  const float count = static_cast<float>(d.count);
+
+  if (d.kind == SM_STAT_B) {
+    // b = sum / count ; b /= max(mean(b), tiny)
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) acc += static_cast<double>(d.sum[i] / count);
+    const float mean_b = static_cast<float>(block_sum_d<256>(acc, sh) / n);
+    const float denom = fmaxf(mean_b, kFltTiny);
+    double acc_e = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float b = (d.sum[i] / count) / denom;
+      const float e = d.init ? b : d.ema[i] * beta + omb * b;
+      d.ema[i] = e;
+      d.sum[i] = 0.0f;
+      acc_e += e;
+    }
+    const float mean_e = static_cast<float>(block_sum_d<256>(acc_e, sh) / n);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float e = d.ema[i];
+      const float nrm = fmaxf(e, mean_e * 1e-6f) / fmaxf(mean_e, kFltTiny);
+      d.inv[i] = 1.0f / sqrtf(fmaxf(nrm, 1e-6f));
+    }
+    return;
+  }
+
+  // A statistics: second = a_sum / count (and mean = a_first_sum / count)
+  const bool rank1 = d.kind == SM_STAT_A_RANK1;
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float second = d.sum[i] / count;
+    const float e = d.init ? second : d.ema[i] * beta + omb * second;
+    d.ema[i] = e;
+    d.sum[i] = 0.0f;
+    if (rank1) {
+      const float mean = d.first_sum[i] / count;
+      d.mean_ema[i] = d.init ? mean : d.mean_ema[i] * beta + omb * mean;
+      d.first_sum[i] = 0.0f;
+    }
+    acc += e;
+  }
+  const float mean_e = static_cast<float>(block_sum_d<256>(acc, sh) / n);
+  if (!rank1) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float nrm = fmaxf(d.ema[i], mean_e * 1e-6f) / fmaxf(mean_e, kFltTiny);
+      d.inv[i] = 1.0f / sqrtf(fmaxf(nrm, 1e-6f));
+    }
+    if (threadIdx.x == 0) {
+      d.scal[0] = 0.0f;
+      d.scal[1] = 0.0f;
+      d.scal[2] = 0.0f;
+      d.scal[3] = 0.0f;
+    }
+    return;
+  }
+  // rank1_inverse_sqrt (sandmuon/optimizer.py:27-35)
+  const float scale = fmaxf(mean_e, kFltTiny);
+  const float root_scale = sqrtf(scale);
+  double acc_z = 0.0, acc_zeta = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float mu = d.mean_ema[i];
+    const float var = fmaxf(d.ema[i] - mu * mu, 0.0f);
+    const float inv = 1.0f / sqrtf(fmaxf(var / scale, 1e-6f));
+    const float z = inv * (mu / root_scale);
+    d.inv[i] = inv;
+    d.z[i] = z;
+    d.zeta[i] = inv * z;
+    acc_z += static_cast<double>(z) * z;
+    acc_zeta += static_cast<double>(inv * z) * (inv * z);
+  }
+  const double kz = block_sum_d<256>(acc_z, sh);
+  const double kzeta = block_sum_d<256>(acc_zeta, sh);
+  if (threadIdx.x == 0) {
+    const float root = sqrtf(1.0f + static_cast<float>(kz));
+    d.scal[0] = -1.0f / (root * (root + 1.0f));
+    d.scal[1] = static_cast<float>(kzeta);
+    d.scal[2] = static_cast<float>(kz);
+    d.scal[3] = 0.0f;
+  }
+}
+
+// ===================================================== per-matrix descriptor
+
+struct MatDev {
+  const float* grad;    // [d_out, d_in]
+  float* mom;           // [d_out, d_in]
+  float* weight;        // [d_out, d_in]
+  const float* inv_a;   // [d_in]
+  const float* z_a;     // [d_in] or null (diagonal A)
+  const float* zeta_a;  // [d_in] inv_a * z_a or null
+  const float* scal_a;  // {coefficient, sum(zeta^2), ...}
+  const float* inv_b;   // [d_out]
+  int32_t d_out, d_in;
+  int32_t transposed;   // d_out > d_in: oriented matrix is the transpose
+  int32_t slot;
+  float lr;
+  float sqrt_rows;      // sqrt(d_out): the graft norm
+  int32_t pad0, pad1;
+};
+
+// ========================================== N3 pass 1: whitening row stats
+// Per param row o (contiguous, d_in long):
+//   m' = .8 m + .2 g ; s = .8 m' + .2 g          (sandmuon/optimizer.py:246-248)
+//   y  = inv_b[o] * s * inv_a                    (whitening diagonals)
+//   rs[o] = { y . z_a , |y|^2 }
+// The rank-one whitening correction V = Y + c (Y z) z^T acts along d_in in
+// both orientations, so its dot products are row dots of the param layout.
+template <int VEC, bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_whiten_rowstats(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs,
+                      int ld_rs) {
+  const MatDev md = mats[blockIdx.y];
+  const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (o >= md.d_out) return;
+  const float* g = md.grad + static_cast<int64_t>(o) * md.d_in;
+  // A null momentum means "use the input as is" (the batch S8 entry point).
+  const bool has_mom = md.mom != nullptr;
+  const float* m = has_mom ? md.mom + static_cast<int64_t>(o) * md.d_in : g;
+  const float ib = md.inv_b[o];
+  float dot = 0.0f, sq = 0.0f;
+  for (int i = lane * VEC; i < md.d_in; i += 32 * VEC) {
+    float gv[VEC], mv[VEC], av[VEC], zv[VEC];
+    if constexpr (VEC == 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(g + i);
+      const float4 m4 = *reinterpret_cast<const float4*>(m + i);
+      const float4 a4 = *reinterpret_cast<const float4*>(md.inv_a + i);
+      gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+      mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+      av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
+      if (RANK1) {
+        const float4 z4 = *reinterpret_cast<const float4*>(md.z_a + i);
+        zv[0] = z4.x; zv[1] = z4.y; zv[2] = z4.z; zv[3] = z4.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        gv[e] = g[i + e];
+        mv[e] = m[i + e];
+        av[e] = md.inv_a[i + e];
+        if (RANK1) zv[e] = md.z_a[i + e];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float mn = mom_beta * mv[e] + omb * gv[e];
+      const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
+      const float y = (src * ib) * av[e];
+      sq += y * y;
+      if (RANK1) dot += y * zv[e];
+    }
+  }
+  sq = warp_sum(sq);
+  if (RANK1) dot = warp_sum(dot);
+  if (lane == 0) rs[static_cast<int64_t>(blockIdx.y) * ld_rs + o] = make_float2(dot, sq);
+}
+
+// inv_norm[b] = 1 / max(|Y_b|_F, 1e-30).  The S8 map is invariant to the
+// scale of its input (stage 1 divides by s = 1.35 |G^2|_F^(1/4)), so any
+// norm that keeps X in range reproduces x / |x|_F (sandmuon/optimizer.py:77-78);
+// |Y|_F bounds |V|_F within the factor rho = sqrt(1 + |z|^2) of the rank-one
+// whitener and never cancels.
+__global__ void __launch_bounds__(256)
+    k_reduce_invnorm(const MatDev* __restrict__ mats, const float2* __restrict__ rs, int ld_rs,
+                     float* __restrict__ inv_norm) {
+  __shared__ double sh[8];
+  const MatDev md = mats[blockIdx.x];
+  double acc = 0.0;
+  for (int o = threadIdx.x; o < md.d_out; o += blockDim.x) acc += rs[static_cast<int64_t>(blockIdx.x) * ld_rs + o].y;
+  const double t = block_sum_d<256>(acc, sh);
+  if (threadIdx.x == 0) inv_norm[blockIdx.x] = 1.0f / fmaxf(static_cast<float>(sqrt(t)), 1e-30f);
+}
+
+// ========================================== N3 pass 2: whiten + split write
+// Tile of 32 param rows x 64 param columns per CTA (256 threads).
+//   m' written back ; v = y + c * dot[o] * z[i] ; x = v * inv_norm
+//   X_hi/X_lo at the oriented position: (o, i), or (i, o) when transposed
+//   (staged through shared memory so both reads and writes are coalesced).
+template <bool RANK1, bool VEC4>
+__global__ void __launch_bounds__(256)
+    k_whiten_write(const MatDev* __restrict__ mats, float mom_beta, float omb, const float2* __restrict__ rs, int ld_rs,
+                   const float* __restrict__ inv_norm, __nv_bfloat16* __restrict__ xh,
+                   __nv_bfloat16* __restrict__ xl, int64_t rp, int64_t cp) {
+  __shared__ uint32_t sh_hi[64][17];  // [i][o/2] packed bf16 pairs, transposed staging
+  __shared__ uint32_t sh_lo[64][17];
+  const int b = blockIdx.z;
+  const MatDev md = mats[b];
+  const int o0 = blockIdx.y * 32;
+  const int i0 = blockIdx.x * 64;
+  if (o0 >= md.d_out || i0 >= md.d_in) return;
+  const float scale = inv_norm[b];
+  const float coef = RANK1 ? md.scal_a[0] : 0.0f;
+  const bool has_mom = md.mom != nullptr;
+  const int tx = threadIdx.x & 15;   // 4 consecutive columns
+  const int ty = threadIdx.x >> 4;   // rows ty and ty + 16
+  const int64_t plane = static_cast<int64_t>(b) * rp * cp;
+  const bool trans = md.transposed != 0;
+
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int ol = ty + 16 * half;
+    const int o = o0 + ol;
+    const int ib = i0 + tx * 4;
+    float xv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (o < md.d_out) {
+      const float invb = md.inv_b[o];
+      const float cw = RANK1 ? coef * rs[static_cast<int64_t>(b) * ld_rs + o].x : 0.0f;
+      const int64_t row = static_cast<int64_t>(o) * md.d_in;
+      if (VEC4 && ib + 3 < md.d_in) {
+        const float4 g4 = *reinterpret_cast<const float4*>(md.grad + row + ib);
+        const float4 m4 = has_mom ? *reinterpret_cast<const float4*>(md.mom + row + ib) : g4;
+        const float4 a4 = *reinterpret_cast<const float4*>(md.inv_a + ib);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+        const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+        float zv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (RANK1) {
+          const float4 z4 = *reinterpret_cast<const float4*>(md.z_a + ib);
+          zv[0] = z4.x; zv[1] = z4.y; zv[2] = z4.z; zv[3] = z4.w;
+        }
+        float mn[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          mn[e] = mom_beta * mv[e] + omb * gv[e];
+          const float src = has_mom ? mom_beta * mn[e] + omb * gv[e] : gv[e];
+          float v = (src * invb) * av[e];
+          if (RANK1) v += cw * zv[e];
+          xv[e] = v * scale;
+        }
+        if (has_mom) *reinterpret_cast<float4*>(md.mom + row + ib) = make_float4(mn[0], mn[1], mn[2], mn[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = ib + e;
+          if (i < md.d_in) {
+            const float gv = md.grad[row + i];
+            float src = gv;
+            if (has_mom) {
+              const float mn = mom_beta * md.mom[row + i] + omb * gv;
+              md.mom[row + i] = mn;
+              src = mom_beta * mn + omb * gv;
+            }
+            float v = (src * invb) * md.inv_a[i];
+            if (RANK1) v += cw * md.z_a[i];
+            xv[e] = v * scale;
+          }
+        }
+      }
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) split_hilo(xv[e], h[e], l[e]);
+    if (!trans) {
+      if (o < md.d_out) {
+        __nv_bfloat16* dh = xh + plane + static_cast<int64_t>(o) * cp;
+        __nv_bfloat16* dl = xl + plane + static_cast<int64_t>(o) * cp;
+        if (ib + 3 < md.d_in) {
+          *reinterpret_cast<uint2*>(dh + ib) = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+          *reinterpret_cast<uint2*>(dl + ib) = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+        } else {
+          for (int e = 0; e < 4; ++e) {
+            if (ib + e < md.d_in) {
+              dh[ib + e] = __float2bfloat16_rn(h[e]);
+              dl[ib + e] = __float2bfloat16_rn(l[e]);
+            }
+          }
+        }
+      }
+    } else {
+      // stage (i, o) pairs: element (il, ol) -> packed word [il][ol/2], half ol&1
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int il = tx * 4 + e;
+        __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(&sh_hi[il][ol >> 1]) + (ol & 1);
+        __nv_bfloat16* pl = reinterpret_cast<__nv_bfloat16*>(&sh_lo[il][ol >> 1]) + (ol & 1);
+        *ph = __float2bfloat16_rn(h[e]);
+        *pl = __float2bfloat16_rn(l[e]);
+      }
+    }
+  }
+  if (trans) {
+    __syncthreads();
+    // oriented X row = i (d_in index), columns = o; 64 rows x 32 bf16 each.
+    const int il = threadIdx.x >> 2;       // 0..63
+    const int oc = (threadIdx.x & 3) * 8;  // 0, 8, 16, 24
+    const int i = i0 + il;
+    if (i < md.d_in) {
+      __nv_bfloat16* dh = xh + plane + static_cast<int64_t>(i) * cp + o0 + oc;
+      __nv_bfloat16* dl = xl + plane + static_cast<int64_t>(i) * cp + o0 + oc;
+      if (o0 + oc + 7 < md.d_out) {
+        uint4 vh, vl;
+        vh.x = sh_hi[il][oc / 2 + 0]; vh.y = sh_hi[il][oc / 2 + 1];
+        vh.z = sh_hi[il][oc / 2 + 2]; vh.w = sh_hi[il][oc / 2 + 3];
+        vl.x = sh_lo[il][oc / 2 + 0]; vl.y = sh_lo[il][oc / 2 + 1];
+        vl.z = sh_lo[il][oc / 2 + 2]; vl.w = sh_lo[il][oc / 2 + 3];
+        *reinterpret_cast<uint4*>(dh) = vh;
+        *reinterpret_cast<uint4*>(dl) = vl;
+      } else {
+        for (int e = 0; e < 8; ++e) {
+          if (o0 + oc + e < md.d_out) {
+            dh[e] = reinterpret_cast<const __nv_bfloat16*>(&sh_hi[il][0])[oc + e];
+            dl[e] = reinterpret_cast<const __nv_bfloat16*>(&sh_lo[il][0])[oc + e];
+          }
+        }
+      }
+    }
+  }
+}
+
+// ================================================ S8 stage-1 scale and poly
+// s[b] = max(1.35 * |G2_b|_F^(1/4), 1e-30) from the per-tile partial sums of
+// squares written by the G*G epilogue (sandmuon/optimizer.py:81).
+__global__ void __launch_bounds__(256)
+    k_reduce_s8scale(const float* __restrict__ partials, int per_mat, float margin, float* __restrict__ s,
+                     float* __restrict__ s_inv) {
+  __shared__ double sh[8];
+  double acc = 0.0;
+  for (int p = threadIdx.x; p < per_mat; p += blockDim.x)
+    acc += partials[static_cast<int64_t>(blockIdx.x) * per_mat + p];
+  const double t = block_sum_d<256>(acc, sh);
+  if (threadIdx.x == 0) {
+    const float nrm = static_cast<float>(sqrt(t));
+    const float sv = fmaxf(margin * powf(nrm, 0.25f), 1e-30f);
+    s[blockIdx.x] = sv;
+    s_inv[blockIdx.x] = 1.0f / sv;
+  }
+}
+
+// P = a I + b G / s / s + c G2 / s / s / s / s (sandmuon/optimizer.py:83-84),
+// emitted as hi/lo BF16 planes in place of the G hi/lo planes.  Sequential
+// divisions keep a zero matrix (s = 1e-30) at exactly P = a I.
+__global__ void __launch_bounds__(256)
+    k_poly_stage1(__nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ gl, const float* __restrict__ g2,
+                  const float* __restrict__ s, int64_t rp, float pa, float pb, float pc) {
+  const int b = blockIdx.y;
+  const int64_t per = rp * rp;
+  const float sv = s[b];
+  const int64_t base = static_cast<int64_t>(b) * per;
+  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 2; e < per;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x * 2) {
+    const uint32_t wh = *reinterpret_cast<const uint32_t*>(gh + base + e);
+    const uint32_t wl = *reinterpret_cast<const uint32_t*>(gl + base + e);
+    const float2 w2 = *reinterpret_cast<const float2*>(g2 + base + e);
+    const float gv[2] = {bf16_lo_to_f(wh) + bf16_lo_to_f(wl), bf16_hi_to_f(wh) + bf16_hi_to_f(wl)};
+    const float g2v[2] = {w2.x, w2.y};
+    float hi[2], lo[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t idx = e + q;
+      const int64_t r = idx / rp, c = idx - r * rp;
+      const float t1 = (gv[q] / sv) / sv;
+      const float t2 = (((g2v[q] / sv) / sv) / sv) / sv;
+      const float p = (r == c ? pa : 0.0f) + pb * t1 + pc * t2;
+      split_hilo(p, hi[q], lo[q]);
+    }
+    *reinterpret_cast<uint32_t*>(gh + base + e) = pack_bf16x2(hi[0], hi[1]);
+    *reinterpret_cast<uint32_t*>(gl + base + e) = pack_bf16x2(lo[0], lo[1]);
+  }
+}
+
+// ============================================ N7 pass 1: mapback row stats
+// Mapback U = diag(inv_b) (Q + c (Q z) z^T) diag(inv_a) in param coordinates
+// (rank1_mapback, sandmuon/optimizer.py:48-60, both orientations).  Per param
+// row o:  t = sum_i z_i Q_oi, S1 = sum_i a_i^2 Q_oi^2, S2 = sum_i a_i^2 z_i Q_oi
+//   |U_o|^2 = inv_b_o^2 (S1 + 2 c t S2 + c^2 t^2 sum_i a_i^2 z_i^2)
+// out[o] = {t, |U_o|^2}.
+// Non-transposed: Q is [d_out, cp] (rows contiguous): one warp per row.
+template <bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_mapback_rowstats_rows(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+                            float2* __restrict__ out, int ld_out) {
+  const int b = blockIdx.y;
+  const MatDev md = mats[b];
+  if (md.transposed) return;
+  const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (o >= md.d_out) return;
+  const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * cp;
+  float t = 0.f, s1 = 0.f, s2 = 0.f;
+  for (int i = lane; i < md.d_in; i += 32) {
+    const float v = qr[i];
+    const float a = md.inv_a[i];
+    const float a2 = a * a;
+    s1 += a2 * v * v;
+    if (RANK1) {
+      const float z = md.z_a[i];
+      t += z * v;
+      s2 += a2 * z * v;
+    }
+  }
+  s1 = warp_sum(s1);
+  if (RANK1) {
+    t = warp_sum(t);
+    s2 = warp_sum(s2);
+  }
+  if (lane == 0) {
+    const double ib = md.inv_b[o];
+    double row = s1;
+    if (RANK1) {
+      const double c = md.scal_a[0], k2 = md.scal_a[1];
+      row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
+    }
+    out[static_cast<int64_t>(b) * ld_out + o] = make_float2(t, static_cast<float>(ib * ib * row));
+  }
+}
+
+// Transposed: Q is [d_in, cp] with param row o = oriented column o; one
+// thread per column walks the d_in rows (coalesced across threads).
+template <bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_mapback_rowstats_cols(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+                            float2* __restrict__ out, int ld_out) {
+  const int b = blockIdx.y;
+  const MatDev md = mats[b];
+  if (!md.transposed) return;
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= md.d_out) return;
+  const float* qc = q + static_cast<int64_t>(b) * rp * cp + o;
+  float t = 0.f, s1 = 0.f, s2 = 0.f;
+  int i = 0;
+  for (; i + 3 < md.d_in; i += 4) {
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = qc[static_cast<int64_t>(i + e) * cp];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = md.inv_a[i + e];
+      const float a2 = a * a;
+      s1 += a2 * v[e] * v[e];
+      if (RANK1) {
+        const float z = md.z_a[i + e];
+        t += z * v[e];
+        s2 += a2 * z * v[e];
+      }
+    }
+  }
+  for (; i < md.d_in; ++i) {
+    const float v = qc[static_cast<int64_t>(i) * cp];
+    const float a = md.inv_a[i];
+    const float a2 = a * a;
+    s1 += a2 * v * v;
+    if (RANK1) {
+      const float z = md.z_a[i];
+      t += z * v;
+      s2 += a2 * z * v;
+    }
+  }
+  const double ib = md.inv_b[o];
+  double row = s1;
+  if (RANK1) {
+    const double c = md.scal_a[0], k2 = md.scal_a[1];
+    row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
+  }
+  out[static_cast<int64_t>(b) * ld_out + o] = make_float2(t, static_cast<float>(ib * ib * row));
+}
+
+// gamma[b] = sqrt(d_out) / max(|U_b|_F, tiny)  (_graft_direction,
+// sandmuon/optimizer.py:63-66)
+__global__ void __launch_bounds__(256)
+    k_reduce_graft(const MatDev* __restrict__ mats, const float2* __restrict__ rs, int ld_rs,
+                   float* __restrict__ gamma) {
+  __shared__ double sh[8];
+  const MatDev md = mats[blockIdx.x];
+  double acc = 0.0;
+  for (int o = threadIdx.x; o < md.d_out; o += blockDim.x) acc += rs[static_cast<int64_t>(blockIdx.x) * ld_rs + o].y;
+  const double t = block_sum_d<256>(acc, sh);
+  if (threadIdx.x == 0) {
+    const float nrm = static_cast<float>(sqrt(t));
+    gamma[blockIdx.x] = md.sqrt_rows / fmaxf(nrm, kFltTiny);
+  }
+}
+
+// ======================================== N7 pass 2: mapback + update apply
+// W[o,i] -= lr * gamma * inv_b[o] * inv_a[i] * (Q^p[o,i] + c t[o] z[i])
+// (sandmuon/optimizer.py:303-315).  Tile 32 param rows x 64 param columns;
+// transposed matrices read Q through a shared-memory transpose.
+template <bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_mapback_apply(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+                    const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma) {
+  __shared__ float sh[64][33];
+  const int b = blockIdx.z;
+  const MatDev md = mats[b];
+  const int o0 = blockIdx.y * 32;
+  const int i0 = blockIdx.x * 64;
+  if (o0 >= md.d_out || i0 >= md.d_in) return;
+  const float* qb = q + static_cast<int64_t>(b) * rp * cp;
+  const float step = md.lr * gamma[b];
+  const float coef = RANK1 ? md.scal_a[0] : 0.0f;
+  const bool trans = md.transposed != 0;
+  if (trans) {
+    // oriented rows i0..i0+63, columns o0..o0+31 -> sh[il][ol]
+    for (int e = threadIdx.x; e < 64 * 32; e += 256) {
+      const int il = e >> 5, ol = e & 31;
+      const int i = i0 + il, o = o0 + ol;
+      sh[il][ol] = (i < md.d_in && o < md.d_out) ? qb[static_cast<int64_t>(i) * cp + o] : 0.0f;
+    }
+    __syncthreads();
+  }
+  const int tx = threadIdx.x & 63;  // column
+  const int ty = threadIdx.x >> 6;  // 0..3
+  const int i = i0 + tx;
+  if (i >= md.d_in) return;
+  const float a = md.inv_a[i];
+  const float z = RANK1 ? md.z_a[i] : 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int ol = ty + 4 * k;
+    const int o = o0 + ol;
+    if (o >= md.d_out) break;
+    const float qv = trans ? sh[tx][ol] : qb[static_cast<int64_t>(o) * cp + i];
+    float v = qv;
+    if (RANK1) v += coef * rs[static_cast<int64_t>(b) * ld_rs + o].x * z;
+    const float u = (v * md.inv_b[o]) * a;
+    const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
+    md.weight[wi] = md.weight[wi] - step * u;
+  }
+}
+
+// ============================================================ N8: AdamW
+constexpr int kAdamMaxTensors = 24;
+
+struct AdamBatch {
+  float* param[kAdamMaxTensors];
+  const float* grad[kAdamMaxTensors];
+  float* m1[kAdamMaxTensors];
+  float* m2[kAdamMaxTensors];
+  int64_t numel[kAdamMaxTensors];
+  int64_t chunk_start[kAdamMaxTensors + 1];  // prefix sums of 4096-element chunks
+  float bc1[kAdamMaxTensors];
+  float bc2[kAdamMaxTensors];
+  int32_t count;
+};
+
+constexpr int kAdamChunk = 4096;
+
+__global__ void __launch_bounds__(256)
+    k_adamw_multi(const AdamBatch batch, float lr, float beta1, float omb1, float beta2, float omb2, float eps,
+                  float decay) {
+  const int64_t total_chunks = batch.chunk_start[batch.count];
+  for (int64_t ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
+    int t = 0;
+    while (batch.chunk_start[t + 1] <= ch) ++t;
+    const int64_t base = (ch - batch.chunk_start[t]) * kAdamChunk;
+    const int64_t end = min(base + kAdamChunk, batch.numel[t]);
+    float* p = batch.param[t];
+    const float* g = batch.grad[t];
+    float* m1 = batch.m1[t];
+    float* m2 = batch.m2[t];
+    const float bc1 = batch.bc1[t], bc2 = batch.bc2[t];
+    for (int64_t e = base + threadIdx.x; e < end; e += blockDim.x) {
+      const float gv = g[e];
+      const float a = m1[e] * beta1 + omb1 * gv;
+      const float v = m2[e] * beta2 + omb2 * (gv * gv);
+      m1[e] = a;
+      m2[e] = v;
+      const float upd = (a / bc1) / (sqrtf(v / bc2) + eps);
+      const float pv = p[e] * decay;
+      p[e] = pv - lr * upd;
+    }
+  }
+}
+
+}  // namespace smb

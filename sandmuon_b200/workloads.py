@@ -1,0 +1,99 @@
+"""Synthetic workloads of the benchmark configurations (seeded numpy).
+
+Used by bench.py and the tests to build the config-1 / config-4 matrix sets
+and the accumulated hook statistics they would have after a number of
+microbatches.  Statistics are drawn like config 0: per-channel activation mean
+~ N(0.1, 0.05^2) and std ~ LogNormal(0, 0.5); per-output-channel cotangent
+scale 1e-3 * LogNormal(0, 0.5).  Not used by the optimizer itself.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+from torch import nn
+
+
+def gpt_matrix_model(layers: int, width: int, hidden: int) -> nn.Module:
+    """Module tree with the historical GPT names (q/k/v/o, mlp.c_fc, mlp.c_proj)
+    holding only the bias-free Linear weights the optimizer selects."""
+    root = nn.Module()
+    root.transformer = nn.Module()
+    blocks = []
+    for _ in range(layers):
+        blk = nn.Module()
+        blk.attn = nn.Module()
+        for proj in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            setattr(blk.attn, proj, nn.Linear(width, width, bias=False))
+        blk.mlp = nn.Module()
+        blk.mlp.c_fc = nn.Linear(width, hidden, bias=False)
+        blk.mlp.c_proj = nn.Linear(hidden, width, bias=False)
+        blocks.append(blk)
+    root.transformer.h = nn.ModuleList(blocks)
+    return root
+
+
+CONFIGS = {
+    "cfg1": dict(layers=9, width=768, hidden=3072, microbatches=8, rows=16 * 1024),
+    "cfg4": dict(layers=24, width=2048, hidden=8192, microbatches=8, rows=8 * 2048),
+}
+
+
+def synth_gpt_statistics(opt, rng: np.random.Generator, count: int, *, inject: bool = True) -> dict:
+    """Accumulated sums of `count` rows for every matrix of `opt`; when
+    `inject`, also writes them into opt.state like the hooks would.
+
+    Returns {name: dict(a_sum, a_first_sum, a_count, b_sum, b_count)} with the
+    a_* entries only for activation-statistic sources."""
+    out = {}
+    for name, p in opt.named_matrices.items():
+        d_out, d_in = p.shape
+        entry = {}
+        source = opt.a_sources[id(p)]
+        if source is p:
+            mean = rng.normal(0.1, 0.05, d_in)
+            std = np.exp(rng.normal(0.0, 0.5, d_in))
+            noise = 1.0 + 0.01 * rng.standard_normal(d_in)
+            entry["a_sum"] = (count * (mean ** 2 + std ** 2) * noise).astype(np.float32)
+            entry["a_first_sum"] = (count * mean * noise).astype(np.float32)
+            entry["a_count"] = count
+        scale = 1e-3 * np.exp(rng.normal(0.0, 0.5, d_out))
+        entry["b_sum"] = (count * scale ** 2 * (1.0 + 0.01 * rng.standard_normal(d_out))).astype(np.float32)
+        entry["b_count"] = count
+        out[name] = entry
+    if inject:
+        inject_statistics(opt, out)
+    return out
+
+
+def inject_statistics(opt, stats: dict) -> None:
+    """Writes accumulated sums into opt.state (the hooks' state layout)."""
+    for name, entry in stats.items():
+        p = opt.named_matrices[name]
+        st = opt.state[p]
+        if "a_sum" in entry:
+            for key in ("a_sum", "a_first_sum"):
+                if key == "a_first_sum" and not opt.rank_one_a:
+                    continue
+                t = torch.from_numpy(entry[key]).to(p.device)
+                if key in st and st[key].shape == t.shape:
+                    st[key].copy_(t, non_blocking=True)
+                else:
+                    st[key] = t
+            st["a_count"] = int(entry["a_count"])
+        t = torch.from_numpy(entry["b_sum"]).to(p.device)
+        if "b_sum" in st and st["b_sum"].shape == t.shape:
+            st["b_sum"].copy_(t, non_blocking=True)
+        else:
+            st["b_sum"] = t
+        st["b_count"] = int(entry["b_count"])
+
+
+def s8_executed_flops(shapes) -> float:
+    """Executed BF16 tensor FLOPs of one S8 map per matrix, summed:
+    7 * (4 r^2 c + 2 r^3) with r <= c (stage 1's three compensated products
+    plus four plain stages)."""
+    total = 0.0
+    for rows, cols in shapes:
+        r, c = min(rows, cols), max(rows, cols)
+        total += 7.0 * (4.0 * r * r * c + 2.0 * r ** 3)
+    return total
