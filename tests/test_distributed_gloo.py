@@ -1,0 +1,119 @@
+"""Multi-rank host logic of the matrix sharding on CPU with gloo, world size 2.
+
+The CUDA step is replaced by a test-only stub (a deterministic per-owner
+update), so these tests check partitioning, the statistic all-reduce and the
+weight exchange without a GPU.  The stub exists only here, not in the product.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from sandmuon_b200.distributed import MatrixSharding, partition_matrices
+from sandmuon_b200.workloads import gpt_matrix_model, s8_executed_flops
+
+
+def test_lpt_partition_balances_s8_flops():
+    shapes = {f"transformer.h.{l}.attn.{p}.weight": (768, 768) for l in range(9)
+              for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
+    shapes.update({f"transformer.h.{l}.mlp.c_fc.weight": (3072, 768) for l in range(9)})
+    shapes.update({f"transformer.h.{l}.mlp.c_proj.weight": (768, 3072) for l in range(9)})
+    for world in (1, 2, 4, 8):
+        owner = partition_matrices(shapes, world, "lpt")
+        load = [0.0] * world
+        for n, r in owner.items():
+            load[r] += s8_executed_flops([shapes[n]])
+        assert set(owner) == set(shapes) and set(owner.values()) <= set(range(world))
+        assert max(load) / (sum(load) / world) < 1.2
+        by_layer = partition_matrices(shapes, world, "layer")
+        layers = {}
+        for n, r in by_layer.items():
+            layers.setdefault(n.split(".")[2], set()).add(r)
+        assert all(len(rs) == 1 for rs in layers.values())
+    with pytest.raises(ValueError):
+        partition_matrices(shapes, 2, "round_robin")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class _StubOptimizer:
+    """The attributes MatrixSharding reads from an optimizer."""
+
+    def __init__(self, model):
+        from sandmuon_b200.optimizer import _QKV_SHARING
+        self.named_matrices = {n + ".weight": m.weight for n, m in model.named_modules()
+                               if isinstance(m, torch.nn.Linear)}
+        self.rank_one_a = True
+        self.state = {}
+        self.a_sources = {id(p): p for p in self.named_matrices.values()}
+        for name, p in self.named_matrices.items():
+            match = _QKV_SHARING.match(name)
+            if match:
+                self.a_sources[id(p)] = self.named_matrices[match.group(1) + "q_proj.weight"]
+
+
+def _worker(rank, world, port, partition, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        model = gpt_matrix_model(3, 16, 64)
+        opt = _StubOptimizer(model)
+        sharding = MatrixSharding(opt, dist.group.WORLD, partition=partition)
+        items = []
+        for name, p in opt.named_matrices.items():
+            src = opt.a_sources[id(p)]
+            st_src = opt.state.setdefault(src, {})
+            if "a_sum" not in st_src:
+                st_src.update(a_sum=torch.full((p.shape[1],), float(rank + 1)),
+                              a_first_sum=torch.full((p.shape[1],), float(rank)), a_count=10 * (rank + 1))
+            st = opt.state.setdefault(p, {})
+            st.update(b_sum=torch.full((p.shape[0],), 2.0 * (rank + 1)), b_count=10 * (rank + 1))
+            items.append((p, src, {}))
+        sharding.reduce_statistics(items)
+        # test-only compute stub: each owner writes a value unique to (matrix, owner)
+        with torch.no_grad():
+            for i, (p, _, _) in enumerate(items):
+                if sharding.owns(p):
+                    p.fill_(100.0 * i + sharding.rank)
+                else:
+                    p.fill_(-1.0)
+        sharding.exchange(items)
+        out = {}
+        for i, (p, src, _) in enumerate(items):
+            out[i] = (float(p.min()), float(p.max()), sharding.owner(p),
+                      float(opt.state[src]["a_sum"][0]), float(opt.state[src]["a_first_sum"][0]),
+                      opt.state[src]["a_count"], float(opt.state[p]["b_sum"][0]), opt.state[p]["b_count"])
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("partition", ["lpt", "layer"])
+def test_two_rank_statistics_reduction_and_weight_exchange(partition):
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, partition, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0, r1 = results[0], results[1]
+    assert r0 == r1                       # every rank ends with identical weights and statistics
+    owners = {v[2] for v in r0.values()}
+    assert owners == {0, 1}
+    for i, (lo, hi, owner, a_sum, a_first, a_count, b_sum, b_count) in r0.items():
+        assert lo == hi == 100.0 * i + owner  # the owner's update reached every rank
+        assert a_sum == 1.0 + 2.0 and a_first == 0.0 + 1.0 and a_count == 30
+        assert b_sum == 2.0 + 4.0 and b_count == 30
