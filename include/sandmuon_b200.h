@@ -90,6 +90,29 @@ int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_c
                         int64_t row_stride, int64_t col_stride, float* sum_sq, float* sum,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same statistics as sm_stats_accumulate, for callers that cannot allocate
+ * device memory.  No counterpart in the reference: its hooks always let torch
+ * allocate temporaries.  Some callers hold only the tensors they were handed:
+ * a statistics hook running inside another framework's training step, where
+ * that framework's allocator owns the rest of HBM (a caching allocator usually
+ * reserves most of it), so a raw cudaMalloc can fail or fragment its pool, and
+ * cudaFree synchronises the whole device in the middle of the step.
+ * The partial sums go to one library-owned scratch array of
+ * SM_STATS_NOALLOC_SCRATCH_FLOATS floats (2 MiB) that every GPU which loads
+ * the library keeps until the process exits.  Limit: n_cols <=
+ * SM_STATS_NOALLOC_MAX_COLS; larger inputs return SM_ERR_ARG before any device
+ * work.  The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Each device has its own copy of the array, shared by every call on that
+ * device; a call overwrites the partial sums the previous call left there
+ * before reading them, so nothing needs clearing, but calls that overlap on
+ * the GPU (for example on two streams) race: keep them in one stream order. */
+#define SM_STATS_NOALLOC_SCRATCH_FLOATS (1 << 19)
+#define SM_STATS_NOALLOC_MAX_COLS (SM_STATS_NOALLOC_SCRATCH_FLOATS / 2)
+int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int64_t n_cols,
+                                int64_t row_stride, int64_t col_stride, float* sum_sq, float* sum,
+                                void* stream);
+
 /* ------------------------------------------------------ optimizer plan */
 
 /* One selected weight matrix (a torch Linear weight, shape [d_out, d_in],

@@ -73,6 +73,8 @@ SIGNATURES = {
     "sm_stats_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
     "sm_stats_accumulate": (_c_int, [_c_void_p, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_void_p, _c_void_p,
                                      _c_void_p, _c_size, _c_void_p]),
+    "sm_stats_accumulate_noalloc": (_c_int, [_c_void_p, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_void_p,
+                                             _c_void_p, _c_void_p]),
     "sm_plan_workspace_bytes": (_c_int, [ctypes.POINTER(SmPlanSpec), ctypes.POINTER(_c_size)]),
     "sm_plan_create": (_c_int, [ctypes.POINTER(SmPlanSpec), _c_void_p, _c_size, _c_void_p, ctypes.POINTER(_c_void_p)]),
     "sm_plan_step": (_c_int, [_c_void_p, ctypes.POINTER(SmStepArgs), _c_void_p]),

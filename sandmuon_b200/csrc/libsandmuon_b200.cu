@@ -727,6 +727,66 @@ static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, 
   return SM_OK;
 }
 
+// ------------------------------------------ statistics without a workspace
+// Library-owned scratch for sm_stats_accumulate_noalloc: the per-split
+// partial sums live here instead of in a caller workspace.  One copy per
+// device, kept until the process exits.  Host code must not use the symbol as
+// a pointer: its device address comes from cudaGetSymbolAddress, looked up
+// once per device with that device current.
+static __device__ __align__(256) float g_noalloc_scratch[SM_STATS_NOALLOC_SCRATCH_FLOATS];
+static std::mutex g_noalloc_mutex;
+static float* g_noalloc_addr[64] = {};
+
+static int noalloc_scratch_address(float** out) {
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(SM_ERR_CUDA, std::string("cudaGetSymbolAddress(noalloc scratch): ") + cudaGetErrorString(e));
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return SM_OK;
+}
+
+// Same two kernels as stats_launch; the number of row splits is capped so the
+// partials fit the fixed scratch array.  Every (split, column) partial is
+// written before the finish kernel reads it, so stale contents never leak.
+template <typename T>
+static int stats_launch_noalloc(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
+                                float* sum, float* scratch, cudaStream_t st, int sms) {
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec_ok = cs == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                      ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
+  const int vec = vec_ok ? kVec : 1;
+  int64_t splits = stats_splits(n_rows, n_cols, vec, sms);
+  const int64_t per_split = n_cols * (sum ? 2 : 1);
+  const int64_t cap = static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS) / per_split;
+  if (cap < 1) return fail(SM_ERR_ARG, "too many columns for the no-allocation scratch");
+  if (splits > cap) splits = cap;
+  const int64_t rps = cdiv(n_rows, splits);
+  splits = cdiv(n_rows, rps);
+  float* part_sq = scratch;
+  float* part_s = sum ? scratch + splits * n_cols : nullptr;
+  dim3 grid(static_cast<unsigned>(cdiv(n_cols, 32 * vec)), static_cast<unsigned>(splits));
+  if (vec_ok) {
+    if (sum) k_colstats_partial<T, kVec, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+    else k_colstats_partial<T, kVec, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+  } else {
+    if (sum) k_colstats_partial<T, 1, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+    else k_colstats_partial<T, 1, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
+  }
+  SM_LAUNCHED();
+  const int fin_blocks = static_cast<int>(std::min<int64_t>(cdiv(n_cols, 256), 4 * sms));
+  k_colstats_finish<<<fin_blocks, 256, 0, st>>>(part_sq, part_s, static_cast<int>(splits), n_cols, sum_sq, sum);
+  SM_LAUNCHED();
+  return SM_OK;
+}
+
 // Layout: Group buffers, then MatDev table [batch], ones [max(rows, cols)].
 static int s8_layout(int32_t batch, int32_t rows, int32_t cols, void* ws, Group* g, MatDev** d_mats, float** ones,
                      size_t* bytes) {
@@ -801,6 +861,38 @@ int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_c
     case SM_DTYPE_F64:
       return stats_launch(static_cast<const double*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq, sum,
                           workspace, workspace_bytes, st, di->sms);
+    default:
+      return fail(SM_ERR_ARG, "unsupported dtype code " + std::to_string(dtype));
+  }
+}
+
+int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int64_t n_cols, int64_t row_stride,
+                                int64_t col_stride, float* sum_sq, float* sum, void* stream) {
+  if (n_rows < 0 || n_cols < 0) return fail(SM_ERR_ARG, "negative shape");
+  if (n_cols > SM_STATS_NOALLOC_MAX_COLS)
+    return fail(SM_ERR_ARG, "sm_stats_accumulate_noalloc supports at most " +
+                                std::to_string(SM_STATS_NOALLOC_MAX_COLS) + " columns; got " + std::to_string(n_cols) +
+                                " (use sm_stats_accumulate with a caller workspace)");
+  if (n_rows == 0 || n_cols == 0) return SM_OK;
+  if (rows == nullptr || sum_sq == nullptr) return fail(SM_ERR_ARG, "null input or output");
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  float* scratch = nullptr;
+  SM_TRY(noalloc_scratch_address(&scratch));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SM_DTYPE_F32:
+      return stats_launch_noalloc(static_cast<const float*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
+                                  sum, scratch, st, di->sms);
+    case SM_DTYPE_BF16:
+      return stats_launch_noalloc(static_cast<const __nv_bfloat16*>(rows), n_rows, n_cols, row_stride, col_stride,
+                                  sum_sq, sum, scratch, st, di->sms);
+    case SM_DTYPE_F16:
+      return stats_launch_noalloc(static_cast<const __half*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
+                                  sum, scratch, st, di->sms);
+    case SM_DTYPE_F64:
+      return stats_launch_noalloc(static_cast<const double*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
+                                  sum, scratch, st, di->sms);
     default:
       return fail(SM_ERR_ARG, "unsupported dtype code " + std::to_string(dtype));
   }
