@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
+    ap.add_argument("--profile", action="store_true",
+                    help="only warm-up + timed steps (for ncu): no CPU baseline, clock probe or e2e pass")
     return ap.parse_args()
 
 
@@ -264,6 +266,18 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
         group = dist.group.WORLD
     model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition)
+    if args.profile:
+        for _ in range(args.warmup + args.steps):
+            refill()
+            opt.step()
+        torch.cuda.synchronize(device)
+        if rank == 0:
+            print(json.dumps({"profile_steps": args.warmup + args.steps,
+                              "launches_per_step": opt._last_plan.launches_per_step()}), flush=True)
+        opt.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
     sampler = ClockSampler(local)
     for _ in range(max(args.warmup, 3)):
         refill()
