@@ -231,6 +231,9 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
 #define SM_EPI_F32_NORM 3   /* FP32 store + per-tile sum of squares partials  */
 #define SM_EPI_POLY 4       /* C = bf16(pa*I + pb*aux + pc*acc)                */
 #define SM_EPI_POLY_HILO 5  /* P = pa*I + pb*(aux + aux_lo) + pc*acc -> hi/lo  */
+#define SM_EPI_SYMMETRIC 0x100 /* flag: C is symmetric (M == N, K-major B); only the
+                                 upper-triangular 128x128 tiles are computed and each
+                                 off-diagonal tile also stores its transpose        */
 
 /* Batched C[b] = A[b] * op(B[b]) on tcgen05 tensor cores.
  *   A: [batch, M, K] BF16 row-major (K contiguous); a_lo != NULL selects the

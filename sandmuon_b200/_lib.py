@@ -23,6 +23,7 @@ SM_EPI_HILO = 2
 SM_EPI_F32_NORM = 3
 SM_EPI_POLY = 4
 SM_EPI_POLY_HILO = 5
+SM_EPI_SYMMETRIC = 0x100
 SM_TCLASS_GEMM = 0
 SM_TCLASS_ELEMWISE = 1
 SM_TCLASS_STATS = 2

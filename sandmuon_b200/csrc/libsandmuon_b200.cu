@@ -121,21 +121,25 @@ static int get_encode(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return SM_OK;
 }
 
-// 3-D BF16 tensor [batch, outer, inner] (inner contiguous), box {64, box_outer, 1},
-// 128-byte swizzle.  inner * 2 bytes must be a multiple of 16.
+// 3-D BF16 tensor [batch, outer, inner] (inner contiguous), box
+// {box_inner, box_outer, 1}; box_inner * 2 bytes = the swizzle width
+// (64 -> 128-byte swizzle, 32 -> 64-byte swizzle).  inner * 2 bytes must be a
+// multiple of 16.
 static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t batch,
-                    uint32_t box_outer) {
+                    uint32_t box_inner, uint32_t box_outer) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   SM_TRY(get_encode(&enc));
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(SM_ERR_ARG, "TMA base not 16-byte aligned");
   if ((inner * 2) % 16 != 0) return fail(SM_ERR_ARG, "TMA row stride not a multiple of 16 bytes");
+  if (box_inner != 32 && box_inner != 64) return fail(SM_ERR_ARG, "TMA box inner extent must be 32 or 64");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner * 2), static_cast<cuuint64_t>(inner * outer * 2)};
-  cuuint32_t box[3] = {64, box_outer, 1};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle swz = box_inner == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SM_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
   return SM_OK;
@@ -143,64 +147,88 @@ static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t out
 
 // ------------------------------------------------------------ GEMM launch
 
+// K extent of one pipeline stage: 64 BF16 = 128-byte rows with the 128-byte
+// swizzle (measured faster per MMA than 32 / 64-byte rows).  The ring holds as
+// many stages as fit next to the epilogue staging: BN=256 compensated 2 x 96 KB,
+// BN=128 compensated 3 x 64 KB, plain 4 x 48 KB or 6 x 32 KB.  The SMB_*
+// macros exist for tuning sweeps; the defaults are the shipped configuration.
+#ifndef SMB_BK
+#define SMB_BK 64
+#endif
+#ifndef SMB_COMP_STAGES
+#define SMB_COMP_STAGES 8
+#endif
+#ifndef SMB_PLAIN_STAGES
+#define SMB_PLAIN_STAGES 8
+#endif
+#ifndef SMB_BN_MAX
+#define SMB_BN_MAX 256
+#endif
+#ifndef SMB_USE_SCHEDULE
+#define SMB_USE_SCHEDULE 1
+#endif
+constexpr int kBK = SMB_BK;
+// Operand boxes (inner extent = kBK): A tiles {BK, 128}; K-major B tiles
+// {BK, BN}; MN-major B chunks {row-bytes/2 N-elements, BK K-rows}.
+constexpr uint32_t kChunk = Swz<kBK>::kChunkElems;
+
 template <int BN, bool COMP, bool B_MN, int EPI>
-static int launch_gemm_t(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
-                         const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
-  constexpr int STAGES = COMP ? (BN == 256 ? 2 : 3) : (BN == 256 ? 4 : 6);
-  using L = GemmSmem<BN, COMP, STAGES>;
-  static_assert(L::kTotal <= 232448, "shared memory budget");
-  auto kern = k_gemm_bf16<BN, COMP, B_MN, STAGES, EPI>;
-  DeviceInfo* di;
-  SM_TRY(current_device_info(&di));
-  // The attribute is per function and device; set it once per device.
+static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
+  // Configured depth, capped by what fits in 227 KB of shared memory.
+  constexpr int kStageBytes = GemmSmem<BN, kBK, COMP, 1>::kStageBytes;
+  constexpr int kFit =
+      (232448 - 1024 - 256 - GemmSmem<BN, kBK, COMP, 1>::kStagingBytes) / kStageBytes;
+  constexpr int kWant = COMP ? SMB_COMP_STAGES : SMB_PLAIN_STAGES;
+  constexpr int STAGES = kWant < kFit ? kWant : kFit;
+  using S = GemmSmem<BN, kBK, COMP, STAGES>;
+  static_assert(S::kTotal <= 232448, "shared memory budget");
+  auto kern = k_gemm_bf16<BN, kBK, COMP, B_MN, STAGES, EPI>;
   static bool attr_done[64] = {};
   int dev = 0;
   SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
   if (!attr_done[dev]) {
-    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
     attr_done[dev] = true;
   }
-  const int total = a.tiles_m * a.tiles_n * a.batch;
-  if (total == 0) return SM_OK;
-  const int grid = std::min(total, di->sms);
-  kern<<<grid, kGemmThreads, L::kTotal, st>>>(ah, al, bh, bl, a);
+  if (L.total_tiles == 0 || grid == 0) return SM_OK;
+  kern<<<grid, kGemmThreads, S::kTotal, st>>>(L);
   SM_LAUNCHED();
   return SM_OK;
 }
 
 template <int BN>
-static int dispatch_gemm_bn(bool comp, bool b_mn, int epi, const CUtensorMap& ah, const CUtensorMap& al,
-                            const CUtensorMap& bh, const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
+static int dispatch_gemm_bn(bool comp, bool b_mn, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
   if (!comp) {
     if (!b_mn) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, false, false, kEpiF32>(ah, al, bh, bl, a, st);
-        case kEpiBF16: return launch_gemm_t<BN, false, false, kEpiBF16>(ah, al, bh, bl, a, st);
-        case kEpiPoly: return launch_gemm_t<BN, false, false, kEpiPoly>(ah, al, bh, bl, a, st);
+        case kEpiF32: return launch_gemm_t<BN, false, false, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, false, false, kEpiBF16>(L, grid, st);
+        case kEpiPoly: return launch_gemm_t<BN, false, false, kEpiPoly>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, false, true, kEpiF32>(ah, al, bh, bl, a, st);
-        case kEpiBF16: return launch_gemm_t<BN, false, true, kEpiBF16>(ah, al, bh, bl, a, st);
+        case kEpiF32: return launch_gemm_t<BN, false, true, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, false, true, kEpiBF16>(L, grid, st);
         default: break;
       }
     }
   } else {
     if (!b_mn) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, true, false, kEpiF32>(ah, al, bh, bl, a, st);
-        case kEpiBF16: return launch_gemm_t<BN, true, false, kEpiBF16>(ah, al, bh, bl, a, st);
-        case kEpiHiLo: return launch_gemm_t<BN, true, false, kEpiHiLo>(ah, al, bh, bl, a, st);
-        case kEpiF32Norm: return launch_gemm_t<BN, true, false, kEpiF32Norm>(ah, al, bh, bl, a, st);
-        case kEpiPolyHiLo: return launch_gemm_t<BN, true, false, kEpiPolyHiLo>(ah, al, bh, bl, a, st);
+        case kEpiF32: return launch_gemm_t<BN, true, false, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, true, false, kEpiBF16>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, true, false, kEpiHiLo>(L, grid, st);
+        case kEpiF32Norm: return launch_gemm_t<BN, true, false, kEpiF32Norm>(L, grid, st);
+        case kEpiPolyHiLo: return launch_gemm_t<BN, true, false, kEpiPolyHiLo>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, true, true, kEpiF32>(ah, al, bh, bl, a, st);
-        case kEpiBF16: return launch_gemm_t<BN, true, true, kEpiBF16>(ah, al, bh, bl, a, st);
-        case kEpiHiLo: return launch_gemm_t<BN, true, true, kEpiHiLo>(ah, al, bh, bl, a, st);
+        case kEpiF32: return launch_gemm_t<BN, true, true, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, true, true, kEpiBF16>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, true, true, kEpiHiLo>(L, grid, st);
         default: break;
       }
     }
@@ -209,14 +237,82 @@ static int dispatch_gemm_bn(bool comp, bool b_mn, int epi, const CUtensorMap& ah
                               ", b_mn_major=" + std::to_string(b_mn) + ", epilogue=" + std::to_string(epi) + ")");
 }
 
-static int dispatch_gemm(int bn, bool comp, bool b_mn, int epi, const CUtensorMap& ah, const CUtensorMap& al,
-                         const CUtensorMap& bh, const CUtensorMap& bl, const GemmArgs& a, cudaStream_t st) {
-  if (bn == 256) return dispatch_gemm_bn<256>(comp, b_mn, epi, ah, al, bh, bl, a, st);
-  if (bn == 128) return dispatch_gemm_bn<128>(comp, b_mn, epi, ah, al, bh, bl, a, st);
+static int dispatch_gemm(int bn, bool comp, bool b_mn, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
+  if (bn == 256) return dispatch_gemm_bn<256>(comp, b_mn, epi, L, grid, st);
+  if (bn == 128) return dispatch_gemm_bn<128>(comp, b_mn, epi, L, grid, st);
   return fail(SM_ERR_ARG, "BN must be 128 or 256");
 }
 
-static inline int pick_bn(int64_t n) { return (n % 256 == 0) ? 256 : 128; }
+static inline int pick_bn(int64_t n) { return (n % 256 == 0 && SMB_BN_MAX >= 256) ? 256 : 128; }
+
+static GemmProblem gemm_problem(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+                                const CUtensorMap& bl, int m, int n, int k, int batch, int bn, int sym = 0) {
+  GemmProblem p;
+  memset(&p, 0, sizeof(p));
+  p.sym = sym;
+  p.a_hi = ah;
+  p.a_lo = al;
+  p.b_hi = bh;
+  p.b_lo = bl;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.batch = batch;
+  p.tiles_m = m / kGemmBM;
+  p.tiles_n = n / bn;
+  return p;
+}
+
+// Tiles of one problem: the full grid, or its upper triangle when symmetric.
+static int64_t problem_tiles(const GemmProblem& p) {
+  if (p.sym) return static_cast<int64_t>(p.tiles_m) * (p.tiles_m + 1) / 2 * p.batch;
+  return static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.batch;
+}
+
+// Executed tensor FLOPs (symmetric products count only the tiles computed).
+static double problem_flops(const GemmProblem& p, bool comp) {
+  const double tile = 2.0 * kGemmBM * (static_cast<double>(p.n) / p.tiles_n) * p.k;
+  return tile * static_cast<double>(problem_tiles(p)) * (comp ? 3.0 : 1.0);
+}
+
+// Balanced static tile schedule for problems given as (tiles, k-blocks per
+// tile), laid out back to back in launch-global tile order.  Tiles are taken
+// longest first and dealt to the least-loaded CTA (ties to the lowest CTA);
+// each CTA keeps its tiles in that order.  Output: [grid + 1] offsets then the
+// tile lists.
+static void lpt_schedule(const std::vector<std::pair<int64_t, int>>& probs, int grid, std::vector<int>& out) {
+  std::vector<std::pair<int, int>> tiles;  // (k-blocks, global tile)
+  int64_t base = 0;
+  for (const auto& pr : probs) {
+    for (int64_t t = 0; t < pr.first; ++t) tiles.push_back({pr.second, static_cast<int>(base + t)});
+    base += pr.first;
+  }
+  std::stable_sort(tiles.begin(), tiles.end(), [](const auto& a, const auto& b) { return a.first > b.first; });
+  std::vector<std::vector<int>> lists(grid);
+  std::vector<int64_t> load(grid, 0);
+  // min-heap on (load, cta)
+  std::vector<std::pair<int64_t, int>> heap;
+  for (int c = 0; c < grid; ++c) heap.push_back({0, c});
+  auto cmp = [](const std::pair<int64_t, int>& a, const std::pair<int64_t, int>& b) {
+    return a.first != b.first ? a.first > b.first : a.second > b.second;
+  };
+  std::make_heap(heap.begin(), heap.end(), cmp);
+  for (const auto& t : tiles) {
+    std::pop_heap(heap.begin(), heap.end(), cmp);
+    auto top = heap.back();
+    lists[top.second].push_back(t.second);
+    top.first += t.first;
+    heap.back() = top;
+    std::push_heap(heap.begin(), heap.end(), cmp);
+  }
+  out.assign(grid + 1 + tiles.size(), 0);
+  int off = 0;
+  for (int c = 0; c < grid; ++c) {
+    out[c] = off;
+    for (int t : lists[c]) out[grid + 1 + off++] = t;
+  }
+  out[grid] = off;
+}
 
 // ------------------------------------------------------------------- timing
 
@@ -322,24 +418,25 @@ static void carve_group(Carver& cv, Group& g) {
 }
 
 static int encode_group_maps(Group& g) {
-  SM_TRY(make_map(&g.xh_A, g.xh, g.cp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.xl_A, g.xl, g.cp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.xh_Bk, g.xh, g.cp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.xl_Bk, g.xl, g.cp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.xh_Bmn, g.xh, g.cp, g.rp, g.batch, 64));
-  SM_TRY(make_map(&g.xl_Bmn, g.xl, g.cp, g.rp, g.batch, 64));
-  SM_TRY(make_map(&g.gh_A, g.gh, g.rp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.gl_A, g.gl, g.rp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.gh_Bk, g.gh, g.rp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.gl_Bk, g.gl, g.rp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.xa_A, g.xa, g.cp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.xa_Bk, g.xa, g.cp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.xa_Bmn, g.xa, g.cp, g.rp, g.batch, 64));
-  SM_TRY(make_map(&g.xb_A, g.xb, g.cp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.xb_Bk, g.xb, g.cp, g.rp, g.batch, g.bn_r));
-  SM_TRY(make_map(&g.xb_Bmn, g.xb, g.cp, g.rp, g.batch, 64));
-  SM_TRY(make_map(&g.ph_A, g.ph, g.rp, g.rp, g.batch, kGemmBM));
-  SM_TRY(make_map(&g.pl_A, g.pl, g.rp, g.rp, g.batch, kGemmBM));
+  const uint32_t bk = kBK;
+  SM_TRY(make_map(&g.xh_A, g.xh, g.cp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.xl_A, g.xl, g.cp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.xh_Bk, g.xh, g.cp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.xl_Bk, g.xl, g.cp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.xh_Bmn, g.xh, g.cp, g.rp, g.batch, kChunk, bk));
+  SM_TRY(make_map(&g.xl_Bmn, g.xl, g.cp, g.rp, g.batch, kChunk, bk));
+  SM_TRY(make_map(&g.gh_A, g.gh, g.rp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.gl_A, g.gl, g.rp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.gh_Bk, g.gh, g.rp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.gl_Bk, g.gl, g.rp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.xa_A, g.xa, g.cp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.xa_Bk, g.xa, g.cp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.xa_Bmn, g.xa, g.cp, g.rp, g.batch, kChunk, bk));
+  SM_TRY(make_map(&g.xb_A, g.xb, g.cp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.xb_Bk, g.xb, g.cp, g.rp, g.batch, bk, g.bn_r));
+  SM_TRY(make_map(&g.xb_Bmn, g.xb, g.cp, g.rp, g.batch, kChunk, bk));
+  SM_TRY(make_map(&g.ph_A, g.ph, g.rp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.pl_A, g.pl, g.rp, g.rp, g.batch, bk, kGemmBM));
   return SM_OK;
 }
 
@@ -348,28 +445,13 @@ static void init_group_shape(Group& g, int r, int c, int batch) {
   g.c = c;
   g.rp = static_cast<int>(round_up(r, 128));
   g.cp = static_cast<int>(round_up(c, 128));
-  g.bn_r = pick_bn(g.rp);
+  g.bn_r = 128;  // X X^T and G G are symmetric: square 128 x 128 tiles, upper triangle only
   g.bn_c = pick_bn(g.cp);
   g.batch = batch;
   g.dmax = c;
 }
 
-static GemmArgs gemm_args(int m, int n, int k, int batch, int bn) {
-  GemmArgs a;
-  memset(&a, 0, sizeof(a));
-  a.m = m;
-  a.n = n;
-  a.k = k;
-  a.batch = batch;
-  a.tiles_m = m / kGemmBM;
-  a.tiles_n = n / bn;
-  return a;
-}
-
-static double gemm_flops(const GemmArgs& a, bool comp) {
-  return 2.0 * a.m * a.n * static_cast<double>(a.k) * a.batch * (comp ? 3.0 : 1.0);
-}
-
+// --------------------------------------------------------- S8 launch plan
 // Stage schedule of the S8 polynomial: stages 1-4 compensated (hi/lo operand
 // planes, three BF16 products, FP32 accumulation), stage 5 plain BF16.
 // Keeping stage 2-4 iterates at ~16 significant bits holds the map within
@@ -377,127 +459,181 @@ static double gemm_flops(const GemmArgs& a, bool comp) {
 // inputs, whose near-zero singular values the later stages amplify ~120x.
 constexpr int kCompensatedStages = 4;
 
-// The five-stage S8 polynomial on the group's stage-1 planes xh/xl (already
-// normalised, oriented, zero-padded).  Result: FP32 Q [B, rp, cp] in g.q.
-// Mirrors _s8_fp32 (sandmuon/optimizer.py:79-91).
-static int run_s8(const Group& g, cudaStream_t st, Timer* tm, int64_t* launches) {
-  const int rp = g.rp, cp = g.cp, B = g.batch;
-  // stage 1: G = X X^T (hi/lo), G2 = G G (FP32 + norm partials)
-  {
-    GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
-    a.out0 = g.gh;
-    a.out1 = g.gl;
-    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-             dispatch_gemm(g.bn_r, true, false, kEpiHiLo, g.xh_A, g.xl_A, g.xh_Bk, g.xl_Bk, a, st));
-    ++*launches;
-  }
-  {
-    GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
-    a.out0 = g.g2;
-    a.partials = g.partials;
-    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-             dispatch_gemm(g.bn_r, true, false, kEpiF32Norm, g.gh_A, g.gl_A, g.gh_Bk, g.gl_Bk, a, st));
-    ++*launches;
-  }
-  {
-    const int per_mat = (rp / kGemmBM) * (rp / g.bn_r) * 4;
-    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-               k_reduce_s8scale<<<B, 256, 0, st>>>(g.partials, per_mat, kS8Margin, g.s, g.s_inv);
-               SM_LAUNCHED();
-               return SM_OK;
-             }()));
-    const int64_t per = static_cast<int64_t>(rp) * rp;
-    const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 2, 256), 512));
-    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-               k_poly_stage1<<<dim3(blocks, B), 256, 0, st>>>(g.gh, g.gl, g.g2, g.s, rp, (float)kS8Coeff[0][0],
-                                                               (float)kS8Coeff[0][1], (float)kS8Coeff[0][2]);
-               SM_LAUNCHED();
-               return SM_OK;
-             }()));
-    *launches += 2;
-  }
-  {
-    // X2 = (P X) / s, emitted as hi/lo planes into xa|xb
-    GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
-    a.out0 = g.xa;
-    a.out1 = g.xb;
-    a.alpha = g.s_inv;
-    SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-             dispatch_gemm(g.bn_c, true, true, kEpiHiLo, g.gh_A, g.gl_A, g.xh_Bmn, g.xl_Bmn, a, st));
-    ++*launches;
-  }
-  // stages 2..5: the iterate alternates between the xa|xb and xh|xl pairs
-  for (int stage = 1; stage < 5; ++stage) {
-    const bool in_a = (stage % 2) == 1;  // stages 2 and 4 read xa|xb
-    const bool comp = stage < kCompensatedStages;
-    const bool next_comp = stage + 1 < kCompensatedStages;
-    const bool last = stage == 4;
-    const CUtensorMap& xA_h = in_a ? g.xa_A : g.xh_A;
-    const CUtensorMap& xA_l = in_a ? g.xb_A : g.xl_A;
-    const CUtensorMap& xBk_h = in_a ? g.xa_Bk : g.xh_Bk;
-    const CUtensorMap& xBk_l = in_a ? g.xb_Bk : g.xl_Bk;
-    const CUtensorMap& xBmn_h = in_a ? g.xa_Bmn : g.xh_Bmn;
-    const CUtensorMap& xBmn_l = in_a ? g.xb_Bmn : g.xl_Bmn;
-    __nv_bfloat16* out_h = in_a ? g.xh : g.xa;
-    __nv_bfloat16* out_l = in_a ? g.xl : g.xb;
-    const float pa = static_cast<float>(kS8Coeff[stage][0]);
-    const float pb = static_cast<float>(kS8Coeff[stage][1]);
-    const float pc = static_cast<float>(kS8Coeff[stage][2]);
-    if (comp) {
-      {  // G = X X^T as hi/lo
-        GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
-        a.out0 = g.gh;
-        a.out1 = g.gl;
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-                 dispatch_gemm(g.bn_r, true, false, kEpiHiLo, xA_h, xA_l, xBk_h, xBk_l, a, st));
+enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
+
+// Groups whose products share a launch (same BN), longest K first, with an
+// optional balanced tile schedule in device memory.
+struct LaunchSet {
+  std::vector<int> groups;
+  int bn = 0;
+  int grid = 0;
+  int* sched = nullptr;
+  std::vector<int> h_sched;
+};
+
+struct S8Launches {
+  std::vector<LaunchSet> sets[3];
+};
+
+static int kind_bn(const Group& g, int kind) { return kind == kPX ? g.bn_c : g.bn_r; }
+static int kind_k(const Group& g, int kind) { return kind == kGram ? g.cp : g.rp; }
+static int kind_n(const Group& g, int kind) { return kind == kPX ? g.cp : g.rp; }
+
+// Builds the launch sets of every GEMM kind.  With `cv` the tile schedules
+// are carved from the workspace (measured when cv.base is null).
+static void build_s8_launches(const std::vector<Group>& groups, int sms, Carver* cv, S8Launches* out) {
+  for (int kind = 0; kind < 3; ++kind) {
+    std::vector<LaunchSet>& sets = out->sets[kind];
+    sets.clear();
+    for (int gi = 0; gi < static_cast<int>(groups.size()); ++gi) {
+      const int bn = kind_bn(groups[gi], kind);
+      LaunchSet* set = nullptr;
+      for (auto& s : sets)
+        if (s.bn == bn && static_cast<int>(s.groups.size()) < kMaxProblems) set = &s;
+      if (set == nullptr) {
+        sets.push_back(LaunchSet());
+        set = &sets.back();
+        set->bn = bn;
       }
-      {  // P = a I + b G + c G G as hi/lo (into the g2 bytes)
-        GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
-        a.out0 = g.ph;
-        a.out1 = g.pl;
-        a.aux = g.gh;
-        a.aux_lo = g.gl;
-        a.pa = pa;
-        a.pb = pb;
-        a.pc = pc;
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-                 dispatch_gemm(g.bn_r, true, false, kEpiPolyHiLo, g.gh_A, g.gl_A, g.gh_Bk, g.gl_Bk, a, st));
+      set->groups.push_back(gi);
+    }
+    for (auto& set : sets) {
+      std::stable_sort(set.groups.begin(), set.groups.end(), [&](int a, int b) {
+        return kind_k(groups[a], kind) > kind_k(groups[b], kind);
+      });
+      std::vector<std::pair<int64_t, int>> probs;
+      int64_t total = 0;
+      for (int gi : set.groups) {
+        const Group& g = groups[gi];
+        const int64_t tm = g.rp / kGemmBM;
+        const int64_t tiles = kind == kPX ? tm * (kind_n(g, kind) / set.bn) * g.batch : tm * (tm + 1) / 2 * g.batch;
+        probs.push_back({tiles, kind_k(g, kind) / kBK});
+        total += tiles;
       }
-      {  // X' = P X (hi/lo for a compensated next stage, else BF16)
-        GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
-        a.out0 = out_h;
-        a.out1 = out_l;
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, true), st,
-                 dispatch_gemm(g.bn_c, true, true, next_comp ? kEpiHiLo : kEpiBF16, g.ph_A, g.pl_A, xBmn_h,
-                               xBmn_l, a, st));
-      }
-    } else {
-      {  // G = X X^T (BF16)
-        GemmArgs a = gemm_args(rp, rp, cp, B, g.bn_r);
-        a.out0 = g.gh;
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
-                 dispatch_gemm(g.bn_r, false, false, kEpiBF16, xA_h, xA_h, xBk_h, xBk_h, a, st));
-      }
-      {  // P = a I + b G + c G G (BF16)
-        GemmArgs a = gemm_args(rp, rp, rp, B, g.bn_r);
-        a.out0 = g.gl;
-        a.aux = g.gh;
-        a.pa = pa;
-        a.pb = pb;
-        a.pc = pc;
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
-                 dispatch_gemm(g.bn_r, false, false, kEpiPoly, g.gh_A, g.gh_A, g.gh_Bk, g.gh_Bk, a, st));
-      }
-      {  // X' = P X; the last stage writes FP32 Q over the xa|xb bytes
-        GemmArgs a = gemm_args(rp, cp, rp, B, g.bn_c);
-        if (last && in_a) return fail(SM_ERR_ARG, "stage schedule would overwrite the last iterate");
-        a.out0 = last ? static_cast<void*>(g.q) : static_cast<void*>(out_h);
-        SM_TIMED(tm, SM_TCLASS_GEMM, gemm_flops(a, false), st,
-                 dispatch_gemm(g.bn_c, false, true, last ? kEpiF32 : kEpiBF16, g.gl_A, g.gl_A, xBmn_h, xBmn_h, a,
-                               st));
+      set.grid = static_cast<int>(std::min<int64_t>(total, sms));
+      if (cv != nullptr && set.grid > 0 && SMB_USE_SCHEDULE) {
+        lpt_schedule(probs, set.grid, set.h_sched);
+        set.sched = cv->take<int>(set.h_sched.size());
       }
     }
-    *launches += 3;
+  }
+}
+
+// The GEMM of `kind` in S8 stage `stage` (0-based) for group g: operands,
+// outputs and epilogue.  Iterates alternate between the xa|xb and xh|xl pairs.
+static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* epi) {
+  const bool comp = stage < kCompensatedStages;
+  const bool in_a = (stage % 2) == 1;  // stages 2 and 4 read xa|xb
+  const CUtensorMap& xA_h = in_a ? g.xa_A : g.xh_A;
+  const CUtensorMap& xA_l = in_a ? g.xb_A : g.xl_A;
+  const CUtensorMap& xBk_h = in_a ? g.xa_Bk : g.xh_Bk;
+  const CUtensorMap& xBk_l = in_a ? g.xb_Bk : g.xl_Bk;
+  const CUtensorMap& xBmn_h = in_a ? g.xa_Bmn : g.xh_Bmn;
+  const CUtensorMap& xBmn_l = in_a ? g.xb_Bmn : g.xl_Bmn;
+  GemmProblem p;
+  if (kind == kGram) {
+    p = gemm_problem(xA_h, comp ? xA_l : xA_h, xBk_h, comp ? xBk_l : xBk_h, g.rp, g.rp, g.cp, g.batch, bn, 1);
+    p.out0 = g.gh;
+    p.out1 = g.gl;
+    *epi = comp ? kEpiHiLo : kEpiBF16;
+  } else if (kind == kGramSq) {
+    p = gemm_problem(g.gh_A, comp ? g.gl_A : g.gh_A, g.gh_Bk, comp ? g.gl_Bk : g.gh_Bk, g.rp, g.rp, g.rp, g.batch,
+                     bn, 1);
+    if (stage == 0) {
+      p.out0 = g.g2;
+      p.partials = g.partials;
+      *epi = kEpiF32Norm;
+    } else {
+      p.pa = static_cast<float>(kS8Coeff[stage][0]);
+      p.pb = static_cast<float>(kS8Coeff[stage][1]);
+      p.pc = static_cast<float>(kS8Coeff[stage][2]);
+      p.aux = g.gh;
+      if (comp) {
+        p.aux_lo = g.gl;
+        p.out0 = g.ph;
+        p.out1 = g.pl;
+        *epi = kEpiPolyHiLo;
+      } else {
+        p.out0 = g.gl;
+        *epi = kEpiPoly;
+      }
+    }
+  } else {
+    // P lives in gh|gl (stage 1, written by k_poly_stage1), in the g2 bytes
+    // (stages 2-4) or in gl (stage 5).
+    const CUtensorMap& pA_h = stage == 0 ? g.gh_A : (comp ? g.ph_A : g.gl_A);
+    const CUtensorMap& pA_l = stage == 0 ? g.gl_A : (comp ? g.pl_A : g.gl_A);
+    p = gemm_problem(pA_h, pA_l, xBmn_h, comp ? xBmn_l : xBmn_h, g.rp, g.cp, g.rp, g.batch, bn);
+    const bool last = stage == 4;
+    const bool next_comp = stage + 1 < kCompensatedStages;
+    if (last) {
+      p.out0 = g.q;  // over the xa|xb bytes; stage 5 reads xh
+      *epi = kEpiF32;
+    } else {
+      p.out0 = in_a ? g.xh : g.xa;
+      p.out1 = in_a ? g.xl : g.xb;
+      *epi = next_comp ? kEpiHiLo : kEpiBF16;
+    }
+    if (stage == 0) p.alpha = g.s_inv;  // X2 = (P X) / s
+  }
+  return p;
+}
+
+static int launch_s8_kind(const std::vector<Group>& groups, const S8Launches& plan, int kind, int stage,
+                          cudaStream_t st, Timer* tm, int64_t* launches) {
+  const bool comp = stage < kCompensatedStages;
+  for (const LaunchSet& set : plan.sets[kind]) {
+    GemmLaunch L;
+    memset(&L, 0, sizeof(L));
+    int epi = -1;
+    int begin = 0;
+    double flops = 0.0;
+    for (int gi : set.groups) {
+      int e = -1;
+      GemmProblem p = s8_problem(groups[gi], kind, stage, set.bn, &e);
+      if (epi >= 0 && e != epi) return fail(SM_ERR_ARG, "mixed epilogues in one launch");
+      epi = e;
+      p.tile_begin = begin;
+      begin += static_cast<int>(problem_tiles(p));
+      flops += problem_flops(p, comp);
+      L.p[L.n_problems++] = p;
+    }
+    L.total_tiles = begin;
+    L.sched = set.sched;
+    SM_TIMED(tm, SM_TCLASS_GEMM, flops, st, dispatch_gemm(set.bn, comp, kind == kPX, epi, L, set.grid, st));
+    ++*launches;
+  }
+  return SM_OK;
+}
+
+// The five-stage S8 polynomial of every group: inputs are the stage-1 planes
+// xh/xl (normalised, oriented, zero-padded); outputs FP32 Q [B, rp, cp] in
+// each group's q.  Mirrors _s8_fp32 (sandmuon/optimizer.py:79-91); every GEMM
+// of a stage covers all groups in one launch.
+static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cudaStream_t st, Timer* tm,
+                  int64_t* launches) {
+  for (int stage = 0; stage < 5; ++stage) {
+    SM_TRY(launch_s8_kind(groups, plan, kGram, stage, st, tm, launches));
+    SM_TRY(launch_s8_kind(groups, plan, kGramSq, stage, st, tm, launches));
+    if (stage == 0) {
+      // s = max(1.35 |G2|_F^(1/4), 1e-30); P = a I + b G/s/s + c G2/s/s/s/s (hi/lo in place of G)
+      for (const Group& g : groups) {
+        const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * 4;
+        const int64_t per = static_cast<int64_t>(g.rp) * g.rp;
+        const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 2, 256), 512));
+        SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
+                   k_reduce_s8scale<<<g.batch, 256, 0, st>>>(g.partials, per_mat, kS8Margin, g.s, g.s_inv);
+                   SM_LAUNCHED();
+                   k_poly_stage1<<<dim3(blocks, g.batch), 256, 0, st>>>(
+                       g.gh, g.gl, g.g2, g.s, g.rp, (float)kS8Coeff[0][0], (float)kS8Coeff[0][1],
+                       (float)kS8Coeff[0][2]);
+                   SM_LAUNCHED();
+                   return SM_OK;
+                 }()));
+        *launches += 2;
+      }
+    }
+    SM_TRY(launch_s8_kind(groups, plan, kPX, stage, st, tm, launches));
   }
   return SM_OK;
 }
@@ -595,6 +731,7 @@ struct SmPlan {
   // per-stat outputs
   std::vector<float*> s_inv, s_z, s_zeta, s_scal;
   std::vector<uint8_t> group_has_trans, group_has_plain;
+  S8Launches s8;
   Timer timer;
   int64_t launches_last = 0;
 };
@@ -665,8 +802,13 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     s_scal[s] = cv.take<float>(4);
   }
   for (auto& g : groups) carve_group(cv, g);
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  S8Launches s8;
+  build_s8_launches(groups, di->sms, &cv, &s8);
   *bytes = round_up(static_cast<int64_t>(cv.off), 256);
   if (plan != nullptr) {
+    plan->s8 = s8;
     plan->mats.assign(spec->matrices, spec->matrices + nm);
     plan->stats.assign(spec->stats, spec->stats + ns);
     plan->groups = groups;
@@ -941,6 +1083,17 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
       if (rc != SM_OK) break;
       rc = encode_group_maps(g);
     }
+    for (int kind = 0; kind < 3 && rc == SM_OK; ++kind) {
+      for (const LaunchSet& set : p->s8.sets[kind]) {
+        if (set.sched == nullptr || set.h_sched.empty()) continue;
+        e = cudaMemcpyAsync(set.sched, set.h_sched.data(), set.h_sched.size() * sizeof(int), cudaMemcpyHostToDevice,
+                            static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) {
+          rc = fail(SM_ERR_CUDA, std::string("schedule upload: ") + cudaGetErrorString(e));
+          break;
+        }
+      }
+    }
     p->h_table.resize(p->table_bytes);
   }
   if (rc != SM_OK) {
@@ -1020,12 +1173,12 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
              return SM_OK;
            }()));
   ++launches;
-  for (size_t gi = 0; gi < p->groups.size(); ++gi) {
-    const Group& g = p->groups[gi];
-    SM_TRY(run_front(g, p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
-    SM_TRY(run_s8(g, st, tm, &launches));
-    SM_TRY(run_back(g, p->d_mats, p->group_has_trans[gi] != 0, p->group_has_plain[gi] != 0, st, tm, &launches));
-  }
+  for (size_t gi = 0; gi < p->groups.size(); ++gi)
+    SM_TRY(run_front(p->groups[gi], p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
+  SM_TRY(run_s8(p->groups, p->s8, st, tm, &launches));
+  for (size_t gi = 0; gi < p->groups.size(); ++gi)
+    SM_TRY(run_back(p->groups[gi], p->d_mats, p->group_has_trans[gi] != 0, p->group_has_plain[gi] != 0, st, tm,
+                    &launches));
   p->launches_last = launches;
   return SM_OK;
 }
@@ -1127,7 +1280,10 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   SM_CUDA(cudaMemcpyAsync(d_mats, hm.data(), sizeof(MatDev) * batch, cudaMemcpyHostToDevice, st));
   int64_t launches = 0;
   SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, st, nullptr, &launches));
-  SM_TRY(run_s8(g, st, nullptr, &launches));
+  std::vector<Group> groups(1, g);
+  S8Launches s8;
+  build_s8_launches(groups, di->sms, nullptr, &s8);  // round-robin tiles: no schedule tables
+  SM_TRY(run_s8(groups, s8, st, nullptr, &launches));
   SM_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * per, st));
   {
     dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), batch);
@@ -1185,6 +1341,9 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   if (batch <= 0 || m <= 0 || n <= 0 || k <= 0) return fail(SM_ERR_ARG, "empty GEMM");
   if (m % 128 != 0 || n % 128 != 0 || k % 64 != 0) return fail(SM_ERR_ARG, "GEMM needs M%128, N%128, K%64 == 0");
   if (a_hi == nullptr || b_hi == nullptr || out0 == nullptr) return fail(SM_ERR_ARG, "null operand");
+  const int sym = (epilogue & SM_EPI_SYMMETRIC) ? 1 : 0;
+  epilogue &= ~SM_EPI_SYMMETRIC;
+  if (sym && (m != n || !b_kmajor)) return fail(SM_ERR_ARG, "symmetric output needs M == N and K-major B");
   const bool comp = a_lo != nullptr;
   if (comp && b_lo == nullptr) return fail(SM_ERR_ARG, "compensated mode needs both lo planes");
   if (epilogue == SM_EPI_HILO && out1 == nullptr) return fail(SM_ERR_ARG, "hi/lo epilogue needs out1");
@@ -1195,31 +1354,38 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   if (epilogue == SM_EPI_F32_NORM && partials == nullptr) return fail(SM_ERR_ARG, "norm epilogue needs partials");
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
-  const int bn = pick_bn(n);
+  const int bn = sym ? 128 : pick_bn(n);
   CUtensorMap ah, al, bh, bl;
-  SM_TRY(make_map(&ah, a_hi, k, m, batch, kGemmBM));
+  SM_TRY(make_map(&ah, a_hi, k, m, batch, kBK, kGemmBM));
   al = ah;
-  if (comp) SM_TRY(make_map(&al, a_lo, k, m, batch, kGemmBM));
+  if (comp) SM_TRY(make_map(&al, a_lo, k, m, batch, kBK, kGemmBM));
   if (b_kmajor) {
-    SM_TRY(make_map(&bh, b_hi, k, n, batch, bn));
+    SM_TRY(make_map(&bh, b_hi, k, n, batch, kBK, bn));
     bl = bh;
-    if (comp) SM_TRY(make_map(&bl, b_lo, k, n, batch, bn));
+    if (comp) SM_TRY(make_map(&bl, b_lo, k, n, batch, kBK, bn));
   } else {
-    SM_TRY(make_map(&bh, b_hi, n, k, batch, 64));
+    SM_TRY(make_map(&bh, b_hi, n, k, batch, kChunk, kBK));
     bl = bh;
-    if (comp) SM_TRY(make_map(&bl, b_lo, n, k, batch, 64));
+    if (comp) SM_TRY(make_map(&bl, b_lo, n, k, batch, kChunk, kBK));
   }
-  GemmArgs a = gemm_args(m, n, k, batch, bn);
-  a.out0 = out0;
-  a.out1 = out1;
-  a.alpha = alpha;
-  a.aux = static_cast<const __nv_bfloat16*>(aux);
-  a.aux_lo = static_cast<const __nv_bfloat16*>(aux_lo);
-  a.pa = pa;
-  a.pb = pb;
-  a.pc = pc;
-  a.partials = partials;
-  return dispatch_gemm(bn, comp, !b_kmajor, epilogue, ah, al, bh, bl, a, static_cast<cudaStream_t>(stream));
+  GemmLaunch L;
+  memset(&L, 0, sizeof(L));
+  GemmProblem& p = L.p[0];
+  p = gemm_problem(ah, al, bh, bl, m, n, k, batch, bn, sym);
+  p.out0 = out0;
+  p.out1 = out1;
+  p.alpha = alpha;
+  p.aux = static_cast<const __nv_bfloat16*>(aux);
+  p.aux_lo = static_cast<const __nv_bfloat16*>(aux_lo);
+  p.pa = pa;
+  p.pb = pb;
+  p.pc = pc;
+  p.partials = partials;
+  L.n_problems = 1;
+  L.total_tiles = static_cast<int>(problem_tiles(p));
+  L.sched = nullptr;
+  const int grid = std::min(L.total_tiles, di->sms);
+  return dispatch_gemm(bn, comp, !b_kmajor, epilogue, L, grid, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

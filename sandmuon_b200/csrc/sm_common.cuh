@@ -118,20 +118,38 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
 
 // ---------------------------------------------------------------- tcgen05
 
-// Shared-memory matrix descriptor for tcgen05.mma, 128-byte swizzle.
+// Shared-memory matrix descriptor for tcgen05.mma.
 //   bits  0-13 start address >> 4, 16-29 leading byte offset >> 4,
 //   32-45 stride byte offset >> 4, 46-47 version (1 on sm_100),
-//   61-63 layout (2 = SWIZZLE_128B).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+//   61-63 layout (2 = SWIZZLE_128B, 4 = SWIZZLE_64B).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
+
+// Geometry of a BF16 operand tile whose K extent per pipeline stage is BK
+// (64 -> 128-byte rows, SWIZZLE_128B; 32 -> 64-byte rows, SWIZZLE_64B).
+//   K-major (rows of BK elements): 8-row swizzle atoms SBO = 8 * row bytes
+//     apart; one K=16 MMA step advances the start address by 32 bytes.
+//   MN-major (rows of K): the tile is stored as chunks of (row bytes / 2)
+//     MN-elements x BK K-rows; chunks LBO = row bytes * BK apart, 8-row
+//     groups SBO = 8 * row bytes apart; one K=16 step advances 16 rows.
+template <int BK>
+struct Swz {
+  static_assert(BK == 64 || BK == 32, "BK must be 32 or 64");
+  static constexpr uint32_t kRowBytes = BK * 2;
+  static constexpr uint32_t kLayout = BK == 64 ? 2u : 4u;
+  static constexpr uint32_t kSbo = 8 * kRowBytes;
+  static constexpr int kChunkElems = kRowBytes / 2;   // MN elements per MN-major chunk
+  static constexpr uint32_t kChunkBytes = kRowBytes * BK;
+  static constexpr uint32_t kMnStepBytes = 16 * kRowBytes;
+};
 
 // Instruction descriptor, kind::f16 with BF16 A/B and FP32 accumulator.
 //   bits 4-5 D format (1 = F32), 7-9 A format (1 = BF16), 10-12 B format,

@@ -147,3 +147,40 @@ def test_gemm_is_deterministic():
         engine.gemm_bf16(a, a, out0=out)
         outs.append(out)
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("epi", ["f32", "hilo", "norm"])
+def test_symmetric_mode_matches_full_product(epi):
+    """Upper-triangular tiles + mirrored stores reproduce the full X X^T."""
+    x = rnd(3, 384, 512, seed=16)
+    xh, xl = split(x)
+    want = torch.bmm(x.double(), x.double().transpose(1, 2))
+    sym = _lib.SM_EPI_SYMMETRIC
+    if epi == "f32":
+        out = torch.full((3, 384, 384), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32 | sym, out0=out)
+        assert rel(out, want) < 2e-5
+    elif epi == "hilo":
+        hi = torch.full((3, 384, 384), float("nan"), device=DEV, dtype=torch.bfloat16)
+        lo = torch.full_like(hi, float("nan"))
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_HILO | sym, out0=hi, out1=lo)
+        assert rel(hi.float() + lo.float(), want) < 2e-5
+    else:
+        out = torch.empty(3, 384, 384, device=DEV)
+        partials = torch.full((3, 3 * 3 * 4), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out, partials=partials)
+        torch.testing.assert_close(partials.double().sum(1), want.square().sum((1, 2)), rtol=1e-5, atol=0)
+
+
+def test_symmetric_poly_epilogue():
+    g = rnd(2, 256, 256, seed=17, scale=0.05)
+    g = (g + g.transpose(1, 2)) / 2
+    gh, gl = split(g)
+    ph = torch.full_like(gh, float("nan"))
+    pl = torch.full_like(gh, float("nan"))
+    a, b, c = 3.28, -2.41, 0.486
+    engine.gemm_bf16(gh, gh, a_lo=gl, b_lo=gl, epilogue=_lib.SM_EPI_POLY_HILO | _lib.SM_EPI_SYMMETRIC, out0=ph,
+                     out1=pl, aux=gh, aux_lo=gl, poly=(a, b, c))
+    gd = (gh.double() + gl.double())
+    want = a * torch.eye(256, device=DEV, dtype=torch.float64) + b * gd + c * torch.bmm(gd, gd.transpose(1, 2))
+    assert rel(ph.float() + pl.float(), want) < 2e-5
