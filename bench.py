@@ -353,6 +353,7 @@ def main():
             "s8_gemm_tflops": round(achieved, 1),
             "s8_gemm_ms_per_step": round(gemm_ms, 4),
             "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),
+            "phase_ms_per_step": {k: round(v / args.steps, 4) for k, v in timing["ms"].items()},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "peak_kind": f"{peak_kind} burst bf16 (sustained {peak_sustained})",

@@ -244,7 +244,8 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
  *   out0/out1: outputs [batch, M, N] (out1 = lo plane for SM_EPI_HILO).
  *   alpha: device [batch] FP32 scales or NULL (1).  aux (and aux_lo for the
  *   hi/lo polynomial): BF16 [batch, M, N] for SM_EPI_POLY / SM_EPI_POLY_HILO.
- *   partials: device FP32 [batch, (M/128)*(N/BN)*4] for SM_EPI_F32_NORM. */
+ *   partials: device FP32 [batch, (M/128)*(N/BN)*8] for SM_EPI_F32_NORM
+ *   (BN = 256 when N % 256 == 0 and the output is not symmetric, else 128). */
 int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo,
                  int b_kmajor, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
                  void* out0, void* out1, const float* alpha, const void* aux, const void* aux_lo,

@@ -374,6 +374,8 @@ struct Group {
   float *q = nullptr, *g2 = nullptr, *partials = nullptr;
   float *inv_norm = nullptr, *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
   float2 *rs_white = nullptr, *rs_map = nullptr;
+  int* tmask = nullptr;  // [B] 1 = transposed matrix: its FP32 Q is stored in param layout
+  std::vector<int> host_tmask;
   CUtensorMap xh_A, xl_A, xh_Bk, xl_Bk, xh_Bmn, xl_Bmn;
   CUtensorMap gh_A, gl_A, gh_Bk, gl_Bk;
   CUtensorMap xa_A, xa_Bk, xa_Bmn, xb_A, xb_Bk, xb_Bmn;
@@ -407,7 +409,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.g2 = cv.take<float>(gs);
   g.ph = reinterpret_cast<__nv_bfloat16*>(g.g2);  // P hi | P lo in the g2 bytes
   g.pl = g.ph ? g.ph + gs : nullptr;
-  const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * 4;
+  const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * kEpiWarps;
   g.partials = cv.take<float>(static_cast<size_t>(g.batch) * per_mat);
   g.inv_norm = cv.take<float>(g.batch);
   g.s = cv.take<float>(g.batch);
@@ -415,6 +417,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.gamma = cv.take<float>(g.batch);
   g.rs_white = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
   g.rs_map = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
+  g.tmask = cv.take<int>(g.batch);
 }
 
 static int encode_group_maps(Group& g) {
@@ -568,6 +571,7 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
     const bool next_comp = stage + 1 < kCompensatedStages;
     if (last) {
       p.out0 = g.q;  // over the xa|xb bytes; stage 5 reads xh
+      p.tmask = g.tmask;  // transposed matrices: Q stored in param layout
       *epi = kEpiF32;
     } else {
       p.out0 = in_a ? g.xh : g.xa;
@@ -618,9 +622,9 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
     if (stage == 0) {
       // s = max(1.35 |G2|_F^(1/4), 1e-30); P = a I + b G/s/s + c G2/s/s/s/s (hi/lo in place of G)
       for (const Group& g : groups) {
-        const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * 4;
+        const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * kEpiWarps;
         const int64_t per = static_cast<int64_t>(g.rp) * g.rp;
-        const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 2, 256), 512));
+        const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 4, 1024), 512));
         SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
                    k_reduce_s8scale<<<g.batch, 256, 0, st>>>(g.partials, per_mat, kS8Margin, g.s, g.s_inv);
                    SM_LAUNCHED();
@@ -675,36 +679,36 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
 }
 
 // Mapback + graft + update back end for one group (N7 passes 1 and 2).
-static int run_back(const Group& g, const MatDev* d_mats, bool has_trans, bool has_plain, cudaStream_t st,
-                    Timer* tm, int64_t* launches) {
+static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cudaStream_t st, Timer* tm,
+                    int64_t* launches) {
   const int B = g.batch;
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-             if (has_plain) {
-               dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
-               if (g.rank1) k_mapback_rowstats_rows<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-               else k_mapback_rowstats_rows<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-               SM_LAUNCHED();
-             }
-             if (has_trans) {
-               dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 256)), B);
-               if (g.rank1) k_mapback_rowstats_cols<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-               else k_mapback_rowstats_cols<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-               SM_LAUNCHED();
-             }
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
+             if (g.rank1) k_mapback_rowstats<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+             else k_mapback_rowstats<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
+             SM_LAUNCHED();
              k_reduce_graft<<<B, 256, 0, st>>>(mats, g.rs_map, ld, g.gamma);
              SM_LAUNCHED();
              return SM_OK;
            }()));
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), B);
-             if (g.rank1) k_mapback_apply<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
-             else k_mapback_apply<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+             // ~4 iterations per thread over the largest matrix of the group
+             const int64_t per = static_cast<int64_t>(g.r) * g.c / (vec4 ? 4 : 1);
+             const unsigned gx = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(per, 1024), 8 * sms)));
+             dim3 grid(gx, B);
+             if (g.rank1) {
+               if (vec4) k_mapback_apply<true, true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+               else k_mapback_apply<true, false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+             } else {
+               if (vec4) k_mapback_apply<false, true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+               else k_mapback_apply<false, false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
+             }
              SM_LAUNCHED();
              return SM_OK;
            }()));
-  *launches += (has_plain ? 1 : 0) + (has_trans ? 1 : 0) + 2;
+  *launches += 3;
   return SM_OK;
 }
 
@@ -730,7 +734,6 @@ struct SmPlan {
   std::vector<uint8_t> h_table;
   // per-stat outputs
   std::vector<float*> s_inv, s_z, s_zeta, s_scal;
-  std::vector<uint8_t> group_has_trans, group_has_plain;
   S8Launches s8;
   Timer timer;
   int64_t launches_last = 0;
@@ -823,12 +826,6 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     plan->s_z = s_z;
     plan->s_zeta = s_zeta;
     plan->s_scal = s_scal;
-    plan->group_has_trans.assign(groups.size(), 0);
-    plan->group_has_plain.assign(groups.size(), 0);
-    for (int i = 0; i < nm; ++i) {
-      const bool tr = spec->matrices[i].d_out > spec->matrices[i].d_in;
-      (tr ? plan->group_has_trans : plan->group_has_plain)[mg[i]] = 1;
-    }
   }
   return SM_OK;
 }
@@ -1083,6 +1080,16 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
       if (rc != SM_OK) break;
       rc = encode_group_maps(g);
     }
+    for (size_t gi = 0; gi < p->groups.size() && rc == SM_OK; ++gi) {
+      Group& g = p->groups[gi];
+      g.host_tmask.assign(g.batch, 0);
+      for (int i = 0; i < spec->n_matrices; ++i)
+        if (p->mat_group[i] == static_cast<int>(gi))
+          g.host_tmask[p->mat_slot[i]] = spec->matrices[i].d_out > spec->matrices[i].d_in ? 1 : 0;
+      e = cudaMemcpyAsync(g.tmask, g.host_tmask.data(), g.batch * sizeof(int), cudaMemcpyHostToDevice,
+                          static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("tmask upload: ") + cudaGetErrorString(e));
+    }
     for (int kind = 0; kind < 3 && rc == SM_OK; ++kind) {
       for (const LaunchSet& set : p->s8.sets[kind]) {
         if (set.sched == nullptr || set.h_sched.empty()) continue;
@@ -1140,7 +1147,8 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     d.lr = args->lrs[i];
     d.sqrt_rows = static_cast<float>(std::sqrt(static_cast<double>(m.d_out)));
     const bool aligned = (m.d_in % 4 == 0) && (reinterpret_cast<uintptr_t>(d.grad) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(d.mom) % 16 == 0);
+                         (reinterpret_cast<uintptr_t>(d.mom) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(d.weight) % 16 == 0);
     if (!aligned) vec4[p->mat_group[i]] = 0;
   }
   for (int s = 0; s < ns; ++s) {
@@ -1176,9 +1184,10 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
     SM_TRY(run_front(p->groups[gi], p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
   SM_TRY(run_s8(p->groups, p->s8, st, tm, &launches));
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
-    SM_TRY(run_back(p->groups[gi], p->d_mats, p->group_has_trans[gi] != 0, p->group_has_plain[gi] != 0, st, tm,
-                    &launches));
+    SM_TRY(run_back(p->groups[gi], p->d_mats, vec4[gi] != 0, di->sms, st, tm, &launches));
   p->launches_last = launches;
   return SM_OK;
 }
@@ -1278,6 +1287,8 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
     d.sqrt_rows = 1.0f;
   }
   SM_CUDA(cudaMemcpyAsync(d_mats, hm.data(), sizeof(MatDev) * batch, cudaMemcpyHostToDevice, st));
+  g.host_tmask.assign(batch, rows > cols ? 1 : 0);
+  SM_CUDA(cudaMemcpyAsync(g.tmask, g.host_tmask.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, st));
   int64_t launches = 0;
   SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, st, nullptr, &launches));
   std::vector<Group> groups(1, g);
@@ -1286,8 +1297,10 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   SM_TRY(run_s8(groups, s8, st, nullptr, &launches));
   SM_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * per, st));
   {
-    dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), batch);
-    k_mapback_apply<false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
+    const bool out_vec4 = vec4 && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(per, 1024), 8 * di->sms))), batch);
+    if (out_vec4) k_mapback_apply<false, true><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
+    else k_mapback_apply<false, false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
     SM_LAUNCHED();
   }
   return SM_OK;

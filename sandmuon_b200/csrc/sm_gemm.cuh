@@ -4,15 +4,16 @@
 // one launch: the dense products of the S8 polynomial (x x^T, gram gram, p x;
 // sandmuon/optimizer.py:79-91) for every shape group of an optimizer at once.
 //
-// Design (one persistent CTA per SM, 6 warps):
+// Design (one persistent CTA per SM, 10 warps):
 //   warp 0      TMA producer: streams A/B k-blocks of BK BF16 (BK = 64:
 //               128-byte rows, 128-byte swizzle; BK = 32: 64-byte rows,
 //               64-byte swizzle) into a STAGES-deep shared-memory ring.
 //   warp 1      MMA issuer: owns the TMEM allocation; one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered FP32
 //               accumulator in TMEM and releases ring slots with tcgen05.commit.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31 = tile rows), apply the fused epilogue, store.
+//   warps 2..9  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows; the two warps of a lane quarter take
+//               alternate 32-column chunks), apply the fused epilogue, store.
 // Compensated mode (stages 1-4 of S8) loads hi and lo BF16 planes of both
 // operands and issues three MMAs per k-step into the same accumulator:
 //   acc += A_hi*B_lo; acc += A_lo*B_hi; acc += A_hi*B_hi
@@ -29,7 +30,8 @@
 namespace smb {
 
 constexpr int kGemmBM = 128;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxProblems = 4;
 
 enum GemmEpi : int {
@@ -56,7 +58,9 @@ struct GemmProblem {
   const __nv_bfloat16* aux;     // [batch, m, n] BF16 gram (hi plane) for the poly epilogues
   const __nv_bfloat16* aux_lo;  // lo plane of the gram for the hi/lo poly epilogue
   float pa, pb, pc;     // poly coefficients: out = pa*I + pb*gram + pc*acc
-  float* partials;      // [batch, tiles_m*tiles_n*4] sum of squares (F32Norm)
+  float* partials;      // [batch, tiles_m*tiles_n*kEpiWarps] sum of squares (F32Norm)
+  const int* tmask;     // [batch] or null: 1 = store this matrix's FP32 result
+                        // transposed ([n, m], row stride m) -- F32 epilogue only
 };
 
 struct GemmLaunch {
@@ -78,7 +82,7 @@ struct GemmSmem {
   // Epilogue staging: per epilogue warp one 32 x 32 FP32 chunk padded to 33
   // floats per row, so row writes and column reads are both conflict-free.
   static constexpr int kStageWords = 32 * 33;
-  static constexpr int kStagingBytes = 4 * kStageWords * 4;
+  static constexpr int kStagingBytes = kEpiWarps * kStageWords * 4;
   // +1024 for manual alignment of the dynamic shared memory base.
   static constexpr int kTotal = STAGES * kStageBytes + kBarrierBytes + kStagingBytes + 1024;
   static constexpr uint32_t kTmemCols = 2 * BN;
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull(a), 1);
-      mbar_init(bar_tempty(a), 4);
+      mbar_init(bar_tempty(a), kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -292,7 +296,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;      // which alternate column chunks it takes
     int local = 0;
     for (TileIter it(L); it.valid(); it.next(), ++local) {
       const TileCoord tc = decode_tile(L, it.tile());
@@ -315,11 +320,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
+      for (int j = half; j < BN / 32; j += 2) {
         uint32_t r[32];
         tmem_ld_32x32(t_row + j * 32, r);
         tmem_wait_ld();
-        if (j == BN / 32 - 1) {
+        if (j + 2 >= BN / 32) {
           // Accumulator fully read into registers: hand it back to the MMA warp.
           tc_fence_before();
           __syncwarp();
@@ -373,15 +378,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         }
         __syncwarp();
         // Coalesced stores of the chunk (rows row0.., cols col0..) and, for an
-        // off-diagonal tile of a symmetric product, of its transpose (rows
-        // col0.., cols row0..), read from the staging tile by columns.
+        // off-diagonal tile of a symmetric product or a matrix whose FP32
+        // result is stored transposed, of its transpose (rows col0.., cols
+        // row0..), read from the staging tile by columns.
+        const bool tout = (EPI == kEpiF32) && P.tmask != nullptr && P.tmask[tc.b] != 0;
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
-          if (pass == 1 && !mirror) break;
+          if (pass == 0 && tout) continue;
+          if (pass == 1 && !mirror && !tout) break;
           const int orow0 = pass == 0 ? row0 : col0;
           const int ocol0 = pass == 0 ? col0 : row0;
           if (EPI == kEpiF32 || EPI == kEpiF32Norm) {
             float* out = static_cast<float*>(P.out0) + mat_off;
+            const size_t ld = tout ? P.m : P.n;
 #pragma unroll
             for (int it = 0; it < 8; ++it) {
               const int rr = 4 * it + (lane >> 3);
@@ -394,7 +403,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
                 o = make_float4(stg[c4 * 33 + rr], stg[(c4 + 1) * 33 + rr], stg[(c4 + 2) * 33 + rr],
                                 stg[(c4 + 3) * 33 + rr]);
               }
-              *reinterpret_cast<float4*>(out + static_cast<size_t>(orow0 + rr) * P.n + ocol0 + c4) = o;
+              *reinterpret_cast<float4*>(out + static_cast<size_t>(orow0 + rr) * ld + ocol0 + c4) = o;
             }
           } else {
             constexpr bool kTwo = (EPI == kEpiHiLo || EPI == kEpiPolyHiLo);
@@ -430,9 +439,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         // partial slots are cleared so the per-matrix sum stays exact.
         sumsq = warp_sum(sumsq);
         if (lane == 0) {
-          float* part = P.partials + static_cast<size_t>(tc.b) * P.tiles_m * P.tiles_n * 4;
-          part[tc.local * 4 + quarter] = mirror ? 2.0f * sumsq : sumsq;
-          if (mirror) part[(tc.ni * P.tiles_n + tc.mi) * 4 + quarter] = 0.0f;
+          const int slot = warp - 2;
+          float* part = P.partials + static_cast<size_t>(tc.b) * P.tiles_m * P.tiles_n * kEpiWarps;
+          part[tc.local * kEpiWarps + slot] = mirror ? 2.0f * sumsq : sumsq;
+          if (mirror) part[(tc.ni * P.tiles_n + tc.mi) * kEpiWarps + slot] = 0.0f;
         }
       }
     }

@@ -497,60 +497,90 @@ __global__ void __launch_bounds__(256)
 }
 
 // P = a I + b G / s / s + c G2 / s / s / s / s (sandmuon/optimizer.py:83-84),
-// emitted as hi/lo BF16 planes in place of the G hi/lo planes.  Sequential
-// divisions keep a zero matrix (s = 1e-30) at exactly P = a I.
+// emitted as hi/lo BF16 planes in place of the G hi/lo planes.  Four
+// consecutive elements (one row, rp % 4 == 0) per thread and iteration.
 __global__ void __launch_bounds__(256)
     k_poly_stage1(__nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ gl, const float* __restrict__ g2,
-                  const float* __restrict__ s, int64_t rp, float pa, float pb, float pc) {
+                  const float* __restrict__ s, int rp, float pa, float pb, float pc) {
   const int b = blockIdx.y;
-  const int64_t per = rp * rp;
-  const float sv = s[b];
-  const int64_t base = static_cast<int64_t>(b) * per;
-  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 2; e < per;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x * 2) {
-    const uint32_t wh = *reinterpret_cast<const uint32_t*>(gh + base + e);
-    const uint32_t wl = *reinterpret_cast<const uint32_t*>(gl + base + e);
-    const float2 w2 = *reinterpret_cast<const float2*>(g2 + base + e);
-    const float gv[2] = {bf16_lo_to_f(wh) + bf16_lo_to_f(wl), bf16_hi_to_f(wh) + bf16_hi_to_f(wl)};
-    const float g2v[2] = {w2.x, w2.y};
-    float hi[2], lo[2];
+  const int64_t per4 = static_cast<int64_t>(rp) * rp / 4;
+  // Multiplications by 1/s, one at a time: for a zero matrix (s = 1e-30, so
+  // 1/s = 1e30 while 1/s^2 would overflow) every partial product stays 0 and
+  // P = a I exactly; for a normalised input s is O(1).
+  const float is = 1.0f / s[b];
+  const int64_t base = static_cast<int64_t>(b) * rp * rp;
+  for (int64_t i4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i4 < per4;
+       i4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i4 * 4;
+    const int r = static_cast<int>(e / rp);
+    const int c = static_cast<int>(e - static_cast<int64_t>(r) * rp);
+    const uint2 wh = *reinterpret_cast<const uint2*>(gh + base + e);
+    const uint2 wl = *reinterpret_cast<const uint2*>(gl + base + e);
+    const float4 w2 = *reinterpret_cast<const float4*>(g2 + base + e);
+    const float gv[4] = {bf16_lo_to_f(wh.x) + bf16_lo_to_f(wl.x), bf16_hi_to_f(wh.x) + bf16_hi_to_f(wl.x),
+                         bf16_lo_to_f(wh.y) + bf16_lo_to_f(wl.y), bf16_hi_to_f(wh.y) + bf16_hi_to_f(wl.y)};
+    const float g2v[4] = {w2.x, w2.y, w2.z, w2.w};
+    float hi[4], lo[4];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int64_t idx = e + q;
-      const int64_t r = idx / rp, c = idx - r * rp;
-      const float t1 = (gv[q] / sv) / sv;
-      const float t2 = (((g2v[q] / sv) / sv) / sv) / sv;
-      const float p = (r == c ? pa : 0.0f) + pb * t1 + pc * t2;
+    for (int q = 0; q < 4; ++q) {
+      const float t1 = (gv[q] * is) * is;
+      const float t2 = (((g2v[q] * is) * is) * is) * is;
+      const float p = (r == c + q ? pa : 0.0f) + pb * t1 + pc * t2;
       split_hilo(p, hi[q], lo[q]);
     }
-    *reinterpret_cast<uint32_t*>(gh + base + e) = pack_bf16x2(hi[0], hi[1]);
-    *reinterpret_cast<uint32_t*>(gl + base + e) = pack_bf16x2(lo[0], lo[1]);
+    *reinterpret_cast<uint2*>(gh + base + e) = make_uint2(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]));
+    *reinterpret_cast<uint2*>(gl + base + e) = make_uint2(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]));
   }
 }
 
 // ============================================ N7 pass 1: mapback row stats
 // Mapback U = diag(inv_b) (Q + c (Q z) z^T) diag(inv_a) in param coordinates
-// (rank1_mapback, sandmuon/optimizer.py:48-60, both orientations).  Per param
-// row o:  t = sum_i z_i Q_oi, S1 = sum_i a_i^2 Q_oi^2, S2 = sum_i a_i^2 z_i Q_oi
+// (rank1_mapback, sandmuon/optimizer.py:48-60, both orientations: the last S8
+// GEMM stores Q of a transposed matrix already transposed, so Q is always in
+// the param layout [d_out, d_in] with row stride ldq = transposed ? rp : cp).
+// Per param row o (one warp, 16-byte loads):
+//   t = sum_i z_i Q_oi, S1 = sum_i a_i^2 Q_oi^2, S2 = sum_i a_i^2 z_i Q_oi
 //   |U_o|^2 = inv_b_o^2 (S1 + 2 c t S2 + c^2 t^2 sum_i a_i^2 z_i^2)
 // out[o] = {t, |U_o|^2}.
-// Non-transposed: Q is [d_out, cp] (rows contiguous): one warp per row.
+__device__ __forceinline__ int64_t q_ld(const MatDev& md, int64_t rp, int64_t cp) {
+  return md.transposed ? rp : cp;
+}
+
 template <bool RANK1>
 __global__ void __launch_bounds__(256)
-    k_mapback_rowstats_rows(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
-                            float2* __restrict__ out, int ld_out) {
+    k_mapback_rowstats(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+                       float2* __restrict__ out, int ld_out) {
   const int b = blockIdx.y;
   const MatDev md = mats[b];
-  if (md.transposed) return;
   const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (o >= md.d_out) return;
-  const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * cp;
+  const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * q_ld(md, rp, cp);
   float t = 0.f, s1 = 0.f, s2 = 0.f;
-  for (int i = lane; i < md.d_in; i += 32) {
+  const int n4 = md.d_in & ~3;
+  for (int i = lane * 4; i < n4; i += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(qr + i);
+    const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    const float aa[4] = {a.x, a.y, a.z, a.w};
+    float zz[4] = {0.f, 0.f, 0.f, 0.f};
+    if (RANK1) {
+      const float4 z = *reinterpret_cast<const float4*>(md.z_a + i);
+      zz[0] = z.x; zz[1] = z.y; zz[2] = z.z; zz[3] = z.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a2 = aa[e] * aa[e];
+      s1 += a2 * vv[e] * vv[e];
+      if (RANK1) {
+        t += zz[e] * vv[e];
+        s2 += a2 * zz[e] * vv[e];
+      }
+    }
+  }
+  for (int i = n4 + lane; i < md.d_in; i += 32) {
     const float v = qr[i];
-    const float a = md.inv_a[i];
-    const float a2 = a * a;
+    const float a2 = md.inv_a[i] * md.inv_a[i];
     s1 += a2 * v * v;
     if (RANK1) {
       const float z = md.z_a[i];
@@ -574,56 +604,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Transposed: Q is [d_in, cp] with param row o = oriented column o; one
-// thread per column walks the d_in rows (coalesced across threads).
-template <bool RANK1>
-__global__ void __launch_bounds__(256)
-    k_mapback_rowstats_cols(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
-                            float2* __restrict__ out, int ld_out) {
-  const int b = blockIdx.y;
-  const MatDev md = mats[b];
-  if (!md.transposed) return;
-  const int o = blockIdx.x * blockDim.x + threadIdx.x;
-  if (o >= md.d_out) return;
-  const float* qc = q + static_cast<int64_t>(b) * rp * cp + o;
-  float t = 0.f, s1 = 0.f, s2 = 0.f;
-  int i = 0;
-  for (; i + 3 < md.d_in; i += 4) {
-    float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = qc[static_cast<int64_t>(i + e) * cp];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float a = md.inv_a[i + e];
-      const float a2 = a * a;
-      s1 += a2 * v[e] * v[e];
-      if (RANK1) {
-        const float z = md.z_a[i + e];
-        t += z * v[e];
-        s2 += a2 * z * v[e];
-      }
-    }
-  }
-  for (; i < md.d_in; ++i) {
-    const float v = qc[static_cast<int64_t>(i) * cp];
-    const float a = md.inv_a[i];
-    const float a2 = a * a;
-    s1 += a2 * v * v;
-    if (RANK1) {
-      const float z = md.z_a[i];
-      t += z * v;
-      s2 += a2 * z * v;
-    }
-  }
-  const double ib = md.inv_b[o];
-  double row = s1;
-  if (RANK1) {
-    const double c = md.scal_a[0], k2 = md.scal_a[1];
-    row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
-  }
-  out[static_cast<int64_t>(b) * ld_out + o] = make_float2(t, static_cast<float>(ib * ib * row));
-}
-
 // gamma[b] = sqrt(d_out) / max(|U_b|_F, tiny)  (_graft_direction,
 // sandmuon/optimizer.py:63-66)
 __global__ void __launch_bounds__(256)
@@ -641,49 +621,48 @@ __global__ void __launch_bounds__(256)
 }
 
 // ======================================== N7 pass 2: mapback + update apply
-// W[o,i] -= lr * gamma * inv_b[o] * inv_a[i] * (Q^p[o,i] + c t[o] z[i])
-// (sandmuon/optimizer.py:303-315).  Tile 32 param rows x 64 param columns;
-// transposed matrices read Q through a shared-memory transpose.
-template <bool RANK1>
+// W[o,i] -= lr * gamma * inv_b[o] * inv_a[i] * (Q[o,i] + c t[o] z[i])
+// (sandmuon/optimizer.py:303-315).  Grid-stride over the matrix (blockIdx.y)
+// in 16-byte groups when d_in % 4 == 0, else element by element.
+template <bool RANK1, bool VEC4>
 __global__ void __launch_bounds__(256)
     k_mapback_apply(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
                     const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma) {
-  __shared__ float sh[64][33];
-  const int b = blockIdx.z;
+  const int b = blockIdx.y;
   const MatDev md = mats[b];
-  const int o0 = blockIdx.y * 32;
-  const int i0 = blockIdx.x * 64;
-  if (o0 >= md.d_out || i0 >= md.d_in) return;
   const float* qb = q + static_cast<int64_t>(b) * rp * cp;
+  const int64_t ldq = q_ld(md, rp, cp);
   const float step = md.lr * gamma[b];
   const float coef = RANK1 ? md.scal_a[0] : 0.0f;
-  const bool trans = md.transposed != 0;
-  if (trans) {
-    // oriented rows i0..i0+63, columns o0..o0+31 -> sh[il][ol]
-    for (int e = threadIdx.x; e < 64 * 32; e += 256) {
-      const int il = e >> 5, ol = e & 31;
-      const int i = i0 + il, o = o0 + ol;
-      sh[il][ol] = (i < md.d_in && o < md.d_out) ? qb[static_cast<int64_t>(i) * cp + o] : 0.0f;
+  const int per_row = VEC4 ? md.d_in / 4 : md.d_in;
+  const int64_t total = static_cast<int64_t>(md.d_out) * per_row;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int o = static_cast<int>(idx / per_row);
+    const int col = static_cast<int>(idx - static_cast<int64_t>(o) * per_row);
+    const float ib = md.inv_b[o];
+    const float ct = RANK1 ? coef * rs[static_cast<int64_t>(b) * ld_rs + o].x : 0.0f;
+    if (VEC4) {
+      const int i = col * 4;
+      const float4 v = *reinterpret_cast<const float4*>(qb + static_cast<int64_t>(o) * ldq + i);
+      const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
+      float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (RANK1) z = *reinterpret_cast<const float4*>(md.z_a + i);
+      float4* wp = reinterpret_cast<float4*>(md.weight + static_cast<int64_t>(o) * md.d_in + i);
+      float4 w = *wp;
+      w.x = w.x - step * (((v.x + ct * z.x) * ib) * a.x);
+      w.y = w.y - step * (((v.y + ct * z.y) * ib) * a.y);
+      w.z = w.z - step * (((v.z + ct * z.z) * ib) * a.z);
+      w.w = w.w - step * (((v.w + ct * z.w) * ib) * a.w);
+      *wp = w;
+    } else {
+      const int i = col;
+      float v = qb[static_cast<int64_t>(o) * ldq + i];
+      if (RANK1) v += ct * md.z_a[i];
+      const float u = (v * ib) * md.inv_a[i];
+      const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
+      md.weight[wi] = md.weight[wi] - step * u;
     }
-    __syncthreads();
-  }
-  const int tx = threadIdx.x & 63;  // column
-  const int ty = threadIdx.x >> 6;  // 0..3
-  const int i = i0 + tx;
-  if (i >= md.d_in) return;
-  const float a = md.inv_a[i];
-  const float z = RANK1 ? md.z_a[i] : 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int ol = ty + 4 * k;
-    const int o = o0 + ol;
-    if (o >= md.d_out) break;
-    const float qv = trans ? sh[tx][ol] : qb[static_cast<int64_t>(o) * cp + i];
-    float v = qv;
-    if (RANK1) v += coef * rs[static_cast<int64_t>(b) * ld_rs + o].x * z;
-    const float u = (v * md.inv_b[o]) * a;
-    const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
-    md.weight[wi] = md.weight[wi] - step * u;
   }
 }
 

@@ -88,7 +88,7 @@ def test_norm_partials_sum_to_frobenius_square():
     x = rnd(3, 256, 256, seed=10)
     xh, xl = split(x)
     out = torch.empty(3, 256, 256, device=DEV)
-    per_mat = (256 // 128) * (256 // 256) * 4
+    per_mat = (256 // 128) * (256 // 256) * 8  # 8 epilogue warps per tile
     partials = torch.empty(3, per_mat, device=DEV)
     engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32_NORM, out0=out, partials=partials)
     torch.testing.assert_close(partials.double().sum(1), out.double().square().sum((1, 2)), rtol=1e-5, atol=0)
@@ -167,7 +167,7 @@ def test_symmetric_mode_matches_full_product(epi):
         assert rel(hi.float() + lo.float(), want) < 2e-5
     else:
         out = torch.empty(3, 384, 384, device=DEV)
-        partials = torch.full((3, 3 * 3 * 4), float("nan"), device=DEV)
+        partials = torch.full((3, 3 * 3 * 8), float("nan"), device=DEV)
         engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out, partials=partials)
         torch.testing.assert_close(partials.double().sum(1), want.square().sum((1, 2)), rtol=1e-5, atol=0)
 
