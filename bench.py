@@ -158,14 +158,15 @@ def build(device, group, partition):
         for key in ("a_sum", "a_first_sum", "b_sum"):
             if key in entry:
                 order.append((n, key, entry[key]))
-    total = sum(a.size for _, _, a in order)
-    flat = torch.empty(total, dtype=torch.float32, device=device)
-    src_host = torch.empty(total, dtype=torch.float32).pin_memory()
-    off = 0
+    # the statistic sums live in the optimizer's flat statistic buffer (the
+    # layout its hooks use), so a refill is one copy of the whole buffer
     for n, key, arr in order:
-        src_host[off:off + arr.size].copy_(torch.from_numpy(arr))
-        opt.state[opt.named_matrices[n]][key] = flat[off:off + arr.size]
-        off += arr.size
+        opt.state[opt.named_matrices[n]][key] = opt._stat_slot(opt.named_matrices[n], key, arr.size, device)
+    flat, layout = opt._stat_flat[device]
+    src_host = torch.zeros(flat.numel(), dtype=torch.float32).pin_memory()
+    for n, key, arr in order:
+        off, size = layout[(id(opt.named_matrices[n]), key)]
+        src_host[off:off + size].copy_(torch.from_numpy(arr))
     src_dev = src_host.to(device)
     counts = [(opt.state[opt.named_matrices[n]], key.replace("_sum", "_count").replace("a_first_count", "a_count"))
               for n, key, _ in order]
@@ -230,6 +231,12 @@ def cpu_baseline_sample(seconds=10.0):
 def run_reference(args, rank):
     if rank != 0:
         return
+    # torch.distributed.run sets OMP_NUM_THREADS=1; the CPU baseline uses every core
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=os.cpu_count())
+    except Exception:
+        pass
     value, cores, reps = None, None, 0
     samples = []
     for _ in range(args.warmup):

@@ -120,6 +120,8 @@ int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int
 typedef struct {
     float* weight;        /* [d_out, d_in] updated in place                  */
     float* momentum;      /* [d_out, d_in] FP32 momentum_buffer              */
+    float* export_to;     /* NULL, or [d_out, d_in]: the updated weight is also
+                             written here (a rank's all-gather send slot)    */
     int32_t d_out;
     int32_t d_in;
     int32_t a_stat;       /* index into the A-statistic table (shared q/k/v)  */
@@ -158,6 +160,10 @@ typedef struct {
     const float* lrs;            /* [n_matrices] learning rate of each matrix      */
     const int64_t* counts;       /* [n_stats] rows accumulated into each statistic */
     const int32_t* ema_init;     /* [n_stats] 1 = first step: EMA <- value (copy)  */
+    const int64_t* device_counts; /* NULL, or a DEVICE array [n_stats] of row counts
+                                     that replaces `counts` in the arithmetic (the
+                                     all-reduced counts of a data-parallel group,
+                                     read without a host synchronisation)         */
 } SmStepArgs;
 
 /* Workspace bytes a plan needs (256-byte aligned pointer required). */
@@ -192,6 +198,19 @@ int sm_plan_timing_read(SmPlan* plan, double* ms_out, int64_t* launches_out,
 int sm_plan_launches_per_step(const SmPlan* plan, int64_t* out);
 
 int sm_plan_destroy(SmPlan* plan);
+
+/* ------------------------------------------------ multi-tensor copy */
+
+typedef struct {
+    void* dst;
+    const void* src;
+    int64_t bytes;        /* both pointers 16-byte aligned when bytes % 16 == 0 */
+} SmCopySpec;
+
+/* Copies every (src -> dst, bytes) of the list in one kernel launch (the
+ * scatter of all-gathered weights back into the parameters of a sharded
+ * step; no counterpart in the single-device reference). */
+int sm_copy_multi(const SmCopySpec* copies, int32_t count, void* stream);
 
 /* --------------------------------------------------------- S8 (batch) */
 

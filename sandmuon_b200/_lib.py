@@ -40,8 +40,12 @@ _c_float = ctypes.c_float
 
 
 class SmMatrixSpec(ctypes.Structure):
-    _fields_ = [("weight", _c_void_p), ("momentum", _c_void_p), ("d_out", _c_i32), ("d_in", _c_i32),
-                ("a_stat", _c_i32), ("b_stat", _c_i32)]
+    _fields_ = [("weight", _c_void_p), ("momentum", _c_void_p), ("export_to", _c_void_p), ("d_out", _c_i32),
+                ("d_in", _c_i32), ("a_stat", _c_i32), ("b_stat", _c_i32)]
+
+
+class SmCopySpec(ctypes.Structure):
+    _fields_ = [("dst", _c_void_p), ("src", _c_void_p), ("bytes", _c_i64)]
 
 
 class SmStatSpec(ctypes.Structure):
@@ -57,7 +61,8 @@ class SmPlanSpec(ctypes.Structure):
 
 class SmStepArgs(ctypes.Structure):
     _fields_ = [("grads", ctypes.POINTER(_c_void_p)), ("lrs", ctypes.POINTER(_c_float)),
-                ("counts", ctypes.POINTER(_c_i64)), ("ema_init", ctypes.POINTER(_c_i32))]
+                ("counts", ctypes.POINTER(_c_i64)), ("ema_init", ctypes.POINTER(_c_i32)),
+                ("device_counts", _c_void_p)]
 
 
 class SmAdamTensor(ctypes.Structure):
@@ -84,6 +89,7 @@ SIGNATURES = {
                                      ctypes.POINTER(ctypes.c_double)]),
     "sm_plan_launches_per_step": (_c_int, [_c_void_p, ctypes.POINTER(_c_i64)]),
     "sm_plan_destroy": (_c_int, [_c_void_p]),
+    "sm_copy_multi": (_c_int, [ctypes.POINTER(SmCopySpec), _c_i32, _c_void_p]),
     "sm_s8_workspace_bytes": (_c_size, [_c_i32, _c_i32, _c_i32]),
     "sm_s8_polar": (_c_int, [_c_void_p, _c_void_p, _c_i32, _c_i32, _c_i32, _c_void_p, _c_size, _c_void_p]),
     "sm_adamw_multi": (_c_int, [ctypes.POINTER(SmAdamTensor), _c_i32, _c_float, _c_float, _c_float, _c_float,

@@ -1135,6 +1135,7 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     d.grad = args->grads[i];
     d.mom = m.momentum;
     d.weight = m.weight;
+    d.export_to = m.export_to;
     d.inv_a = p->s_inv[m.a_stat];
     d.z_a = p->s_z[m.a_stat];
     d.zeta_a = p->s_zeta[m.a_stat];
@@ -1165,6 +1166,7 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     d.zeta = p->s_zeta[s];
     d.scal = p->s_scal[s];
     d.count = args->counts[s];
+    d.count_dev = args->device_counts != nullptr ? args->device_counts + s : nullptr;
     d.n = sp.n;
     d.kind = sp.kind;
     d.init = args->ema_init[s] ? 1 : 0;
@@ -1301,6 +1303,35 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
     dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(per, 1024), 8 * di->sms))), batch);
     if (out_vec4) k_mapback_apply<false, true><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
     else k_mapback_apply<false, false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
+    SM_LAUNCHED();
+  }
+  return SM_OK;
+}
+
+// ------------------------------------------------------- multi-tensor copy
+
+int sm_copy_multi(const SmCopySpec* copies, int32_t count, void* stream) {
+  if (count < 0 || (count > 0 && copies == nullptr)) return fail(SM_ERR_ARG, "bad copy list");
+  if (count == 0) return SM_OK;
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int start = 0; start < count; start += kCopyMax) {
+    CopyBatch b;
+    memset(&b, 0, sizeof(b));
+    b.count = std::min(kCopyMax, count - start);
+    for (int t = 0; t < b.count; ++t) {
+      const SmCopySpec& c = copies[start + t];
+      if (c.bytes < 0 || (c.bytes > 0 && (c.dst == nullptr || c.src == nullptr)))
+        return fail(SM_ERR_ARG, "bad copy " + std::to_string(start + t));
+      b.dst[t] = static_cast<uint8_t*>(c.dst);
+      b.src[t] = static_cast<const uint8_t*>(c.src);
+      b.bytes[t] = c.bytes;
+      b.chunk_start[t + 1] = b.chunk_start[t] + cdiv(c.bytes, kCopyChunk);
+    }
+    const int64_t chunks = b.chunk_start[b.count];
+    if (chunks == 0) continue;
+    k_copy_multi<<<static_cast<int>(std::min<int64_t>(chunks, 8 * di->sms)), 256, 0, st>>>(b);
     SM_LAUNCHED();
   }
   return SM_OK;

@@ -143,6 +143,7 @@ struct StatDev {
   float* z;       // out [n] (rank-one)
   float* zeta;    // out [n] = inv * z (rank-one)
   float* scal;    // out [4]: {coefficient, sum(zeta^2), sum(z^2), 0}
+  const int64_t* count_dev;  // device row count, or null: use `count`
   int64_t count;
   int32_t n;
   int32_t kind;
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(256) k_stats_finish(const StatDev* __restrict_
   __shared__ double sh[8];
   const StatDev d = stats[blockIdx.x];
   const int n = d.n;
-  const float count = static_cast<float>(d.count);
+  const float count = static_cast<float>(d.count_dev != nullptr ? *d.count_dev : d.count);
 
   if (d.kind == SM_STAT_B) {
     // b = sum / count ; b /= max(mean(b), tiny)
@@ -255,6 +256,7 @@ struct MatDev {
   const float* grad;    // [d_out, d_in]
   float* mom;           // [d_out, d_in]
   float* weight;        // [d_out, d_in]
+  float* export_to;     // [d_out, d_in] copy of the updated weight, or null
   const float* inv_a;   // [d_in]
   const float* z_a;     // [d_in] or null (diagonal A)
   const float* zeta_a;  // [d_in] inv_a * z_a or null
@@ -655,13 +657,49 @@ __global__ void __launch_bounds__(256)
       w.z = w.z - step * (((v.z + ct * z.z) * ib) * a.z);
       w.w = w.w - step * (((v.w + ct * z.w) * ib) * a.w);
       *wp = w;
+      if (md.export_to != nullptr)
+        *reinterpret_cast<float4*>(md.export_to + static_cast<int64_t>(o) * md.d_in + i) = w;
     } else {
       const int i = col;
       float v = qb[static_cast<int64_t>(o) * ldq + i];
       if (RANK1) v += ct * md.z_a[i];
       const float u = (v * ib) * md.inv_a[i];
       const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
-      md.weight[wi] = md.weight[wi] - step * u;
+      const float w = md.weight[wi] - step * u;
+      md.weight[wi] = w;
+      if (md.export_to != nullptr) md.export_to[wi] = w;
+    }
+  }
+}
+
+// ======================================================= multi-tensor copy
+constexpr int kCopyMax = 64;
+
+struct CopyBatch {
+  uint8_t* dst[kCopyMax];
+  const uint8_t* src[kCopyMax];
+  int64_t bytes[kCopyMax];
+  int64_t chunk_start[kCopyMax + 1];  // prefix sums of 64 KB chunks
+  int32_t count;
+};
+
+constexpr int64_t kCopyChunk = 65536;
+
+__global__ void __launch_bounds__(256) k_copy_multi(const CopyBatch batch) {
+  const int64_t total = batch.chunk_start[batch.count];
+  for (int64_t ch = blockIdx.x; ch < total; ch += gridDim.x) {
+    int t = 0;
+    while (batch.chunk_start[t + 1] <= ch) ++t;
+    const int64_t base = (ch - batch.chunk_start[t]) * kCopyChunk;
+    const int64_t end = min(base + kCopyChunk, batch.bytes[t]);
+    const uint8_t* s = batch.src[t];
+    uint8_t* d = batch.dst[t];
+    const bool vec = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d) | batch.bytes[t]) & 15) == 0;
+    if (vec) {
+      for (int64_t o = base + threadIdx.x * 16; o < end; o += blockDim.x * 16)
+        *reinterpret_cast<uint4*>(d + o) = *reinterpret_cast<const uint4*>(s + o);
+    } else {
+      for (int64_t o = base + threadIdx.x; o < end; o += blockDim.x) d[o] = s[o];
     }
   }
 }

@@ -3,8 +3,9 @@
 One process per GPU.  Every rank holds the whole model and runs the hooks on
 its own microbatches; at step():
   1. reduce_statistics: the accumulated statistic sums and row counts of all
-     selected matrices are summed over the group with one flat all-reduce, so
-     every rank finishes identical whiteners (as one large batch would);
+     selected matrices are summed over the group (one flat all-reduce plus a
+     small one for the counts, which stay on the device), so every rank
+     finishes identical whiteners (as one large batch would);
   2. each rank runs momentum -> whitening -> S8 -> mapback -> update only for
      the matrices it owns (partition "lpt": longest-processing-time greedy
      over S8 FLOPs; "layer": contiguous transformer layers per rank);
@@ -68,61 +69,65 @@ class MatrixSharding:
         return self._owner[id(parameter)]
 
     # ------------------------------------------------------ statistics
-    def reduce_statistics(self, matrix_items) -> None:
-        """Sums statistic vectors and row counts over the group."""
-        if self.world == 1 or not matrix_items:
-            return
-        opt = self.opt
-        seen, tensors, counters = set(), [], []
-        for parameter, source, _ in matrix_items:
-            if id(source) not in seen:
-                seen.add(id(source))
-                st = opt.state[source]
-                tensors.append(st["a_sum"])
-                if opt.rank_one_a:
-                    tensors.append(st["a_first_sum"])
-                counters.append((st, "a_count"))
-            st = opt.state[parameter]
-            tensors.append(st["b_sum"])
-            counters.append((st, "b_count"))
-        flat = torch.cat([t.reshape(-1) for t in tensors])
-        counts = torch.tensor([st[key] for st, key in counters], dtype=torch.float64, device=flat.device)
-        dist.all_reduce(flat, group=self.group)
-        dist.all_reduce(counts, group=self.group)
-        offset = 0
-        for t in tensors:
-            t.copy_(flat[offset:offset + t.numel()].view_as(t))
-            offset += t.numel()
-        for (st, key), value in zip(counters, counts.tolist()):
-            st[key] = int(round(value))
+    def reduce_statistics(self, tensors: list[torch.Tensor], counts: list[int]) -> torch.Tensor | None:
+        """Sums the statistic vectors (in place) and their row counts over the
+        group; returns the summed counts as an int64 tensor on the tensors'
+        device, read by the statistics kernel without a host synchronisation.
+        None for a single rank."""
+        if self.world == 1 or not tensors:
+            return None
+        total = torch.tensor(counts, dtype=torch.int64).to(tensors[0].device, non_blocking=True)
+        if len(tensors) == 1:
+            dist.all_reduce(tensors[0], group=self.group)  # the optimizer's flat statistic buffer
+        else:
+            flat = torch.cat([t.reshape(-1) for t in tensors])
+            dist.all_reduce(flat, group=self.group)
+            offset = 0
+            for t in tensors:
+                t.copy_(flat[offset:offset + t.numel()].view_as(t))
+                offset += t.numel()
+        dist.all_reduce(total, group=self.group)
+        return total
 
     # --------------------------------------------------------- weights
-    def exchange(self, matrix_items) -> None:
-        """All-gathers every matrix from its owner into all ranks."""
-        if self.world == 1 or not matrix_items:
-            return
-        params = [item[0] for item in matrix_items]
-        key = tuple(id(p) for p in params)
-        if self._gather is None or self._gather[0] != key:
+    def _layout(self):
+        """Static all-gather layout: each rank's owned matrices back to back in
+        its send slot of `shard` floats (every selected matrix, every step)."""
+        if self._gather is None:
+            params = list(self.opt.named_matrices.values())
             per_rank = [[] for _ in range(self.world)]
             for p in params:
                 per_rank[self.owner(p)].append(p)
             shard = max(sum(p.numel() for p in ps) for ps in per_rank)
             device = params[0].device
-            send = torch.empty(shard, dtype=torch.float32, device=device)
+            send = torch.zeros(shard, dtype=torch.float32, device=device)
             recv = torch.empty(shard * self.world, dtype=torch.float32, device=device)
-            self._gather = (key, per_rank, send, recv, shard)
-        _, per_rank, send, recv, shard = self._gather
-        offset = 0
-        for p in per_rank[self.rank]:
-            send[offset:offset + p.numel()].copy_(p.detach().reshape(-1))
-            offset += p.numel()
-        dist.all_gather_into_tensor(recv, send, group=self.group)
-        with torch.no_grad():
+            slots, unpack = {}, []
             for r, ps in enumerate(per_rank):
-                if r == self.rank:
-                    continue
-                offset = r * shard
+                offset = 0
                 for p in ps:
-                    p.copy_(recv[offset:offset + p.numel()].view_as(p))
+                    if r == self.rank:
+                        slots[id(p)] = send[offset:offset + p.numel()].view_as(p)
+                    else:
+                        unpack.append((p, recv[r * shard + offset:r * shard + offset + p.numel()]))
                     offset += p.numel()
+            self._gather = (send, recv, slots, unpack)
+        return self._gather
+
+    def send_slot(self, parameter) -> torch.Tensor | None:
+        """Where the step also writes an owned matrix's updated weight (its
+        all-gather send slot); None for a single rank."""
+        if self.world == 1:
+            return None
+        return self._layout()[2][id(parameter)]
+
+    def exchange(self, matrix_items) -> None:
+        """All-gathers every matrix from its owner into all ranks.  The owners'
+        send slots were filled by the update kernel itself; the received
+        weights are scattered back with one multi-tensor copy launch."""
+        if self.world == 1:
+            return
+        from .engine import copy_multi
+        send, recv, slots, unpack = self._layout()
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        copy_multi([(p.detach(), src) for p, src in unpack], recv.device)

@@ -173,14 +173,17 @@ class StepPlan:
 
     def __init__(self, device: torch.device, matrices: list[tuple], stats: list[tuple], *,
                  statistic_beta: float, momentum: float):
-        """matrices: (weight, momentum_buffer, a_stat_index, b_stat_index)
+        """matrices: (weight, momentum_buffer, a_stat_index, b_stat_index, export | None)
         stats: (kind, sum, first_sum | None, ema, mean_ema | None)."""
         _lib.ensure_device(device)
         self.device = device
         self._keep = []
         mat_arr = (_lib.SmMatrixSpec * len(matrices))()
-        for slot, (w, m, ia, ib) in zip(mat_arr, matrices):
+        for slot, (w, m, ia, ib, ex) in zip(mat_arr, matrices):
             slot.weight, slot.momentum = w.data_ptr(), m.data_ptr()
+            slot.export_to = 0 if ex is None else ex.data_ptr()
+            if ex is not None:
+                self._keep.append(ex)
             slot.d_out, slot.d_in = w.shape
             slot.a_stat, slot.b_stat = ia, ib
             self._keep += [w, m]
@@ -211,14 +214,21 @@ class StepPlan:
         self._counts = (ctypes.c_int64 * self.n_stats)()
         self._init = (ctypes.c_int32 * self.n_stats)()
 
-    def step(self, grads: list[torch.Tensor], lrs: list[float], counts: list[int], ema_init: list[bool]) -> None:
+    def step(self, grads: list[torch.Tensor], lrs: list[float], counts: list[int], ema_init: list[bool],
+             device_counts: torch.Tensor | None = None) -> None:
+        """device_counts: optional int64 CUDA tensor [n_stats] whose values replace
+        `counts` on the device (all-reduced counts, no host synchronisation)."""
         for i, g in enumerate(grads):
             self._grads[i] = g.data_ptr()
             self._lrs[i] = lrs[i]
         for i, (c, e) in enumerate(zip(counts, ema_init)):
             self._counts[i] = c
             self._init[i] = 1 if e else 0
-        args = _lib.SmStepArgs(self._grads, self._lrs, self._counts, self._init)
+        if device_counts is not None and (device_counts.dtype != torch.int64 or device_counts.numel() != self.n_stats
+                                          or device_counts.device != self.device):
+            raise ValueError("device_counts must be an int64 tensor [n_stats] on the plan's device")
+        args = _lib.SmStepArgs(self._grads, self._lrs, self._counts, self._init,
+                               0 if device_counts is None else device_counts.data_ptr())
         with torch.cuda.device(self.device):
             rc = _lib.load().sm_plan_step(self._handle, ctypes.byref(args), _stream(self.device))
         _lib.check(rc, "sm_plan_step")
@@ -249,6 +259,21 @@ class StepPlan:
             self.close()
         except Exception:
             pass
+
+
+def copy_multi(pairs: list[tuple[torch.Tensor, torch.Tensor]], device: torch.device) -> None:
+    """dst.copy_(src) for every (dst, src) pair of same-size contiguous CUDA
+    tensors, in one kernel launch per 64 pairs."""
+    if not pairs:
+        return
+    arr = (_lib.SmCopySpec * len(pairs))()
+    for slot, (dst, src) in zip(arr, pairs):
+        if dst.numel() * dst.element_size() != src.numel() * src.element_size():
+            raise ValueError("copy_multi: size mismatch")
+        slot.dst, slot.src, slot.bytes = dst.data_ptr(), src.data_ptr(), dst.numel() * dst.element_size()
+    with torch.cuda.device(device):
+        rc = _lib.load().sm_copy_multi(arr, len(pairs), _stream(device))
+    _lib.check(rc, "sm_copy_multi")
 
 
 def s8_flops_per_matrix(rows: int, cols: int) -> float:

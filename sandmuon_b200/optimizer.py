@@ -77,6 +77,7 @@ class DiagonalWeightedPE(Optimizer):
         super().__init__(groups, defaults)
 
         self._plans: dict[tuple, engine.StepPlan] = {}
+        self._stat_flat: dict = {}
         self._sharding = None
         if process_group is not None:
             from .distributed import MatrixSharding
@@ -100,10 +101,10 @@ class DiagonalWeightedPE(Optimizer):
             state = self.state[parameter]
             if capture_a:
                 if "a_sum" not in state:
-                    state["a_sum"] = torch.zeros(rows.shape[-1], device=rows.device, dtype=torch.float32)
+                    state["a_sum"] = self._stat_slot(parameter, "a_sum", rows.shape[-1], rows.device)
                     state["a_count"] = 0
                     if self.rank_one_a:
-                        state["a_first_sum"] = torch.zeros_like(state["a_sum"])
+                        state["a_first_sum"] = self._stat_slot(parameter, "a_first_sum", rows.shape[-1], rows.device)
                 engine.accumulate_column_stats(rows, state["a_sum"],
                                                state["a_first_sum"] if self.rank_one_a else None)
                 state["a_count"] += rows.shape[0]
@@ -111,13 +112,58 @@ class DiagonalWeightedPE(Optimizer):
             def cotangent_hook(gradient):
                 delta = gradient.detach().reshape(-1, gradient.shape[-1])
                 if "b_sum" not in state:
-                    state["b_sum"] = torch.zeros(delta.shape[-1], device=delta.device, dtype=torch.float32)
+                    state["b_sum"] = self._stat_slot(parameter, "b_sum", delta.shape[-1], delta.device)
                     state["b_count"] = 0
                 engine.accumulate_column_stats(delta, state["b_sum"])
                 state["b_count"] += delta.shape[0]
                 return gradient
             output.register_hook(cotangent_hook)
         return hook
+
+    # ------------------------------------------------- statistic storage
+
+    def _stat_slot(self, parameter, key, n, device):
+        """A zeroed statistic vector for state[parameter][key]: a view into one
+        flat per-device buffer holding every statistic sum of the optimizer, so
+        a data-parallel step all-reduces them in place with one collective.
+        Falls back to a fresh tensor for shapes the layout does not expect."""
+        flat = self._stat_flat.get(device)
+        if flat is None:
+            layout, offset = {}, 0
+            for p in self.named_matrices.values():
+                d_out, d_in = p.shape
+                if self.a_sources[id(p)] is p:
+                    for k in ("a_sum", "a_first_sum") if self.rank_one_a else ("a_sum",):
+                        layout[(id(p), k)] = (offset, d_in)
+                        offset += d_in
+                layout[(id(p), "b_sum")] = (offset, d_out)
+                offset += d_out
+            flat = (torch.zeros(offset, dtype=torch.float32, device=device), layout)
+            self._stat_flat[device] = flat
+        buf, layout = flat
+        where = layout.get((id(parameter), key))
+        if where is None or where[1] != n:
+            return torch.zeros(n, dtype=torch.float32, device=device)
+        view = buf[where[0]:where[0] + n]
+        view.zero_()
+        return view
+
+    def _flat_statistics(self, device, stat_specs):
+        """The flat buffer if every statistic sum of this step is a view of it
+        and every selected matrix takes part, else None."""
+        flat = self._stat_flat.get(device)
+        if flat is None:
+            return None
+        buf, layout = flat
+        lo, hi = buf.data_ptr(), buf.data_ptr() + buf.numel() * 4
+        n_sums = sum(1 + (fs is not None) for _, _, fs, _, _ in stat_specs)
+        if n_sums != len(layout):
+            return None
+        for _, s_, fs, _, _ in stat_specs:
+            for t in (s_, fs):
+                if t is not None and not (lo <= t.data_ptr() < hi):
+                    return None
+        return buf
 
     # -------------------------------------------------------------- step
 
@@ -163,8 +209,6 @@ class DiagonalWeightedPE(Optimizer):
             with torch.enable_grad():
                 loss = closure()
         matrix_items, auxiliary_items = self._collect()
-        if self._sharding is not None:
-            self._sharding.reduce_statistics(matrix_items)
         self._step_auxiliary(auxiliary_items)
         if matrix_items:
             self._step_matrices(matrix_items)
@@ -243,12 +287,14 @@ class DiagonalWeightedPE(Optimizer):
             st = self.state[parameter]
             if "momentum_buffer" not in st:
                 st["momentum_buffer"] = torch.zeros_like(parameter, dtype=torch.float32)
+            export = self._sharding.send_slot(parameter) if self._sharding is not None else None
             mats.append((parameter, st["momentum_buffer"], stat_index[("a", id(source))],
-                         stat_index[("b", id(parameter))]))
+                         stat_index[("b", id(parameter))], export))
             grads.append(parameter.grad)
             lrs.append(group["lr"])
         momentum = float(owned[0][2]["momentum"]) if owned else .8
-        key = (tuple((m[0].data_ptr(), m[1].data_ptr(), m[2], m[3]) for m in mats),
+        key = (tuple((m[0].data_ptr(), m[1].data_ptr(), m[2], m[3], 0 if m[4] is None else m[4].data_ptr())
+                     for m in mats),
                tuple((s[0],) + tuple(0 if t is None else t.data_ptr() for t in s[1:]) for s in stat_specs),
                momentum, self.statistic_beta)
         plan = self._plans.get(key)
@@ -259,7 +305,19 @@ class DiagonalWeightedPE(Optimizer):
                 self._plans.clear()
             plan = engine.StepPlan(device, mats, stat_specs, statistic_beta=self.statistic_beta, momentum=momentum)
             self._plans[key] = plan
-        plan.step(grads, lrs, counts, ema_init)
+        device_counts = None
+        if self._sharding is not None:
+            flat = self._flat_statistics(device, stat_specs)
+            if flat is not None:
+                sums = [flat]
+            else:
+                sums = []
+                for kind, s_, fs, _, _ in stat_specs:
+                    sums.append(s_)
+                    if fs is not None:
+                        sums.append(fs)
+            device_counts = self._sharding.reduce_statistics(sums, counts)
+        plan.step(grads, lrs, counts, ema_init, device_counts=device_counts)
         # host-side counters follow the reference (sums are zeroed on the device)
         for source in sources.values():
             self.state[source]["a_count"] = 0

@@ -1,0 +1,48 @@
+"""Worker for tests/test_gpu_multi.py: one rank of a sharded optimizer step.
+
+Launched by torch.distributed.run (one process per GPU).  Every rank builds the
+same mini GPT-named model, injects the same statistics and gradients, runs two
+sharded steps (statistic all-reduce, owned-matrix S8, weight all-gather) and
+saves its weights to <out_dir>/rank<r>.pt.
+"""
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def main(out_dir: str, partition: str):
+    from sandmuon_b200 import RankOneAWeightedPE
+    from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    rank = int(os.environ["RANK"])
+    local = int(os.environ["LOCAL_RANK"])
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        torch.manual_seed(5)
+        model = gpt_matrix_model(3, 256, 1024).to(device)
+        opt = RankOneAWeightedPE(model, lr=1e-2, process_group=dist.group.WORLD, partition=partition)
+        rng = np.random.default_rng(5)
+        for step in range(2):
+            synth_gpt_statistics(opt, rng, count=4096)
+            for p in model.parameters():
+                p.grad = torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)).to(device)
+            opt.step()
+        torch.cuda.synchronize()
+        torch.save({n: p.detach().cpu() for n, p in model.named_parameters()}, Path(out_dir) / f"rank{rank}.pt")
+        opt.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "lpt")

@@ -42,10 +42,10 @@ def test_binding_signatures_cover_the_header(built_library):
 
 def test_ctypes_structs_match_c_layout():
     from sandmuon_b200 import _lib
-    assert ctypes.sizeof(_lib.SmMatrixSpec) == 32
+    assert ctypes.sizeof(_lib.SmMatrixSpec) == 40
     assert ctypes.sizeof(_lib.SmStatSpec) == 40
     assert ctypes.sizeof(_lib.SmAdamTensor) == 48
-    assert ctypes.sizeof(_lib.SmStepArgs) == 32
+    assert ctypes.sizeof(_lib.SmStepArgs) == 40
 
 
 def test_engine_constants_match_package_constants():

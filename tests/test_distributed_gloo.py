@@ -77,7 +77,17 @@ def _worker(rank, world, port, partition, results):
             st = opt.state.setdefault(p, {})
             st.update(b_sum=torch.full((p.shape[0],), 2.0 * (rank + 1)), b_count=10 * (rank + 1))
             items.append((p, src, {}))
-        sharding.reduce_statistics(items)
+        seen, tensors, counters = set(), [], []
+        for p, src, _ in items:
+            if id(src) not in seen:
+                seen.add(id(src))
+                tensors += [opt.state[src]["a_sum"], opt.state[src]["a_first_sum"]]
+                counters.append((opt.state[src], "a_count"))
+            tensors.append(opt.state[p]["b_sum"])
+            counters.append((opt.state[p], "b_count"))
+        total = sharding.reduce_statistics(tensors, [st[k] for st, k in counters])
+        for (st, k), v in zip(counters, total.tolist()):
+            st[k] = v
         # test-only compute stub: each owner writes a value unique to (matrix, owner)
         with torch.no_grad():
             for i, (p, _, _) in enumerate(items):
@@ -85,7 +95,17 @@ def _worker(rank, world, port, partition, results):
                     p.fill_(100.0 * i + sharding.rank)
                 else:
                     p.fill_(-1.0)
-        sharding.exchange(items)
+        # the update kernel writes owned weights into their send slots; here the
+        # test packs them, gathers over gloo and scatters like exchange() does
+        send, recv, slots, unpack = sharding._layout()
+        for p, _, _ in items:
+            if sharding.owns(p):
+                assert sharding.send_slot(p).data_ptr() == slots[id(p)].data_ptr()
+                slots[id(p)].copy_(p.detach())
+        dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
+        with torch.no_grad():
+            for p, src in unpack:
+                p.copy_(src.view_as(p))
         out = {}
         for i, (p, src, _) in enumerate(items):
             out[i] = (float(p.min()), float(p.max()), sharding.owner(p),

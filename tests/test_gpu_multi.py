@@ -1,0 +1,53 @@
+"""Sharded optimizer step on 2 GPUs (NCCL): every rank ends with bitwise
+identical weights, equal to a single-GPU run within the parity tolerance.
+Needs at least two GPUs; skipped otherwise."""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def single_gpu_reference():
+    from sandmuon_b200 import RankOneAWeightedPE
+    from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    device = torch.device("cuda:0")
+    torch.manual_seed(5)
+    model = gpt_matrix_model(3, 256, 1024).to(device)
+    opt = RankOneAWeightedPE(model, lr=1e-2)
+    rng = np.random.default_rng(5)
+    for step in range(2):
+        stats = synth_gpt_statistics(opt, rng, count=4096)
+        # the sharded run all-reduces statistics over 2 ranks: sums and counts
+        # double, so the normalised statistics are the same as here
+        for p in model.parameters():
+            p.grad = torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)).to(device)
+        opt.step()
+    torch.cuda.synchronize()
+    out = {n: p.detach().cpu() for n, p in model.named_parameters()}
+    opt.close()
+    return out
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("partition", ["lpt", "layer"])
+def test_two_gpu_sharded_step_matches_single_gpu(tmp_path, partition):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531",
+           str(ROOT / "tests" / "multi_gpu_worker.py"), str(tmp_path), partition]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-4000:]
+    r0 = torch.load(tmp_path / "rank0.pt")
+    r1 = torch.load(tmp_path / "rank1.pt")
+    ref = single_gpu_reference()
+    for n in ref:
+        assert torch.equal(r0[n], r1[n]), n
+        d = (r0[n] - ref[n]).double().norm() / ref[n].double().norm()
+        assert d < 1e-5, (n, float(d))
