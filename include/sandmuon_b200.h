@@ -254,11 +254,14 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
                                  upper-triangular 128x128 tiles are computed and each
                                  off-diagonal tile also stores its transpose        */
 
+#define SM_GEMM_B_KMAJOR 1   /* layout flag: B is [batch, N, K] (C = A B^T), else [batch, K, N] */
+#define SM_GEMM_A_MNMAJOR 2  /* layout flag: A is stored [batch, K, M] (A^T); needs an MN-major B */
+
 /* Batched C[b] = A[b] * op(B[b]) on tcgen05 tensor cores.
- *   A: [batch, M, K] BF16 row-major (K contiguous); a_lo != NULL selects the
- *      compensated 3-product mode (a_hi*b_lo + a_lo*b_hi + a_hi*b_hi), which
- *      then also needs b_lo.
- *   B: b_kmajor = 1 -> [batch, N, K] (C = A B^T);  0 -> [batch, K, N] (C = A B).
+ *   A: [batch, M, K] BF16 row-major (K contiguous), or [batch, K, M] with
+ *      SM_GEMM_A_MNMAJOR; a_lo != NULL selects the compensated 3-product mode
+ *      (a_hi*b_lo + a_lo*b_hi + a_hi*b_hi), which then also needs b_lo.
+ *   B: SM_GEMM_B_KMAJOR -> [batch, N, K] (C = A B^T); otherwise [batch, K, N].
  *   M % 128 == 0, N % 128 == 0, K % 64 == 0.
  *   out0/out1: outputs [batch, M, N] (out1 = lo plane for SM_EPI_HILO).
  *   alpha: device [batch] FP32 scales or NULL (1).  aux (and aux_lo for the
@@ -266,7 +269,7 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
  *   partials: device FP32 [batch, (M/128)*(N/BN)*8] for SM_EPI_F32_NORM
  *   (BN = 256 when N % 256 == 0 and the output is not symmetric, else 128). */
 int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo,
-                 int b_kmajor, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
+                 int layout, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
                  void* out0, void* out1, const float* alpha, const void* aux, const void* aux_lo,
                  float pa, float pb, float pc, float* partials, void* stream);
 

@@ -122,16 +122,15 @@ static int get_encode(PFN_cuTensorMapEncodeTiled_v12000* out) {
 }
 
 // 3-D BF16 tensor [batch, outer, inner] (inner contiguous), box
-// {box_inner, box_outer, 1}; box_inner * 2 bytes = the swizzle width
-// (64 -> 128-byte swizzle, 32 -> 64-byte swizzle).  inner * 2 bytes must be a
-// multiple of 16.
+// {64, box_outer, 1} with the 128-byte swizzle (one box row = 128 bytes).
+// inner * 2 bytes must be a multiple of 16.
 static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t batch,
                     uint32_t box_inner, uint32_t box_outer) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   SM_TRY(get_encode(&enc));
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(SM_ERR_ARG, "TMA base not 16-byte aligned");
   if ((inner * 2) % 16 != 0) return fail(SM_ERR_ARG, "TMA row stride not a multiple of 16 bytes");
-  if (box_inner != 32 && box_inner != 64) return fail(SM_ERR_ARG, "TMA box inner extent must be 32 or 64");
+  if (box_inner != 64) return fail(SM_ERR_ARG, "TMA box inner extent must be 64 (128-byte swizzle)");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner * 2), static_cast<cuuint64_t>(inner * outer * 2)};
@@ -152,9 +151,6 @@ static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t out
 // many stages as fit next to the epilogue staging: BN=256 compensated 2 x 96 KB,
 // BN=128 compensated 3 x 64 KB, plain 4 x 48 KB or 6 x 32 KB.  The SMB_*
 // macros exist for tuning sweeps; the defaults are the shipped configuration.
-#ifndef SMB_BK
-#define SMB_BK 64
-#endif
 #ifndef SMB_COMP_STAGES
 #define SMB_COMP_STAGES 8
 #endif
@@ -167,22 +163,25 @@ static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t out
 #ifndef SMB_USE_SCHEDULE
 #define SMB_USE_SCHEDULE 1
 #endif
-constexpr int kBK = SMB_BK;
-// Operand boxes (inner extent = kBK): A tiles {BK, 128}; K-major B tiles
-// {BK, BN}; MN-major B chunks {row-bytes/2 N-elements, BK K-rows}.
-constexpr uint32_t kChunk = Swz<kBK>::kChunkElems;
+// Every operand tile uses the 128-byte swizzle and 64-deep k-blocks (measured:
+// 32-deep stages, with twice as many in the ring, are 10-30% slower, and an
+// MN-major A reads no faster than a K-major one).  The ring holds as many
+// stages as fit next to the epilogue staging.  The SMB_* macros exist for
+// tuning sweeps; the defaults are the shipped configuration.
+constexpr int kBkK = 64;   // every launch of the S8 path (K-major A)
+constexpr int kBkMN = 64;  // launches whose A and B are both MN-major (unit tests)
+constexpr uint32_t kChunk = Swz::kChunkElems;
 
-template <int BN, bool COMP, bool B_MN, int EPI>
+template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int EPI>
 static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
   // Configured depth, capped by what fits in 227 KB of shared memory.
-  constexpr int kStageBytes = GemmSmem<BN, kBK, COMP, 1>::kStageBytes;
-  constexpr int kFit =
-      (232448 - 1024 - 256 - GemmSmem<BN, kBK, COMP, 1>::kStagingBytes) / kStageBytes;
+  constexpr int kStageBytes = GemmSmem<BN, BK, COMP, 1>::kStageBytes;
+  constexpr int kFit = (232448 - 1024 - 256 - GemmSmem<BN, BK, COMP, 1>::kStagingBytes) / kStageBytes;
   constexpr int kWant = COMP ? SMB_COMP_STAGES : SMB_PLAIN_STAGES;
   constexpr int STAGES = kWant < kFit ? kWant : kFit;
-  using S = GemmSmem<BN, kBK, COMP, STAGES>;
+  using S = GemmSmem<BN, BK, COMP, STAGES>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
-  auto kern = k_gemm_bf16<BN, kBK, COMP, B_MN, STAGES, EPI>;
+  auto kern = k_gemm_bf16<BN, BK, COMP, A_MN, B_MN, STAGES, EPI>;
   static bool attr_done[64] = {};
   int dev = 0;
   SM_CUDA(cudaGetDevice(&dev));
@@ -197,49 +196,57 @@ static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
   return SM_OK;
 }
 
+// Operand layouts: 0 = A and B K-major; 1 = A K-major, B MN-major; 2 = both MN-major.
+enum GemmLayout : int { kLayoutKK = 0, kLayoutKM = 1, kLayoutMM = 2 };
+
 template <int BN>
-static int dispatch_gemm_bn(bool comp, bool b_mn, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
-  if (!comp) {
-    if (!b_mn) {
+static int dispatch_gemm_bn(bool comp, int layout, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
+  if (layout == kLayoutKK) {
+    if (comp) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, false, false, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, false, false, kEpiBF16>(L, grid, st);
-        case kEpiPoly: return launch_gemm_t<BN, false, false, kEpiPoly>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, false, kEpiBF16>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiHiLo>(L, grid, st);
+        case kEpiF32Norm: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32Norm>(L, grid, st);
+        case kEpiPolyHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiPolyHiLo>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, false, true, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, false, true, kEpiBF16>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, false, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, false, kEpiBF16>(L, grid, st);
+        case kEpiPoly: return launch_gemm_t<BN, kBkK, false, false, false, kEpiPoly>(L, grid, st);
         default: break;
       }
     }
-  } else {
-    if (!b_mn) {
+  } else if (layout == kLayoutKM) {
+    if (comp) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, true, false, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, true, false, kEpiBF16>(L, grid, st);
-        case kEpiHiLo: return launch_gemm_t<BN, true, false, kEpiHiLo>(L, grid, st);
-        case kEpiF32Norm: return launch_gemm_t<BN, true, false, kEpiF32Norm>(L, grid, st);
-        case kEpiPolyHiLo: return launch_gemm_t<BN, true, false, kEpiPolyHiLo>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, true, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, true, kEpiBF16>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, true, kEpiHiLo>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, true, true, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, true, true, kEpiBF16>(L, grid, st);
-        case kEpiHiLo: return launch_gemm_t<BN, true, true, kEpiHiLo>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, true, kEpiF32>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, true, kEpiBF16>(L, grid, st);
         default: break;
       }
+    }
+  } else if (layout == kLayoutMM) {
+    if (epi == kEpiF32) {
+      return comp ? launch_gemm_t<BN, kBkMN, true, true, true, kEpiF32>(L, grid, st)
+                  : launch_gemm_t<BN, kBkMN, false, true, true, kEpiF32>(L, grid, st);
     }
   }
   return fail(SM_ERR_ARG, "unsupported GEMM mode combination (compensated=" + std::to_string(comp) +
-                              ", b_mn_major=" + std::to_string(b_mn) + ", epilogue=" + std::to_string(epi) + ")");
+                              ", layout=" + std::to_string(layout) + ", epilogue=" + std::to_string(epi) + ")");
 }
 
-static int dispatch_gemm(int bn, bool comp, bool b_mn, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
-  if (bn == 256) return dispatch_gemm_bn<256>(comp, b_mn, epi, L, grid, st);
-  if (bn == 128) return dispatch_gemm_bn<128>(comp, b_mn, epi, L, grid, st);
+static int dispatch_gemm(int bn, bool comp, int layout, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
+  if (bn == 256) return dispatch_gemm_bn<256>(comp, layout, epi, L, grid, st);
+  if (bn == 128) return dispatch_gemm_bn<128>(comp, layout, epi, L, grid, st);
   return fail(SM_ERR_ARG, "BN must be 128 or 256");
 }
 
@@ -376,10 +383,12 @@ struct Group {
   float2 *rs_white = nullptr, *rs_map = nullptr;
   int* tmask = nullptr;  // [B] 1 = transposed matrix: its FP32 Q is stored in param layout
   std::vector<int> host_tmask;
-  CUtensorMap xh_A, xl_A, xh_Bk, xl_Bk, xh_Bmn, xl_Bmn;
-  CUtensorMap gh_A, gl_A, gh_Bk, gl_Bk;
-  CUtensorMap xa_A, xa_Bk, xa_Bmn, xb_A, xb_Bk, xb_Bmn;
-  CUtensorMap ph_A, pl_A;
+  // K-major boxes {64, 128}: the iterate as both operands of X X^T, and G / P
+  // (128-row tiles of A; G also as the 128-row B tiles of G G)
+  CUtensorMap xh_K, xl_K, xa_K, xb_K;
+  CUtensorMap gh_K, gl_K, ph_K, pl_K;
+  // MN-major boxes {64, 64}: the iterate as the B of P X
+  CUtensorMap xh_MN, xl_MN, xa_MN, xb_MN;
 };
 
 // Bump allocator over a caller workspace (or a null base to measure).
@@ -421,25 +430,18 @@ static void carve_group(Carver& cv, Group& g) {
 }
 
 static int encode_group_maps(Group& g) {
-  const uint32_t bk = kBK;
-  SM_TRY(make_map(&g.xh_A, g.xh, g.cp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.xl_A, g.xl, g.cp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.xh_Bk, g.xh, g.cp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.xl_Bk, g.xl, g.cp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.xh_Bmn, g.xh, g.cp, g.rp, g.batch, kChunk, bk));
-  SM_TRY(make_map(&g.xl_Bmn, g.xl, g.cp, g.rp, g.batch, kChunk, bk));
-  SM_TRY(make_map(&g.gh_A, g.gh, g.rp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.gl_A, g.gl, g.rp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.gh_Bk, g.gh, g.rp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.gl_Bk, g.gl, g.rp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.xa_A, g.xa, g.cp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.xa_Bk, g.xa, g.cp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.xa_Bmn, g.xa, g.cp, g.rp, g.batch, kChunk, bk));
-  SM_TRY(make_map(&g.xb_A, g.xb, g.cp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.xb_Bk, g.xb, g.cp, g.rp, g.batch, bk, g.bn_r));
-  SM_TRY(make_map(&g.xb_Bmn, g.xb, g.cp, g.rp, g.batch, kChunk, bk));
-  SM_TRY(make_map(&g.ph_A, g.ph, g.rp, g.rp, g.batch, bk, kGemmBM));
-  SM_TRY(make_map(&g.pl_A, g.pl, g.rp, g.rp, g.batch, bk, kGemmBM));
+  SM_TRY(make_map(&g.xh_K, g.xh, g.cp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.xl_K, g.xl, g.cp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.xa_K, g.xa, g.cp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.xb_K, g.xb, g.cp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.gh_K, g.gh, g.rp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.gl_K, g.gl, g.rp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.ph_K, g.ph, g.rp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.pl_K, g.pl, g.rp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.xh_MN, g.xh, g.cp, g.rp, g.batch, kChunk, kBkK));
+  SM_TRY(make_map(&g.xl_MN, g.xl, g.cp, g.rp, g.batch, kChunk, kBkK));
+  SM_TRY(make_map(&g.xa_MN, g.xa, g.cp, g.rp, g.batch, kChunk, kBkK));
+  SM_TRY(make_map(&g.xb_MN, g.xb, g.cp, g.rp, g.batch, kChunk, kBkK));
   return SM_OK;
 }
 
@@ -510,7 +512,7 @@ static void build_s8_launches(const std::vector<Group>& groups, int sms, Carver*
         const Group& g = groups[gi];
         const int64_t tm = g.rp / kGemmBM;
         const int64_t tiles = kind == kPX ? tm * (kind_n(g, kind) / set.bn) * g.batch : tm * (tm + 1) / 2 * g.batch;
-        probs.push_back({tiles, kind_k(g, kind) / kBK});
+        probs.push_back({tiles, kind_k(g, kind) / kBkK});
         total += tiles;
       }
       set.grid = static_cast<int>(std::min<int64_t>(total, sms));
@@ -527,20 +529,20 @@ static void build_s8_launches(const std::vector<Group>& groups, int sms, Carver*
 static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* epi) {
   const bool comp = stage < kCompensatedStages;
   const bool in_a = (stage % 2) == 1;  // stages 2 and 4 read xa|xb
-  const CUtensorMap& xA_h = in_a ? g.xa_A : g.xh_A;
-  const CUtensorMap& xA_l = in_a ? g.xb_A : g.xl_A;
-  const CUtensorMap& xBk_h = in_a ? g.xa_Bk : g.xh_Bk;
-  const CUtensorMap& xBk_l = in_a ? g.xb_Bk : g.xl_Bk;
-  const CUtensorMap& xBmn_h = in_a ? g.xa_Bmn : g.xh_Bmn;
-  const CUtensorMap& xBmn_l = in_a ? g.xb_Bmn : g.xl_Bmn;
+  const CUtensorMap& xK_h = in_a ? g.xa_K : g.xh_K;
+  const CUtensorMap& xK_l = in_a ? g.xb_K : g.xl_K;
+  const CUtensorMap& xMN_h = in_a ? g.xa_MN : g.xh_MN;
+  const CUtensorMap& xMN_l = in_a ? g.xb_MN : g.xl_MN;
   GemmProblem p;
   if (kind == kGram) {
-    p = gemm_problem(xA_h, comp ? xA_l : xA_h, xBk_h, comp ? xBk_l : xBk_h, g.rp, g.rp, g.cp, g.batch, bn, 1);
+    // X X^T: A = B = X, K-major, symmetric 128 x 128 tiles
+    p = gemm_problem(xK_h, comp ? xK_l : xK_h, xK_h, comp ? xK_l : xK_h, g.rp, g.rp, g.cp, g.batch, bn, 1);
     p.out0 = g.gh;
     p.out1 = g.gl;
     *epi = comp ? kEpiHiLo : kEpiBF16;
   } else if (kind == kGramSq) {
-    p = gemm_problem(g.gh_A, comp ? g.gl_A : g.gh_A, g.gh_Bk, comp ? g.gl_Bk : g.gh_Bk, g.rp, g.rp, g.rp, g.batch,
+    // G G with G symmetric: B = G read K-major as G^T
+    p = gemm_problem(g.gh_K, comp ? g.gl_K : g.gh_K, g.gh_K, comp ? g.gl_K : g.gh_K, g.rp, g.rp, g.rp, g.batch,
                      bn, 1);
     if (stage == 0) {
       p.out0 = g.g2;
@@ -562,11 +564,11 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
       }
     }
   } else {
-    // P lives in gh|gl (stage 1, written by k_poly_stage1), in the g2 bytes
-    // (stages 2-4) or in gl (stage 5).
-    const CUtensorMap& pA_h = stage == 0 ? g.gh_A : (comp ? g.ph_A : g.gl_A);
-    const CUtensorMap& pA_l = stage == 0 ? g.gl_A : (comp ? g.pl_A : g.gl_A);
-    p = gemm_problem(pA_h, pA_l, xBmn_h, comp ? xBmn_l : xBmn_h, g.rp, g.cp, g.rp, g.batch, bn);
+    // P X with X read MN-major; P lives in gh|gl (stage 1, written by
+    // k_poly_stage1), in the g2 bytes (stages 2-4) or in gl (stage 5).
+    const CUtensorMap& pA_h = stage == 0 ? g.gh_K : (comp ? g.ph_K : g.gl_K);
+    const CUtensorMap& pA_l = stage == 0 ? g.gl_K : (comp ? g.pl_K : g.gl_K);
+    p = gemm_problem(pA_h, pA_l, xMN_h, comp ? xMN_l : xMN_h, g.rp, g.cp, g.rp, g.batch, bn);
     const bool last = stage == 4;
     const bool next_comp = stage + 1 < kCompensatedStages;
     if (last) {
@@ -604,7 +606,8 @@ static int launch_s8_kind(const std::vector<Group>& groups, const S8Launches& pl
     }
     L.total_tiles = begin;
     L.sched = set.sched;
-    SM_TIMED(tm, SM_TCLASS_GEMM, flops, st, dispatch_gemm(set.bn, comp, kind == kPX, epi, L, set.grid, st));
+    const int layout = kind == kPX ? kLayoutKM : kLayoutKK;
+    SM_TIMED(tm, SM_TCLASS_GEMM, flops, st, dispatch_gemm(set.bn, comp, layout, epi, L, set.grid, st));
     ++*launches;
   }
   return SM_OK;
@@ -1378,13 +1381,16 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
 
 // ------------------------------------------------------------------- GEMM
 
-int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int b_kmajor, int32_t batch,
+int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int layout, int32_t batch,
                  int32_t m, int32_t n, int32_t k, int epilogue, void* out0, void* out1, const float* alpha,
                  const void* aux, const void* aux_lo, float pa, float pb, float pc, float* partials,
                  void* stream) {
   if (batch <= 0 || m <= 0 || n <= 0 || k <= 0) return fail(SM_ERR_ARG, "empty GEMM");
   if (m % 128 != 0 || n % 128 != 0 || k % 64 != 0) return fail(SM_ERR_ARG, "GEMM needs M%128, N%128, K%64 == 0");
   if (a_hi == nullptr || b_hi == nullptr || out0 == nullptr) return fail(SM_ERR_ARG, "null operand");
+  const bool b_kmajor = (layout & SM_GEMM_B_KMAJOR) != 0;
+  const bool a_mn = (layout & SM_GEMM_A_MNMAJOR) != 0;
+  if (a_mn && b_kmajor) return fail(SM_ERR_ARG, "an MN-major A needs an MN-major B");
   const int sym = (epilogue & SM_EPI_SYMMETRIC) ? 1 : 0;
   epilogue &= ~SM_EPI_SYMMETRIC;
   if (sym && (m != n || !b_kmajor)) return fail(SM_ERR_ARG, "symmetric output needs M == N and K-major B");
@@ -1394,23 +1400,26 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   if (epilogue == SM_EPI_POLY && aux == nullptr) return fail(SM_ERR_ARG, "poly epilogue needs aux");
   if (epilogue == SM_EPI_POLY_HILO && (aux == nullptr || aux_lo == nullptr || out1 == nullptr))
     return fail(SM_ERR_ARG, "hi/lo poly epilogue needs aux, aux_lo and out1");
-  if (epilogue == SM_EPI_HILO && out1 == nullptr) return fail(SM_ERR_ARG, "hi/lo epilogue needs out1");
   if (epilogue == SM_EPI_F32_NORM && partials == nullptr) return fail(SM_ERR_ARG, "norm epilogue needs partials");
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
   const int bn = sym ? 128 : pick_bn(n);
+  const int bk = a_mn ? kBkMN : kBkK;
   CUtensorMap ah, al, bh, bl;
-  SM_TRY(make_map(&ah, a_hi, k, m, batch, kBK, kGemmBM));
+  // A: K-major [batch, M, K]; MN-major [batch, K, M].  B: K-major [batch, N, K]; MN-major [batch, K, N].
+  if (!a_mn) SM_TRY(make_map(&ah, a_hi, k, m, batch, kChunk, kGemmBM));
+  else SM_TRY(make_map(&ah, a_hi, m, k, batch, kChunk, bk));
   al = ah;
-  if (comp) SM_TRY(make_map(&al, a_lo, k, m, batch, kBK, kGemmBM));
-  if (b_kmajor) {
-    SM_TRY(make_map(&bh, b_hi, k, n, batch, kBK, bn));
-    bl = bh;
-    if (comp) SM_TRY(make_map(&bl, b_lo, k, n, batch, kBK, bn));
-  } else {
-    SM_TRY(make_map(&bh, b_hi, n, k, batch, kChunk, kBK));
-    bl = bh;
-    if (comp) SM_TRY(make_map(&bl, b_lo, n, k, batch, kChunk, kBK));
+  if (comp) {
+    if (!a_mn) SM_TRY(make_map(&al, a_lo, k, m, batch, kChunk, kGemmBM));
+    else SM_TRY(make_map(&al, a_lo, m, k, batch, kChunk, bk));
+  }
+  if (b_kmajor) SM_TRY(make_map(&bh, b_hi, k, n, batch, kChunk, bn));
+  else SM_TRY(make_map(&bh, b_hi, n, k, batch, kChunk, bk));
+  bl = bh;
+  if (comp) {
+    if (b_kmajor) SM_TRY(make_map(&bl, b_lo, k, n, batch, kChunk, bn));
+    else SM_TRY(make_map(&bl, b_lo, n, k, batch, kChunk, bk));
   }
   GemmLaunch L;
   memset(&L, 0, sizeof(L));
@@ -1429,7 +1438,8 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   L.total_tiles = static_cast<int>(problem_tiles(p));
   L.sched = nullptr;
   const int grid = std::min(L.total_tiles, di->sms);
-  return dispatch_gemm(bn, comp, !b_kmajor, epilogue, L, grid, static_cast<cudaStream_t>(stream));
+  const int lay = a_mn ? kLayoutMM : (b_kmajor ? kLayoutKK : kLayoutKM);
+  return dispatch_gemm(bn, comp, lay, epilogue, L, grid, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -133,29 +133,26 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
-// Geometry of a BF16 operand tile whose K extent per pipeline stage is BK
-// (64 -> 128-byte rows, SWIZZLE_128B; 32 -> 64-byte rows, SWIZZLE_64B).
-//   K-major (rows of BK elements): 8-row swizzle atoms SBO = 8 * row bytes
-//     apart; one K=16 MMA step advances the start address by 32 bytes.
-//   MN-major (rows of K): the tile is stored as chunks of (row bytes / 2)
-//     MN-elements x BK K-rows; chunks LBO = row bytes * BK apart, 8-row
-//     groups SBO = 8 * row bytes apart; one K=16 step advances 16 rows.
-template <int BK>
+// BF16 operand tiles in shared memory, all with the 128-byte swizzle
+// (128-byte rows, 8-row / 1024-byte swizzle atoms):
+//   K-major tile (rows of K): BK must be 64 (one row = 64 K-elements); one
+//     K=16 MMA step advances the start address by 32 bytes; SBO = 1024.
+//   MN-major tile (rows of MN): stored as chunks of 64 MN-elements x BK
+//     K-rows; chunks LBO = 128 * BK bytes apart, 8-row groups SBO = 1024
+//     apart; one K=16 step advances 16 rows = 2048 bytes.  Any BK % 16 == 0.
 struct Swz {
-  static_assert(BK == 64 || BK == 32, "BK must be 32 or 64");
-  static constexpr uint32_t kRowBytes = BK * 2;
-  static constexpr uint32_t kLayout = BK == 64 ? 2u : 4u;
-  static constexpr uint32_t kSbo = 8 * kRowBytes;
-  static constexpr int kChunkElems = kRowBytes / 2;   // MN elements per MN-major chunk
-  static constexpr uint32_t kChunkBytes = kRowBytes * BK;
-  static constexpr uint32_t kMnStepBytes = 16 * kRowBytes;
+  static constexpr uint32_t kLayout = 2u;  // SWIZZLE_128B
+  static constexpr uint32_t kSbo = 1024;
+  static constexpr int kChunkElems = 64;
+  static constexpr uint32_t kMnStepBytes = 2048;
+  __host__ __device__ static constexpr uint32_t chunk_bytes(int bk) { return 128u * static_cast<uint32_t>(bk); }
 };
 
 // Instruction descriptor, kind::f16 with BF16 A/B and FP32 accumulator.
 //   bits 4-5 D format (1 = F32), 7-9 A format (1 = BF16), 10-12 B format,
 //   15 A major (0 = K), 16 B major (1 = MN), 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((static_cast<uint32_t>(m) >> 4) << 24);
 }
 

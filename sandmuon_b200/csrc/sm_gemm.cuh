@@ -5,9 +5,9 @@
 // sandmuon/optimizer.py:79-91) for every shape group of an optimizer at once.
 //
 // Design (one persistent CTA per SM, 10 warps):
-//   warp 0      TMA producer: streams A/B k-blocks of BK BF16 (BK = 64:
-//               128-byte rows, 128-byte swizzle; BK = 32: 64-byte rows,
-//               64-byte swizzle) into a STAGES-deep shared-memory ring.
+//   warp 0      TMA producer: streams A/B k-blocks (128-byte swizzle; BK = 64
+//               for K-major operands, BK = 32 when both operands are MN-major)
+//               into a STAGES-deep shared-memory ring.
 //   warp 1      MMA issuer: owns the TMEM allocation; one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered FP32
 //               accumulator in TMEM and releases ring slots with tcgen05.commit.
@@ -19,8 +19,9 @@
 //   acc += A_hi*B_lo; acc += A_lo*B_hi; acc += A_hi*B_hi
 // (the three-product order of the historical compensated kernel,
 // reproduction/odl/ops/bf16_compensated_mm_fast.py:64-66).
-// B is either K-major ([N, K] rows, for x x^T and the symmetric gram gram) or
-// MN-major ([K, N] rows, for p x).  No cluster multicast is used.
+// Operands are K-major ([M or N, K] rows: x for x x^T) or MN-major ([K, M or
+// N] rows: x for p x, and the symmetric p and g read as their own transposes).
+// No cluster multicast is used.
 // Tiles are visited in a host-computed per-CTA order (longest first, balanced
 // by k-blocks) when a schedule is given, else round-robin.
 #pragma once
@@ -147,12 +148,14 @@ struct TileIter {
   __device__ __forceinline__ void next() { pos += step; }
 };
 
-template <int BN, int BK, bool COMP, bool B_MN, int STAGES, int EPI>
+template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_constant__ GemmLaunch L) {
   using S = GemmSmem<BN, BK, COMP, STAGES>;
-  using W = Swz<BK>;
+  using W = Swz;
+  static_assert((A_MN || BK == 64) && (B_MN || BK == 64), "K-major operands need BK = 64");
   constexpr int kKSteps = BK / 16;
-  constexpr uint32_t kIdesc = umma_idesc_bf16(kGemmBM, BN, B_MN);
+  constexpr uint32_t kChunk = W::chunk_bytes(BK);
+  constexpr uint32_t kIdesc = umma_idesc_bf16(kGemmBM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -223,8 +226,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
           const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
           const uint32_t sb = sa + S::kOps * S::kABytes;
           const int kc = kb * BK;
-          tma_load_3d(sa, &P.a_hi, fb, kc, tc.mi * kGemmBM, tc.b);
-          if (COMP) tma_load_3d(sa + S::kABytes, &P.a_lo, fb, kc, tc.mi * kGemmBM, tc.b);
+          if (!A_MN) {
+            tma_load_3d(sa, &P.a_hi, fb, kc, tc.mi * kGemmBM, tc.b);
+            if (COMP) tma_load_3d(sa + S::kABytes, &P.a_lo, fb, kc, tc.mi * kGemmBM, tc.b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kGemmBM / W::kChunkElems; ++j) {
+              const int mc = tc.mi * kGemmBM + W::kChunkElems * j;
+              tma_load_3d(sa + j * kChunk, &P.a_hi, fb, mc, kc, tc.b);
+              if (COMP) tma_load_3d(sa + S::kABytes + j * kChunk, &P.a_lo, fb, mc, kc, tc.b);
+            }
+          }
           if (!B_MN) {
             tma_load_3d(sb, &P.b_hi, fb, kc, tc.ni * BN, tc.b);
             if (COMP) tma_load_3d(sb + S::kBBytes, &P.b_lo, fb, kc, tc.ni * BN, tc.b);
@@ -232,8 +244,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
 #pragma unroll
             for (int j = 0; j < BN / W::kChunkElems; ++j) {
               const int nc = tc.ni * BN + W::kChunkElems * j;
-              tma_load_3d(sb + j * W::kChunkBytes, &P.b_hi, fb, nc, kc, tc.b);
-              if (COMP) tma_load_3d(sb + S::kBBytes + j * W::kChunkBytes, &P.b_lo, fb, nc, kc, tc.b);
+              tma_load_3d(sb + j * kChunk, &P.b_hi, fb, nc, kc, tc.b);
+              if (COMP) tma_load_3d(sb + S::kBBytes + j * kChunk, &P.b_lo, fb, nc, kc, tc.b);
             }
           }
           if (++stage == STAGES) {
@@ -268,15 +280,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
           const uint32_t sb = sa + S::kOps * S::kABytes;
 #pragma unroll
           for (int ks = 0; ks < kKSteps; ++ks) {
-            const uint64_t a_hi = umma_desc(sa + ks * 32, 16, W::kSbo, W::kLayout);
-            const uint64_t b_hi = B_MN ? umma_desc(sb + ks * W::kMnStepBytes, W::kChunkBytes, W::kSbo, W::kLayout)
-                                       : umma_desc(sb + ks * 32, 16, W::kSbo, W::kLayout);
+            auto opdesc = [&](uint32_t base, bool mn) -> uint64_t {
+              return mn ? umma_desc(base + ks * W::kMnStepBytes, kChunk, W::kSbo, W::kLayout)
+                        : umma_desc(base + ks * 32, 16, W::kSbo, W::kLayout);
+            };
+            const uint64_t a_hi = opdesc(sa, A_MN);
+            const uint64_t b_hi = opdesc(sb, B_MN);
             const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
             if (COMP) {
-              const uint64_t a_lo = umma_desc(sa + S::kABytes + ks * 32, 16, W::kSbo, W::kLayout);
-              const uint64_t b_lo =
-                  B_MN ? umma_desc(sb + S::kBBytes + ks * W::kMnStepBytes, W::kChunkBytes, W::kSbo, W::kLayout)
-                       : umma_desc(sb + S::kBBytes + ks * 32, 16, W::kSbo, W::kLayout);
+              const uint64_t a_lo = opdesc(sa + S::kABytes, A_MN);
+              const uint64_t b_lo = opdesc(sb + S::kBBytes, B_MN);
               umma_bf16(d_tmem, a_hi, b_lo, kIdesc, accumulate);
               umma_bf16(d_tmem, a_lo, b_hi, kIdesc, 1u);
               umma_bf16(d_tmem, a_hi, b_hi, kIdesc, 1u);

@@ -184,3 +184,23 @@ def test_symmetric_poly_epilogue():
     gd = (gh.double() + gl.double())
     want = a * torch.eye(256, device=DEV, dtype=torch.float64) + b * gd + c * torch.bmm(gd, gd.transpose(1, 2))
     assert rel(ph.float() + pl.float(), want) < 2e-5
+
+
+@pytest.mark.parametrize("comp", [False, True])
+@pytest.mark.parametrize("n", [256, 384])
+def test_mn_major_a_and_b(comp, n):
+    """A read MN-major ([K, M] storage) with an MN-major B: the layout of the
+    symmetric P and G in P X and G G (32-deep k-blocks)."""
+    at = rnd(2, 192, 256, seed=18)    # [K, M]
+    b = rnd(2, 192, n, seed=19)       # [K, N]
+    ah, al = split(at)
+    bh, bl = split(b)
+    out = torch.empty(2, 256, n, device=DEV)
+    engine.gemm_bf16(ah, bh, a_lo=al if comp else None, b_lo=bl if comp else None, b_kmajor=False, a_mnmajor=True,
+                     epilogue=_lib.SM_EPI_F32, out0=out)
+    if comp:
+        want = torch.bmm(at.double().transpose(1, 2), b.double())
+        assert rel(out, want) < 2e-5
+    else:
+        want = torch.bmm(ah.float().transpose(1, 2), bh.float())
+        assert rel(out, want) < 1e-5
