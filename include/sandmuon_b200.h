@@ -251,11 +251,14 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
 #define SM_EPI_POLY 4       /* C = bf16(pa*I + pb*aux + pc*acc)                */
 #define SM_EPI_POLY_HILO 5  /* P = pa*I + pb*(aux + aux_lo) + pc*acc -> hi/lo  */
 #define SM_EPI_SYMMETRIC 0x100 /* flag: C is symmetric (M == N, K-major B); only the
-                                 upper-triangular 128x128 tiles are computed and each
+                                 upper-triangular square tiles are computed and each
                                  off-diagonal tile also stores its transpose        */
+#define SM_EPI_NORM_SLOTS 16   /* SM_EPI_F32_NORM partial sums per output tile   */
 
 #define SM_GEMM_B_KMAJOR 1   /* layout flag: B is [batch, N, K] (C = A B^T), else [batch, K, N] */
 #define SM_GEMM_A_MNMAJOR 2  /* layout flag: A is stored [batch, K, M] (A^T); needs an MN-major B */
+#define SM_GEMM_PAIR 4       /* layout flag: CTA-pair tiles of 256 rows (tcgen05 cta_group::2);
+                                needs M % 256 == 0 */
 
 /* Batched C[b] = A[b] * op(B[b]) on tcgen05 tensor cores.
  *   A: [batch, M, K] BF16 row-major (K contiguous), or [batch, K, M] with
@@ -266,8 +269,10 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
  *   out0/out1: outputs [batch, M, N] (out1 = lo plane for SM_EPI_HILO).
  *   alpha: device [batch] FP32 scales or NULL (1).  aux (and aux_lo for the
  *   hi/lo polynomial): BF16 [batch, M, N] for SM_EPI_POLY / SM_EPI_POLY_HILO.
- *   partials: device FP32 [batch, (M/128)*(N/BN)*8] for SM_EPI_F32_NORM
- *   (BN = 256 when N % 256 == 0 and the output is not symmetric, else 128). */
+ *   partials: device FP32 [batch, (M/TM)*(N/BN)*SM_EPI_NORM_SLOTS] for
+ *   SM_EPI_F32_NORM, whose sum over a matrix is |C|_F^2.  Tile rows TM = 256
+ *   with SM_GEMM_PAIR, else 128; tile columns BN = TM for a symmetric output,
+ *   else 256 when N % 256 == 0, else 128. */
 int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo,
                  int layout, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
                  void* out0, void* out1, const float* alpha, const void* aux, const void* aux_lo,

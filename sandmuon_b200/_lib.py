@@ -24,8 +24,10 @@ SM_EPI_F32_NORM = 3
 SM_EPI_POLY = 4
 SM_EPI_POLY_HILO = 5
 SM_EPI_SYMMETRIC = 0x100
+SM_EPI_NORM_SLOTS = 16
 SM_GEMM_B_KMAJOR = 1
 SM_GEMM_A_MNMAJOR = 2
+SM_GEMM_PAIR = 4
 SM_TCLASS_GEMM = 0
 SM_TCLASS_ELEMWISE = 1
 SM_TCLASS_STATS = 2

@@ -76,6 +76,7 @@ static inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 struct DeviceInfo {
   int sms = 0;
   bool attrs_set = false;
+  int pair_workers = -1;  // CTA pairs of the GEMM that can be resident at once (0: no pair mode)
 };
 static std::mutex g_dev_mutex;
 static DeviceInfo g_dev[64];
@@ -163,6 +164,11 @@ static int make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t out
 #ifndef SMB_USE_SCHEDULE
 #define SMB_USE_SCHEDULE 1
 #endif
+// S8 GEMMs of groups whose padded row count is a multiple of 256 run on CTA
+// pairs (256-row tiles, tcgen05 cta_group::2).
+#ifndef SMB_PAIR
+#define SMB_PAIR 1
+#endif
 // Every operand tile uses the 128-byte swizzle and 64-deep k-blocks (measured:
 // 32-deep stages, with twice as many in the ring, are 10-30% slower, and an
 // MN-major A reads no faster than a K-major one).  The ring holds as many
@@ -172,88 +178,153 @@ constexpr int kBkK = 64;   // every launch of the S8 path (K-major A)
 constexpr int kBkMN = 64;  // launches whose A and B are both MN-major (unit tests)
 constexpr uint32_t kChunk = Swz::kChunkElems;
 
-template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int EPI>
-static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
-  // Configured depth, capped by what fits in 227 KB of shared memory.
-  constexpr int kStageBytes = GemmSmem<BN, BK, COMP, 1>::kStageBytes;
-  constexpr int kFit = (232448 - 1024 - 256 - GemmSmem<BN, BK, COMP, 1>::kStagingBytes) / kStageBytes;
-  constexpr int kWant = COMP ? SMB_COMP_STAGES : SMB_PLAIN_STAGES;
-  constexpr int STAGES = kWant < kFit ? kWant : kFit;
-  using S = GemmSmem<BN, BK, COMP, STAGES>;
+// Ring depth of a configuration: the configured depth, capped by what fits in
+// 227 KB of shared memory next to the epilogue staging.
+template <int BN, int BK, bool COMP, int CG>
+struct GemmConfig {
+  static constexpr int kStageBytes = GemmSmem<BN, BK, COMP, 1, CG>::kStageBytes;
+  static constexpr int kFit = (232448 - 1024 - 256 - GemmSmem<BN, BK, COMP, 1, CG>::kStagingBytes) / kStageBytes;
+  static constexpr int kWant = COMP ? SMB_COMP_STAGES : SMB_PLAIN_STAGES;
+  static constexpr int kStages = kWant < kFit ? kWant : kFit;
+  using S = GemmSmem<BN, BK, COMP, kStages, CG>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
-  auto kern = k_gemm_bf16<BN, BK, COMP, A_MN, B_MN, STAGES, EPI>;
+};
+
+template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int EPI, int CG>
+static int gemm_kernel(void (**out)(GemmLaunch), int* smem_bytes) {
+  using C = GemmConfig<BN, BK, COMP, CG>;
+  auto kern = k_gemm_bf16<BN, BK, COMP, A_MN, B_MN, C::kStages, EPI, CG>;
   static bool attr_done[64] = {};
   int dev = 0;
   SM_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
   if (!attr_done[dev]) {
-    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::S::kTotal));
     attr_done[dev] = true;
   }
+  *out = kern;
+  *smem_bytes = C::S::kTotal;
+  return SM_OK;
+}
+
+static void pair_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int grid, int smem,
+                               cudaStream_t st) {
+  memset(cfg, 0, sizeof(*cfg));
+  memset(attr, 0, sizeof(*attr));
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = 2;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  cfg->gridDim = dim3(static_cast<unsigned>(grid));
+  cfg->blockDim = dim3(kGemmThreads);
+  cfg->dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg->stream = st;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+}
+
+template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int EPI, int CG>
+static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
+  void (*kern)(GemmLaunch);
+  int smem = 0;
+  SM_TRY((gemm_kernel<BN, BK, COMP, A_MN, B_MN, EPI, CG>(&kern, &smem)));
   if (L.total_tiles == 0 || grid == 0) return SM_OK;
-  kern<<<grid, kGemmThreads, S::kTotal, st>>>(L);
+  if (CG == 1) {
+    kern<<<grid, kGemmThreads, smem, st>>>(L);
+  } else {
+    if (grid % 2 != 0) return fail(SM_ERR_ARG, "a CTA-pair GEMM needs an even grid");
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    pair_launch_config(&cfg, &attr, grid, smem, st);
+    SM_CUDA(cudaLaunchKernelEx(&cfg, kern, L));
+  }
   SM_LAUNCHED();
+  return SM_OK;
+}
+
+// How many CTA pairs of the GEMM can be resident at once on this device (one
+// CTA per SM; pairs are placed within a GPC, so this can be below sms / 2).
+// Every pair configuration holds one CTA per SM, so the largest stands for all.
+static int pair_workers(DeviceInfo* di, int* out) {
+  if (di->pair_workers < 0) {
+    int n = 0;
+    if (SMB_PAIR) {
+      void (*kern)(GemmLaunch);
+      int smem = 0;
+      SM_TRY((gemm_kernel<256, 64, true, false, false, kEpiF32, 2>(&kern, &smem)));
+      cudaLaunchConfig_t cfg;
+      cudaLaunchAttribute attr;
+      pair_launch_config(&cfg, &attr, 2 * std::max(1, di->sms / 2), smem, nullptr);
+      SM_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    }
+    di->pair_workers = std::max(0, n);
+  }
+  *out = di->pair_workers;
   return SM_OK;
 }
 
 // Operand layouts: 0 = A and B K-major; 1 = A K-major, B MN-major; 2 = both MN-major.
 enum GemmLayout : int { kLayoutKK = 0, kLayoutKM = 1, kLayoutMM = 2 };
 
-template <int BN>
+template <int BN, int CG>
 static int dispatch_gemm_bn(bool comp, int layout, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
   if (layout == kLayoutKK) {
     if (comp) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, false, kEpiBF16>(L, grid, st);
-        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiHiLo>(L, grid, st);
-        case kEpiF32Norm: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32Norm>(L, grid, st);
-        case kEpiPolyHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiPolyHiLo>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32, CG>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, false, kEpiBF16, CG>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiHiLo, CG>(L, grid, st);
+        case kEpiF32Norm: return launch_gemm_t<BN, kBkK, true, false, false, kEpiF32Norm, CG>(L, grid, st);
+        case kEpiPolyHiLo: return launch_gemm_t<BN, kBkK, true, false, false, kEpiPolyHiLo, CG>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, false, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, false, kEpiBF16>(L, grid, st);
-        case kEpiPoly: return launch_gemm_t<BN, kBkK, false, false, false, kEpiPoly>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, false, kEpiF32, CG>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, false, kEpiBF16, CG>(L, grid, st);
+        case kEpiPoly: return launch_gemm_t<BN, kBkK, false, false, false, kEpiPoly, CG>(L, grid, st);
         default: break;
       }
     }
   } else if (layout == kLayoutKM) {
     if (comp) {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, true, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, true, kEpiBF16>(L, grid, st);
-        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, true, kEpiHiLo>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, true, false, true, kEpiF32, CG>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, true, false, true, kEpiBF16, CG>(L, grid, st);
+        case kEpiHiLo: return launch_gemm_t<BN, kBkK, true, false, true, kEpiHiLo, CG>(L, grid, st);
         default: break;
       }
     } else {
       switch (epi) {
-        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, true, kEpiF32>(L, grid, st);
-        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, true, kEpiBF16>(L, grid, st);
+        case kEpiF32: return launch_gemm_t<BN, kBkK, false, false, true, kEpiF32, CG>(L, grid, st);
+        case kEpiBF16: return launch_gemm_t<BN, kBkK, false, false, true, kEpiBF16, CG>(L, grid, st);
         default: break;
       }
     }
-  } else if (layout == kLayoutMM) {
+  } else if (layout == kLayoutMM && CG == 1) {
     if (epi == kEpiF32) {
-      return comp ? launch_gemm_t<BN, kBkMN, true, true, true, kEpiF32>(L, grid, st)
-                  : launch_gemm_t<BN, kBkMN, false, true, true, kEpiF32>(L, grid, st);
+      return comp ? launch_gemm_t<BN, kBkMN, true, true, true, kEpiF32, CG>(L, grid, st)
+                  : launch_gemm_t<BN, kBkMN, false, true, true, kEpiF32, CG>(L, grid, st);
     }
   }
   return fail(SM_ERR_ARG, "unsupported GEMM mode combination (compensated=" + std::to_string(comp) +
-                              ", layout=" + std::to_string(layout) + ", epilogue=" + std::to_string(epi) + ")");
+                              ", layout=" + std::to_string(layout) + ", epilogue=" + std::to_string(epi) +
+                              ", cta pair=" + std::to_string(CG == 2) + ")");
 }
 
-static int dispatch_gemm(int bn, bool comp, int layout, int epi, const GemmLaunch& L, int grid, cudaStream_t st) {
-  if (bn == 256) return dispatch_gemm_bn<256>(comp, layout, epi, L, grid, st);
-  if (bn == 128) return dispatch_gemm_bn<128>(comp, layout, epi, L, grid, st);
-  return fail(SM_ERR_ARG, "BN must be 128 or 256");
+static int dispatch_gemm(int bn, int cg, bool comp, int layout, int epi, const GemmLaunch& L, int grid,
+                         cudaStream_t st) {
+  if (cg == 1 && bn == 256) return dispatch_gemm_bn<256, 1>(comp, layout, epi, L, grid, st);
+  if (cg == 1 && bn == 128) return dispatch_gemm_bn<128, 1>(comp, layout, epi, L, grid, st);
+  if (cg == 2 && bn == 256) return dispatch_gemm_bn<256, 2>(comp, layout, epi, L, grid, st);
+  if (cg == 2 && bn == 128) return dispatch_gemm_bn<128, 2>(comp, layout, epi, L, grid, st);
+  return fail(SM_ERR_ARG, "BN must be 128 or 256 and the CTA group 1 or 2");
 }
 
 static inline int pick_bn(int64_t n) { return (n % 256 == 0 && SMB_BN_MAX >= 256) ? 256 : 128; }
 
 static GemmProblem gemm_problem(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
-                                const CUtensorMap& bl, int m, int n, int k, int batch, int bn, int sym = 0) {
+                                const CUtensorMap& bl, int m, int n, int k, int batch, int bn, int cg, int sym) {
   GemmProblem p;
   memset(&p, 0, sizeof(p));
   p.sym = sym;
@@ -265,7 +336,7 @@ static GemmProblem gemm_problem(const CUtensorMap& ah, const CUtensorMap& al, co
   p.n = n;
   p.k = k;
   p.batch = batch;
-  p.tiles_m = m / kGemmBM;
+  p.tiles_m = m / (kGemmBM * cg);
   p.tiles_n = n / bn;
   return p;
 }
@@ -278,15 +349,15 @@ static int64_t problem_tiles(const GemmProblem& p) {
 
 // Executed tensor FLOPs (symmetric products count only the tiles computed).
 static double problem_flops(const GemmProblem& p, bool comp) {
-  const double tile = 2.0 * kGemmBM * (static_cast<double>(p.n) / p.tiles_n) * p.k;
+  const double tile = 2.0 * (static_cast<double>(p.m) / p.tiles_m) * (static_cast<double>(p.n) / p.tiles_n) * p.k;
   return tile * static_cast<double>(problem_tiles(p)) * (comp ? 3.0 : 1.0);
 }
 
 // Balanced static tile schedule for problems given as (tiles, k-blocks per
 // tile), laid out back to back in launch-global tile order.  Tiles are taken
-// longest first and dealt to the least-loaded CTA (ties to the lowest CTA);
-// each CTA keeps its tiles in that order.  Output: [grid + 1] offsets then the
-// tile lists.
+// longest first and dealt to the least-loaded worker (CTA or CTA pair; ties to
+// the lowest); each worker keeps its tiles in that order.  Output: [grid + 1]
+// offsets then the tile lists, grid = the number of workers.
 static void lpt_schedule(const std::vector<std::pair<int64_t, int>>& probs, int grid, std::vector<int>& out) {
   std::vector<std::pair<int, int>> tiles;  // (k-blocks, global tile)
   int64_t base = 0;
@@ -371,7 +442,8 @@ struct Timer {
 struct Group {
   int r = 0, c = 0;      // oriented shape, r <= c
   int rp = 0, cp = 0;    // padded to multiples of 128
-  int bn_r = 0, bn_c = 0;
+  int cg = 1;            // 2: X X^T and P X run on CTA pairs (256-row tiles)
+  int bn_c = 0;          // N tile of P X
   int batch = 0;
   int mat_off = 0;       // first descriptor of this group in the MatDev table
   bool rank1 = false;
@@ -405,6 +477,12 @@ struct Carver {
   }
 };
 
+// F32Norm partial sums of one matrix's G*G (single-CTA symmetric 128 x 128 tiles).
+static int norm_slots_per_matrix(const Group& g) {
+  const int tiles = g.rp / kGemmBM;
+  return tiles * tiles * kNormSlots;
+}
+
 static void carve_group(Carver& cv, Group& g) {
   const size_t xs = static_cast<size_t>(g.batch) * g.rp * g.cp;
   const size_t gs = static_cast<size_t>(g.batch) * g.rp * g.rp;
@@ -418,8 +496,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.g2 = cv.take<float>(gs);
   g.ph = reinterpret_cast<__nv_bfloat16*>(g.g2);  // P hi | P lo in the g2 bytes
   g.pl = g.ph ? g.ph + gs : nullptr;
-  const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * kEpiWarps;
-  g.partials = cv.take<float>(static_cast<size_t>(g.batch) * per_mat);
+  g.partials = cv.take<float>(static_cast<size_t>(g.batch) * norm_slots_per_matrix(g));
   g.inv_norm = cv.take<float>(g.batch);
   g.s = cv.take<float>(g.batch);
   g.s_inv = cv.take<float>(g.batch);
@@ -445,12 +522,12 @@ static int encode_group_maps(Group& g) {
   return SM_OK;
 }
 
-static void init_group_shape(Group& g, int r, int c, int batch) {
+static void init_group_shape(Group& g, int r, int c, int batch, bool pair_ok) {
   g.r = r;
   g.c = c;
   g.rp = static_cast<int>(round_up(r, 128));
   g.cp = static_cast<int>(round_up(c, 128));
-  g.bn_r = 128;  // X X^T and G G are symmetric: square 128 x 128 tiles, upper triangle only
+  g.cg = (SMB_PAIR && g.rp % 256 == 0 && pair_ok) ? 2 : 1;
   g.bn_c = pick_bn(g.cp);
   g.batch = batch;
   g.dmax = c;
@@ -471,7 +548,8 @@ enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 struct LaunchSet {
   std::vector<int> groups;
   int bn = 0;
-  int grid = 0;
+  int cg = 1;
+  int grid = 0;  // CTAs (cg per worker)
   int* sched = nullptr;
   std::vector<int> h_sched;
 };
@@ -480,25 +558,33 @@ struct S8Launches {
   std::vector<LaunchSet> sets[3];
 };
 
-static int kind_bn(const Group& g, int kind) { return kind == kPX ? g.bn_c : g.bn_r; }
+// X X^T and P X run on CTA pairs where the group allows; G G (K = rows,
+// polynomial epilogue) stays on single-CTA 128 x 128 tiles, whose finer
+// triangle wastes less and balances better (measured: 256-row symmetric
+// tiles made G G 25% slower, while pairs made P X 10-12% faster).
+static int kind_cg(const Group& g, int kind) { return kind == kGramSq ? 1 : g.cg; }
+static int kind_bn(const Group& g, int kind) { return kind == kPX ? g.bn_c : kGemmBM * kind_cg(g, kind); }
 static int kind_k(const Group& g, int kind) { return kind == kGram ? g.cp : g.rp; }
 static int kind_n(const Group& g, int kind) { return kind == kPX ? g.cp : g.rp; }
 
 // Builds the launch sets of every GEMM kind.  With `cv` the tile schedules
-// are carved from the workspace (measured when cv.base is null).
-static void build_s8_launches(const std::vector<Group>& groups, int sms, Carver* cv, S8Launches* out) {
+// are carved from the workspace (measured when cv.base is null).  `pairs` is
+// the number of CTA pairs that can be resident at once.
+static void build_s8_launches(const std::vector<Group>& groups, int sms, int pairs, Carver* cv, S8Launches* out) {
   for (int kind = 0; kind < 3; ++kind) {
     std::vector<LaunchSet>& sets = out->sets[kind];
     sets.clear();
     for (int gi = 0; gi < static_cast<int>(groups.size()); ++gi) {
       const int bn = kind_bn(groups[gi], kind);
+      const int cg = kind_cg(groups[gi], kind);
       LaunchSet* set = nullptr;
       for (auto& s : sets)
-        if (s.bn == bn && static_cast<int>(s.groups.size()) < kMaxProblems) set = &s;
+        if (s.bn == bn && s.cg == cg && static_cast<int>(s.groups.size()) < kMaxProblems) set = &s;
       if (set == nullptr) {
         sets.push_back(LaunchSet());
         set = &sets.back();
         set->bn = bn;
+        set->cg = cg;
       }
       set->groups.push_back(gi);
     }
@@ -510,14 +596,15 @@ static void build_s8_launches(const std::vector<Group>& groups, int sms, Carver*
       int64_t total = 0;
       for (int gi : set.groups) {
         const Group& g = groups[gi];
-        const int64_t tm = g.rp / kGemmBM;
+        const int64_t tm = g.rp / (kGemmBM * set.cg);
         const int64_t tiles = kind == kPX ? tm * (kind_n(g, kind) / set.bn) * g.batch : tm * (tm + 1) / 2 * g.batch;
         probs.push_back({tiles, kind_k(g, kind) / kBkK});
         total += tiles;
       }
-      set.grid = static_cast<int>(std::min<int64_t>(total, sms));
-      if (cv != nullptr && set.grid > 0 && SMB_USE_SCHEDULE) {
-        lpt_schedule(probs, set.grid, set.h_sched);
+      const int workers = static_cast<int>(std::min<int64_t>(total, set.cg == 2 ? pairs : sms));
+      set.grid = workers * set.cg;
+      if (cv != nullptr && workers > 0 && SMB_USE_SCHEDULE) {
+        lpt_schedule(probs, workers, set.h_sched);
         set.sched = cv->take<int>(set.h_sched.size());
       }
     }
@@ -536,14 +623,15 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
   GemmProblem p;
   if (kind == kGram) {
     // X X^T: A = B = X, K-major, symmetric 128 x 128 tiles
-    p = gemm_problem(xK_h, comp ? xK_l : xK_h, xK_h, comp ? xK_l : xK_h, g.rp, g.rp, g.cp, g.batch, bn, 1);
+    p = gemm_problem(xK_h, comp ? xK_l : xK_h, xK_h, comp ? xK_l : xK_h, g.rp, g.rp, g.cp, g.batch, bn,
+                     kind_cg(g, kind), 1);
     p.out0 = g.gh;
     p.out1 = g.gl;
     *epi = comp ? kEpiHiLo : kEpiBF16;
   } else if (kind == kGramSq) {
     // G G with G symmetric: B = G read K-major as G^T
     p = gemm_problem(g.gh_K, comp ? g.gl_K : g.gh_K, g.gh_K, comp ? g.gl_K : g.gh_K, g.rp, g.rp, g.rp, g.batch,
-                     bn, 1);
+                     bn, kind_cg(g, kind), 1);
     if (stage == 0) {
       p.out0 = g.g2;
       p.partials = g.partials;
@@ -568,7 +656,7 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
     // k_poly_stage1), in the g2 bytes (stages 2-4) or in gl (stage 5).
     const CUtensorMap& pA_h = stage == 0 ? g.gh_K : (comp ? g.ph_K : g.gl_K);
     const CUtensorMap& pA_l = stage == 0 ? g.gl_K : (comp ? g.pl_K : g.gl_K);
-    p = gemm_problem(pA_h, pA_l, xMN_h, comp ? xMN_l : xMN_h, g.rp, g.cp, g.rp, g.batch, bn);
+    p = gemm_problem(pA_h, pA_l, xMN_h, comp ? xMN_l : xMN_h, g.rp, g.cp, g.rp, g.batch, bn, kind_cg(g, kind), 0);
     const bool last = stage == 4;
     const bool next_comp = stage + 1 < kCompensatedStages;
     if (last) {
@@ -607,7 +695,7 @@ static int launch_s8_kind(const std::vector<Group>& groups, const S8Launches& pl
     L.total_tiles = begin;
     L.sched = set.sched;
     const int layout = kind == kPX ? kLayoutKM : kLayoutKK;
-    SM_TIMED(tm, SM_TCLASS_GEMM, flops, st, dispatch_gemm(set.bn, comp, layout, epi, L, set.grid, st));
+    SM_TIMED(tm, SM_TCLASS_GEMM, flops, st, dispatch_gemm(set.bn, set.cg, comp, layout, epi, L, set.grid, st));
     ++*launches;
   }
   return SM_OK;
@@ -625,7 +713,7 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
     if (stage == 0) {
       // s = max(1.35 |G2|_F^(1/4), 1e-30); P = a I + b G/s/s + c G2/s/s/s/s (hi/lo in place of G)
       for (const Group& g : groups) {
-        const int per_mat = (g.rp / kGemmBM) * (g.rp / g.bn_r) * kEpiWarps;
+        const int per_mat = norm_slots_per_matrix(g);
         const int64_t per = static_cast<int64_t>(g.rp) * g.rp;
         const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 4, 1024), 512));
         SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
@@ -780,10 +868,14 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     mg[i] = g;
     slot[i] = counts[g]++;
   }
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  int pairs = 0;
+  SM_TRY(pair_workers(di, &pairs));
   std::vector<Group> groups(shapes.size());
   int off = 0;
   for (size_t g = 0; g < shapes.size(); ++g) {
-    init_group_shape(groups[g], shapes[g].first, shapes[g].second, counts[g]);
+    init_group_shape(groups[g], shapes[g].first, shapes[g].second, counts[g], pairs > 0);
     groups[g].mat_off = off;
     off += counts[g];
     bool any_r1 = false, any_diag = false;
@@ -808,10 +900,8 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     s_scal[s] = cv.take<float>(4);
   }
   for (auto& g : groups) carve_group(cv, g);
-  DeviceInfo* di;
-  SM_TRY(current_device_info(&di));
   S8Launches s8;
-  build_s8_launches(groups, di->sms, &cv, &s8);
+  build_s8_launches(groups, di->sms, pairs, &cv, &s8);
   *bytes = round_up(static_cast<int64_t>(cv.off), 256);
   if (plan != nullptr) {
     plan->s8 = s8;
@@ -930,10 +1020,10 @@ static int stats_launch_noalloc(const T* x, int64_t n_rows, int64_t n_cols, int6
 }
 
 // Layout: Group buffers, then MatDev table [batch], ones [max(rows, cols)].
-static int s8_layout(int32_t batch, int32_t rows, int32_t cols, void* ws, Group* g, MatDev** d_mats, float** ones,
-                     size_t* bytes) {
+static int s8_layout(int32_t batch, int32_t rows, int32_t cols, bool pair_ok, void* ws, Group* g, MatDev** d_mats,
+                     float** ones, size_t* bytes) {
   Carver cv(ws);
-  init_group_shape(*g, std::min(rows, cols), std::max(rows, cols), batch);
+  init_group_shape(*g, std::min(rows, cols), std::max(rows, cols), batch, pair_ok);
   g->rank1 = false;
   g->mat_off = 0;
   *d_mats = cv.take<MatDev>(batch);
@@ -1245,7 +1335,8 @@ size_t sm_s8_workspace_bytes(int32_t batch, int32_t rows, int32_t cols) {
   MatDev* dm;
   float* ones;
   size_t bytes = 0;
-  s8_layout(batch, rows, cols, nullptr, &g, &dm, &ones, &bytes);
+  // Sized for single-CTA tiles, whose norm partials outnumber a pair's.
+  s8_layout(batch, rows, cols, false, nullptr, &g, &dm, &ones, &bytes);
   return bytes;
 }
 
@@ -1258,14 +1349,16 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
     return fail(SM_ERR_ARG, "workspace must be a 256-byte aligned device pointer");
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
+  int pairs = 0;
+  SM_TRY(pair_workers(di, &pairs));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Group g;
   MatDev* d_mats;
   float* ones;
   size_t need = 0;
-  s8_layout(batch, rows, cols, nullptr, &g, &d_mats, &ones, &need);
+  s8_layout(batch, rows, cols, pairs > 0, nullptr, &g, &d_mats, &ones, &need);
   if (workspace_bytes < need) return fail(SM_ERR_WORKSPACE, "S8 workspace too small");
-  s8_layout(batch, rows, cols, workspace, &g, &d_mats, &ones, &need);
+  s8_layout(batch, rows, cols, pairs > 0, workspace, &g, &d_mats, &ones, &need);
   SM_TRY(encode_group_maps(g));
   SM_CUDA(cudaMemsetAsync(workspace, 0, need, st));
   const int64_t nmax = std::max(rows, cols);
@@ -1298,7 +1391,7 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, st, nullptr, &launches));
   std::vector<Group> groups(1, g);
   S8Launches s8;
-  build_s8_launches(groups, di->sms, nullptr, &s8);  // round-robin tiles: no schedule tables
+  build_s8_launches(groups, di->sms, pairs, nullptr, &s8);  // round-robin tiles: no schedule tables
   SM_TRY(run_s8(groups, s8, st, nullptr, &launches));
   SM_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * batch * per, st));
   {
@@ -1390,7 +1483,10 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   if (a_hi == nullptr || b_hi == nullptr || out0 == nullptr) return fail(SM_ERR_ARG, "null operand");
   const bool b_kmajor = (layout & SM_GEMM_B_KMAJOR) != 0;
   const bool a_mn = (layout & SM_GEMM_A_MNMAJOR) != 0;
+  const int cg = (layout & SM_GEMM_PAIR) ? 2 : 1;
   if (a_mn && b_kmajor) return fail(SM_ERR_ARG, "an MN-major A needs an MN-major B");
+  if (cg == 2 && m % 256 != 0) return fail(SM_ERR_ARG, "CTA-pair tiles need M%256 == 0");
+  if (cg == 2 && a_mn) return fail(SM_ERR_ARG, "CTA-pair tiles need a K-major A");
   const int sym = (epilogue & SM_EPI_SYMMETRIC) ? 1 : 0;
   epilogue &= ~SM_EPI_SYMMETRIC;
   if (sym && (m != n || !b_kmajor)) return fail(SM_ERR_ARG, "symmetric output needs M == N and K-major B");
@@ -1403,7 +1499,13 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   if (epilogue == SM_EPI_F32_NORM && partials == nullptr) return fail(SM_ERR_ARG, "norm epilogue needs partials");
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
-  const int bn = sym ? 128 : pick_bn(n);
+  int workers = di->sms;
+  if (cg == 2) {
+    SM_TRY(pair_workers(di, &workers));
+    if (workers <= 0) return fail(SM_ERR_UNSUPPORTED, "no CTA pair of the GEMM fits on this device");
+  }
+  const int bn = sym ? kGemmBM * cg : pick_bn(n);
+  const int b_box = bn / cg;  // K-major B rows one CTA stages
   const int bk = a_mn ? kBkMN : kBkK;
   CUtensorMap ah, al, bh, bl;
   // A: K-major [batch, M, K]; MN-major [batch, K, M].  B: K-major [batch, N, K]; MN-major [batch, K, N].
@@ -1414,17 +1516,17 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
     if (!a_mn) SM_TRY(make_map(&al, a_lo, k, m, batch, kChunk, kGemmBM));
     else SM_TRY(make_map(&al, a_lo, m, k, batch, kChunk, bk));
   }
-  if (b_kmajor) SM_TRY(make_map(&bh, b_hi, k, n, batch, kChunk, bn));
+  if (b_kmajor) SM_TRY(make_map(&bh, b_hi, k, n, batch, kChunk, b_box));
   else SM_TRY(make_map(&bh, b_hi, n, k, batch, kChunk, bk));
   bl = bh;
   if (comp) {
-    if (b_kmajor) SM_TRY(make_map(&bl, b_lo, k, n, batch, kChunk, bn));
+    if (b_kmajor) SM_TRY(make_map(&bl, b_lo, k, n, batch, kChunk, b_box));
     else SM_TRY(make_map(&bl, b_lo, n, k, batch, kChunk, bk));
   }
   GemmLaunch L;
   memset(&L, 0, sizeof(L));
   GemmProblem& p = L.p[0];
-  p = gemm_problem(ah, al, bh, bl, m, n, k, batch, bn, sym);
+  p = gemm_problem(ah, al, bh, bl, m, n, k, batch, bn, cg, sym);
   p.out0 = out0;
   p.out1 = out1;
   p.alpha = alpha;
@@ -1437,9 +1539,9 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   L.n_problems = 1;
   L.total_tiles = static_cast<int>(problem_tiles(p));
   L.sched = nullptr;
-  const int grid = std::min(L.total_tiles, di->sms);
+  const int grid = std::min(L.total_tiles, workers) * cg;
   const int lay = a_mn ? kLayoutMM : (b_kmajor ? kLayoutKK : kLayoutKM);
-  return dispatch_gemm(bn, comp, lay, epilogue, L, grid, static_cast<cudaStream_t>(stream));
+  return dispatch_gemm(bn, cg, comp, lay, epilogue, L, grid, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -5,8 +5,7 @@
 // sandmuon/optimizer.py:79-91) for every shape group of an optimizer at once.
 //
 // Design (one persistent CTA per SM, 10 warps):
-//   warp 0      TMA producer: streams A/B k-blocks (128-byte swizzle; BK = 64
-//               for K-major operands, BK = 32 when both operands are MN-major)
+//   warp 0      TMA producer: streams A/B k-blocks (128-byte swizzle, BK = 64)
 //               into a STAGES-deep shared-memory ring.
 //   warp 1      MMA issuer: owns the TMEM allocation; one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered FP32
@@ -14,6 +13,15 @@
 //   warps 2..9  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows; the two warps of a lane quarter take
 //               alternate 32-column chunks), apply the fused epilogue, store.
+// CTA-pair mode (CG = 2, clusters of two CTAs): a pair computes a 256 x BN
+// tile with tcgen05 cta_group::2 (M = 256).  Each CTA streams its own 128 A
+// rows and BN/2 of the B columns, so a ring slot holds half the B bytes of
+// the single-CTA mode and one SM's operand traffic per FLOP drops by a third
+// (compensated BN=256: 64 KB per slot instead of 96 KB, three slots instead
+// of two).  Both CTAs' TMA loads complete on the leader's full barrier; the
+// leader alone issues the MMAs and multicasts its commits to both CTAs' ring
+// and accumulator barriers; each CTA's epilogue drains its own TMEM rows and
+// arrives on the leader's accumulator-empty barrier.
 // Compensated mode (stages 1-4 of S8) loads hi and lo BF16 planes of both
 // operands and issues three MMAs per k-step into the same accumulator:
 //   acc += A_hi*B_lo; acc += A_lo*B_hi; acc += A_hi*B_hi
@@ -34,6 +42,9 @@ constexpr int kGemmBM = 128;
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxProblems = 4;
+// F32Norm partial slots per output tile: one per epilogue warp and CTA of a pair.
+constexpr int kNormSlots = SM_EPI_NORM_SLOTS;
+static_assert(kNormSlots == 2 * kEpiWarps, "norm partial slots");
 
 enum GemmEpi : int {
   kEpiF32 = SM_EPI_F32,
@@ -51,15 +62,15 @@ struct GemmProblem {
   int batch;
   int tiles_m, tiles_n;
   int tile_begin;       // first launch-global tile index of this problem
-  int sym;              // 1: C is symmetric (m == n, BN == 128): only tiles with
-                        // ni >= mi are computed, off-diagonal ones also store C^T
+  int sym;              // 1: C is symmetric (m == n, BN == tile rows): only tiles
+                        // with ni >= mi are computed, off-diagonal ones also store C^T
   void* out0;           // [batch, m, n] FP32 or BF16 (hi plane for hi/lo outputs)
   void* out1;           // lo plane for hi/lo outputs
   const float* alpha;   // [batch] scale of the accumulator, or null (= 1)
   const __nv_bfloat16* aux;     // [batch, m, n] BF16 gram (hi plane) for the poly epilogues
   const __nv_bfloat16* aux_lo;  // lo plane of the gram for the hi/lo poly epilogue
   float pa, pb, pc;     // poly coefficients: out = pa*I + pb*gram + pc*acc
-  float* partials;      // [batch, tiles_m*tiles_n*kEpiWarps] sum of squares (F32Norm)
+  float* partials;      // [batch, tiles_m*tiles_n*kNormSlots] sum of squares (F32Norm)
   const int* tmask;     // [batch] or null: 1 = store this matrix's FP32 result
                         // transposed ([n, m], row stride m) -- F32 epilogue only
 };
@@ -68,15 +79,16 @@ struct GemmLaunch {
   GemmProblem p[kMaxProblems];
   int n_problems;
   int total_tiles;
-  // Optional schedule: sched[0..grid] = per-CTA offsets into sched[grid+1..]
-  // (launch-global tile indices).  Null: CTA c visits c, c + grid, ...
+  // Optional schedule over workers (CTAs, or CTA pairs in pair mode):
+  // sched[0..workers] = per-worker offsets into sched[workers+1..] (launch-
+  // global tile indices).  Null: worker w visits w, w + workers, ...
   const int* sched;
 };
 
-template <int BN, int BK, bool COMP, int STAGES>
+template <int BN, int BK, bool COMP, int STAGES, int CG>
 struct GemmSmem {
-  static constexpr int kABytes = kGemmBM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kABytes = kGemmBM * BK * 2;       // this CTA's 128 A rows
+  static constexpr int kBBytes = (BN / CG) * BK * 2;     // this CTA's share of B
   static constexpr int kOps = COMP ? 2 : 1;
   static constexpr int kStageBytes = kOps * (kABytes + kBBytes);
   static constexpr int kBarrierBytes = (2 * STAGES + 4) * 8 + 16;
@@ -126,21 +138,25 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmLaunch& L, int t) {
   return c;
 }
 
-// The sequence of tiles a CTA visits; identical for all three warp roles.
+// The sequence of tiles a worker (CTA, or CTA pair) visits; identical for
+// all three warp roles and both CTAs of a pair.
+template <int CG>
 struct TileIter {
   const int* list;
   int pos, end, step;
   __device__ __forceinline__ explicit TileIter(const GemmLaunch& L) {
+    const int worker = static_cast<int>(blockIdx.x) / CG;
+    const int workers = static_cast<int>(gridDim.x) / CG;
     if (L.sched != nullptr) {
-      list = L.sched + gridDim.x + 1;
-      pos = L.sched[blockIdx.x];
-      end = L.sched[blockIdx.x + 1];
+      list = L.sched + workers + 1;
+      pos = L.sched[worker];
+      end = L.sched[worker + 1];
       step = 1;
     } else {
       list = nullptr;
-      pos = blockIdx.x;
+      pos = worker;
       end = L.total_tiles;
-      step = gridDim.x;
+      step = workers;
     }
   }
   __device__ __forceinline__ bool valid() const { return pos < end; }
@@ -148,14 +164,19 @@ struct TileIter {
   __device__ __forceinline__ void next() { pos += step; }
 };
 
-template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int STAGES, int EPI>
+template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int STAGES, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_constant__ GemmLaunch L) {
-  using S = GemmSmem<BN, BK, COMP, STAGES>;
+  using S = GemmSmem<BN, BK, COMP, STAGES, CG>;
   using W = Swz;
   static_assert((A_MN || BK == 64) && (B_MN || BK == 64), "K-major operands need BK = 64");
+  static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
+  static_assert(!B_MN || (BN / CG) % W::kChunkElems == 0, "an MN-major B share is whole 64-column chunks");
+  constexpr bool kPair = CG == 2;
+  constexpr int kTileM = kGemmBM * CG;  // output rows of one tile (both CTAs of a pair)
+  constexpr int kBRows = BN / CG;       // B rows / columns this CTA stages
   constexpr int kKSteps = BK / 16;
   constexpr uint32_t kChunk = W::chunk_bytes(BK);
-  constexpr uint32_t kIdesc = umma_idesc_bf16(kGemmBM, BN, A_MN, B_MN);
+  constexpr uint32_t kIdesc = umma_idesc_bf16(kTileM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -168,6 +189,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;  // 0 = the pair's MMA leader
   const uint32_t bar_base = smem_u32(bars);
   auto bar_full = [&](int s) { return bar_base + 8u * s; };
   auto bar_empty = [&](int s) { return bar_base + 8u * (STAGES + s); };
@@ -181,15 +203,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull(a), 1);
-      mbar_init(bar_tempty(a), kEpiWarps);
+      mbar_init(bar_tempty(a), kEpiWarps * CG);  // the epilogue warps of both CTAs of a pair
     }
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
+  __syncwarp();
+  // A pair's CTAs signal each other's barriers: both are initialised first.
+  if (kPair) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), S::kTmemCols);
+    if (kPair) tmem_alloc_pair(smem_u32(tmem_slot), S::kTmemCols);
+    else tmem_alloc(smem_u32(tmem_slot), S::kTmemCols);
   }
   if (warp == 0 && lane == 0) {
     for (int q = 0; q < L.n_problems; ++q) {
@@ -212,40 +238,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (TileIter it(L); it.valid() && ok; it.next()) {
+      for (TileIter<CG> it(L); it.valid() && ok; it.next()) {
         const TileCoord tc = decode_tile(L, it.tile());
         const GemmProblem& P = L.p[tc.q];
         const int kblocks = P.k / BK;
+        const int a_row = tc.mi * kTileM + static_cast<int>(rank) * kGemmBM;
+        const int b_row = tc.ni * BN + static_cast<int>(rank) * kBRows;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(bar_empty(stage), phase ^ 1u, abort_flag, kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
+          // The leader's full barrier counts the bytes of both CTAs of a pair.
           const uint32_t fb = bar_full(stage);
-          mbar_arrive_expect_tx(fb, S::kStageBytes);
+          const uint32_t fb_tx = kPair ? mapa_shared(fb, 0) : fb;
+          if (rank == 0) mbar_arrive_expect_tx(fb, CG * S::kStageBytes);
+          auto load = [&](uint32_t dst, const CUtensorMap* map, int c0, int c1) {
+            if (kPair) tma_load_3d_pair(dst, map, fb_tx, c0, c1, tc.b);
+            else tma_load_3d(dst, map, fb, c0, c1, tc.b);
+          };
           const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
           const uint32_t sb = sa + S::kOps * S::kABytes;
           const int kc = kb * BK;
           if (!A_MN) {
-            tma_load_3d(sa, &P.a_hi, fb, kc, tc.mi * kGemmBM, tc.b);
-            if (COMP) tma_load_3d(sa + S::kABytes, &P.a_lo, fb, kc, tc.mi * kGemmBM, tc.b);
+            load(sa, &P.a_hi, kc, a_row);
+            if (COMP) load(sa + S::kABytes, &P.a_lo, kc, a_row);
           } else {
 #pragma unroll
             for (int j = 0; j < kGemmBM / W::kChunkElems; ++j) {
-              const int mc = tc.mi * kGemmBM + W::kChunkElems * j;
-              tma_load_3d(sa + j * kChunk, &P.a_hi, fb, mc, kc, tc.b);
-              if (COMP) tma_load_3d(sa + S::kABytes + j * kChunk, &P.a_lo, fb, mc, kc, tc.b);
+              const int mc = a_row + W::kChunkElems * j;
+              load(sa + j * kChunk, &P.a_hi, mc, kc);
+              if (COMP) load(sa + S::kABytes + j * kChunk, &P.a_lo, mc, kc);
             }
           }
           if (!B_MN) {
-            tma_load_3d(sb, &P.b_hi, fb, kc, tc.ni * BN, tc.b);
-            if (COMP) tma_load_3d(sb + S::kBBytes, &P.b_lo, fb, kc, tc.ni * BN, tc.b);
+            load(sb, &P.b_hi, kc, b_row);
+            if (COMP) load(sb + S::kBBytes, &P.b_lo, kc, b_row);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / W::kChunkElems; ++j) {
-              const int nc = tc.ni * BN + W::kChunkElems * j;
-              tma_load_3d(sb + j * kChunk, &P.b_hi, fb, nc, kc, tc.b);
-              if (COMP) tma_load_3d(sb + S::kBBytes + j * kChunk, &P.b_lo, fb, nc, kc, tc.b);
+            for (int j = 0; j < kBRows / W::kChunkElems; ++j) {
+              const int nc = b_row + W::kChunkElems * j;
+              load(sb + j * kChunk, &P.b_hi, nc, kc);
+              if (COMP) load(sb + S::kBBytes + j * kChunk, &P.b_lo, nc, kc);
             }
           }
           if (++stage == STAGES) {
@@ -254,15 +288,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
           }
         }
       }
+      // Drain: every ring slot's last release (a commit, from the peer's
+      // leader in a pair) has arrived before this CTA may leave.
+      for (int i = 0; i < STAGES && ok; ++i) {
+        ok = mbar_wait(bar_empty(stage), phase ^ 1u, abort_flag, kStatusTimeoutProducer);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // (the leader's thread only, for both CTAs of a pair)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (TileIter it(L); it.valid() && ok; it.next(), ++local) {
+      for (TileIter<CG> it(L); it.valid() && ok; it.next(), ++local) {
         const TileCoord tc = decode_tile(L, it.tile());
         const int kblocks = L.p[tc.q].k / BK;
         const int acc = local & 1;
@@ -284,35 +328,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
               return mn ? umma_desc(base + ks * W::kMnStepBytes, kChunk, W::kSbo, W::kLayout)
                         : umma_desc(base + ks * 32, 16, W::kSbo, W::kLayout);
             };
+            auto mma = [&](uint64_t a, uint64_t b, uint32_t accumulate) {
+              if (kPair) umma_bf16_pair(d_tmem, a, b, kIdesc, accumulate);
+              else umma_bf16(d_tmem, a, b, kIdesc, accumulate);
+            };
             const uint64_t a_hi = opdesc(sa, A_MN);
             const uint64_t b_hi = opdesc(sb, B_MN);
             const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
             if (COMP) {
               const uint64_t a_lo = opdesc(sa + S::kABytes, A_MN);
               const uint64_t b_lo = opdesc(sb + S::kBBytes, B_MN);
-              umma_bf16(d_tmem, a_hi, b_lo, kIdesc, accumulate);
-              umma_bf16(d_tmem, a_lo, b_hi, kIdesc, 1u);
-              umma_bf16(d_tmem, a_hi, b_hi, kIdesc, 1u);
+              mma(a_hi, b_lo, accumulate);
+              mma(a_lo, b_hi, 1u);
+              mma(a_hi, b_hi, 1u);
             } else {
-              umma_bf16(d_tmem, a_hi, b_hi, kIdesc, accumulate);
+              mma(a_hi, b_hi, accumulate);
             }
           }
-          umma_commit(bar_empty(stage));
+          // Ring slot `stage` is free in both CTAs once these MMAs complete.
+          if (kPair) umma_commit_pair(bar_empty(stage), 0x3);
+          else umma_commit(bar_empty(stage));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(bar_tfull(acc));
+        if (kPair) umma_commit_pair(bar_tfull(acc), 0x3);
+        else umma_commit(bar_tfull(acc));
+      }
+      // Drain: both accumulators released by every epilogue warp (the
+      // peer's arrive remotely) before the leader may leave.
+      for (int i = 0; i < 2 && ok; ++i, ++local) {
+        ok = mbar_wait(bar_tempty(local & 1), ((local >> 1) & 1) ^ 1u, abort_flag, kStatusTimeoutMma);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;          // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;      // which alternate column chunks it takes
+    // the leader's accumulator-empty barriers (shared::cluster addresses)
+    const uint32_t tempty_leader0 = kPair ? mapa_shared(bar_tempty(0), 0) : bar_tempty(0);
     int local = 0;
-    for (TileIter it(L); it.valid(); it.next(), ++local) {
+    for (TileIter<CG> it(L); it.valid(); it.next(), ++local) {
       const TileCoord tc = decode_tile(L, it.tile());
       const GemmProblem& P = L.p[tc.q];
       const int acc = local & 1;
@@ -323,7 +381,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
 
-      const int row0 = tc.mi * kGemmBM + quarter * 32;  // first row of this warp's slab
+      // first row of this warp's slab: the tile, this CTA's half of a pair, the lane quarter
+      const int row0 = tc.mi * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const int row = row0 + lane;                        // the TMEM lane = tile row of this thread
       const size_t mat_off = static_cast<size_t>(tc.b) * P.m * P.n;
       const float alpha = P.alpha != nullptr ? P.alpha[tc.b] : 1.0f;
@@ -341,7 +400,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
           // Accumulator fully read into registers: hand it back to the MMA warp.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty(acc));
+          if (lane == 0) {
+            if (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * acc);
+            else mbar_arrive(bar_tempty(acc));
+          }
         }
         const int col0 = tc.ni * BN + j * 32;
         float v[32];
@@ -449,13 +511,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       }
       if (EPI == kEpiF32Norm) {
         // An off-diagonal tile stands for itself and its mirror; the mirror's
-        // partial slots are cleared so the per-matrix sum stays exact.
+        // partial slots are cleared so the per-matrix sum stays exact.  A
+        // single CTA also clears the slots a pair's second CTA would use.
         sumsq = warp_sum(sumsq);
         if (lane == 0) {
-          const int slot = warp - 2;
-          float* part = P.partials + static_cast<size_t>(tc.b) * P.tiles_m * P.tiles_n * kEpiWarps;
-          part[tc.local * kEpiWarps + slot] = mirror ? 2.0f * sumsq : sumsq;
-          if (mirror) part[(tc.ni * P.tiles_n + tc.mi) * kEpiWarps + slot] = 0.0f;
+          const int slot = static_cast<int>(rank) * kEpiWarps + (warp - 2);
+          float* part = P.partials + static_cast<size_t>(tc.b) * P.tiles_m * P.tiles_n * kNormSlots;
+          const size_t own = static_cast<size_t>(tc.local) * kNormSlots;
+          part[own + slot] = mirror ? 2.0f * sumsq : sumsq;
+          if (!kPair) part[own + kEpiWarps + slot] = 0.0f;
+          if (mirror) {
+            const size_t mt = static_cast<size_t>(tc.ni * P.tiles_n + tc.mi) * kNormSlots;
+            part[mt + slot] = 0.0f;
+            if (!kPair) part[mt + kEpiWarps + slot] = 0.0f;
+          }
         }
       }
     }
@@ -463,10 +532,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
 
   tc_fence_before();
   __syncthreads();
+  // Neither CTA of a pair frees TMEM or leaves while the other may still
+  // signal its barriers or the leader's MMAs may still read its operands.
+  if (kPair) cluster_sync_all();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::kTmemCols);
+    if (kPair) tmem_dealloc_pair(tmem_base, S::kTmemCols);
+    else tmem_dealloc(tmem_base, S::kTmemCols);
   }
 }
 

@@ -109,18 +109,21 @@ def s8_polar(x: torch.Tensor) -> torch.Tensor:
 
 # ---------------------------------------------------------------- GEMM (tests)
 
-def gemm_bf16(a_hi, b_hi, *, a_lo=None, b_lo=None, b_kmajor=True, a_mnmajor=False, epilogue=_lib.SM_EPI_F32,
-              out0=None, out1=None, alpha=None, aux=None, aux_lo=None, poly=(0.0, 0.0, 0.0), partials=None):
+def gemm_bf16(a_hi, b_hi, *, a_lo=None, b_lo=None, b_kmajor=True, a_mnmajor=False, pair=False,
+              epilogue=_lib.SM_EPI_F32, out0=None, out1=None, alpha=None, aux=None, aux_lo=None,
+              poly=(0.0, 0.0, 0.0), partials=None):
     """Direct access to the batched tcgen05 GEMM for unit tests.
 
     a: [batch, M, K] bf16, or [batch, K, M] (a_mnmajor); b: [batch, N, K]
-    (b_kmajor) or [batch, K, N] bf16."""
+    (b_kmajor) or [batch, K, N] bf16.  pair: 256-row tiles computed by CTA
+    pairs (tcgen05 cta_group::2), M % 256 == 0."""
     if a_mnmajor:
         batch, k, m = a_hi.shape
     else:
         batch, m, k = a_hi.shape
     n = b_hi.shape[1] if b_kmajor else b_hi.shape[2]
-    layout = (_lib.SM_GEMM_B_KMAJOR if b_kmajor else 0) | (_lib.SM_GEMM_A_MNMAJOR if a_mnmajor else 0)
+    layout = ((_lib.SM_GEMM_B_KMAJOR if b_kmajor else 0) | (_lib.SM_GEMM_A_MNMAJOR if a_mnmajor else 0)
+              | (_lib.SM_GEMM_PAIR if pair else 0))
     device = a_hi.device
     _lib.ensure_device(device)
     with torch.cuda.device(device):

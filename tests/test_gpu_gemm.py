@@ -88,7 +88,7 @@ def test_norm_partials_sum_to_frobenius_square():
     x = rnd(3, 256, 256, seed=10)
     xh, xl = split(x)
     out = torch.empty(3, 256, 256, device=DEV)
-    per_mat = (256 // 128) * (256 // 256) * 8  # 8 epilogue warps per tile
+    per_mat = (256 // 128) * (256 // 256) * _lib.SM_EPI_NORM_SLOTS
     partials = torch.empty(3, per_mat, device=DEV)
     engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32_NORM, out0=out, partials=partials)
     torch.testing.assert_close(partials.double().sum(1), out.double().square().sum((1, 2)), rtol=1e-5, atol=0)
@@ -167,7 +167,7 @@ def test_symmetric_mode_matches_full_product(epi):
         assert rel(hi.float() + lo.float(), want) < 2e-5
     else:
         out = torch.empty(3, 384, 384, device=DEV)
-        partials = torch.full((3, 3 * 3 * 8), float("nan"), device=DEV)
+        partials = torch.full((3, 3 * 3 * _lib.SM_EPI_NORM_SLOTS), float("nan"), device=DEV)
         engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out, partials=partials)
         torch.testing.assert_close(partials.double().sum(1), want.square().sum((1, 2)), rtol=1e-5, atol=0)
 
@@ -204,3 +204,100 @@ def test_mn_major_a_and_b(comp, n):
     else:
         want = torch.bmm(ah.float().transpose(1, 2), bh.float())
         assert rel(out, want) < 1e-5
+
+
+# ------------------------------------------------------------ CTA-pair mode
+# 256-row tiles computed by two CTAs with tcgen05 cta_group::2: each CTA
+# stages its own A rows and half of B; the leader issues the MMAs.
+
+@pytest.mark.parametrize("batch,m,n,k", [(1, 256, 256, 64), (2, 512, 384, 192), (2, 768, 768, 768),
+                                         (1, 256, 3072, 128)])
+@pytest.mark.parametrize("b_kmajor", [True, False])
+def test_pair_plain_f32(batch, m, n, k, b_kmajor):
+    a = rnd(batch, m, k, seed=21).to(torch.bfloat16)
+    b = rnd(batch, n, k, seed=22).to(torch.bfloat16) if b_kmajor else rnd(batch, k, n, seed=22).to(torch.bfloat16)
+    out = torch.full((batch, m, n), float("nan"), device=DEV)
+    engine.gemm_bf16(a, b, b_kmajor=b_kmajor, pair=True, epilogue=_lib.SM_EPI_F32, out0=out)
+    want = torch.bmm(a.float(), b.float().transpose(1, 2) if b_kmajor else b.float())
+    assert rel(out, want) < 1e-5
+    assert _lib.device_status(DEV) == 0
+
+
+@pytest.mark.parametrize("b_kmajor", [True, False])
+def test_pair_compensated_hilo_with_alpha(b_kmajor):
+    p = rnd(2, 512, 256, seed=23)
+    x = rnd(2, 512, 256, seed=24) if b_kmajor else rnd(2, 256, 512, seed=24)
+    ph, pl = split(p)
+    xh, xl = split(x)
+    oh = torch.full((2, 512, 512), float("nan"), device=DEV, dtype=torch.bfloat16)
+    ol = torch.full_like(oh, float("nan"))
+    alpha = torch.tensor([0.5, -3.0], device=DEV)
+    engine.gemm_bf16(ph, xh, a_lo=pl, b_lo=xl, b_kmajor=b_kmajor, pair=True, epilogue=_lib.SM_EPI_HILO, out0=oh,
+                     out1=ol, alpha=alpha)
+    want = torch.bmm(p.double(), x.double().transpose(1, 2) if b_kmajor else x.double())
+    want = want * alpha.double()[:, None, None]
+    assert rel(oh.float() + ol.float(), want) < 2e-5
+
+
+def test_pair_matches_single_cta_bitwise():
+    """Same tiles' K order and the same FP32 accumulation: identical results."""
+    x = rnd(3, 512, 768, seed=25)
+    xh, xl = split(x)
+    outs = []
+    for pair in (False, True):
+        out = torch.empty(3, 512, 512, device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=pair, epilogue=_lib.SM_EPI_F32, out0=out)
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("epi", ["f32", "hilo", "norm"])
+def test_pair_symmetric_mode(epi):
+    x = rnd(3, 768, 512, seed=26)
+    xh, xl = split(x)
+    want = torch.bmm(x.double(), x.double().transpose(1, 2))
+    sym = _lib.SM_EPI_SYMMETRIC
+    if epi == "f32":
+        out = torch.full((3, 768, 768), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_F32 | sym, out0=out)
+        assert rel(out, want) < 2e-5
+    elif epi == "hilo":
+        hi = torch.full((3, 768, 768), float("nan"), device=DEV, dtype=torch.bfloat16)
+        lo = torch.full_like(hi, float("nan"))
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_HILO | sym, out0=hi, out1=lo)
+        assert rel(hi.float() + lo.float(), want) < 2e-5
+    else:
+        out = torch.empty(3, 768, 768, device=DEV)
+        partials = torch.full((3, 3 * 3 * _lib.SM_EPI_NORM_SLOTS), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out,
+                         partials=partials)
+        torch.testing.assert_close(partials.double().sum(1), want.square().sum((1, 2)), rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("comp", [False, True])
+def test_pair_symmetric_poly_epilogues(comp):
+    g = rnd(2, 512, 512, seed=27, scale=0.05)
+    g = (g + g.transpose(1, 2)) / 2
+    gh, gl = split(g)
+    a, b, c = 3.28, -2.41, 0.486
+    out = torch.full_like(gh, float("nan"))
+    if comp:
+        out_lo = torch.full_like(gh, float("nan"))
+        engine.gemm_bf16(gh, gh, a_lo=gl, b_lo=gl, pair=True, epilogue=_lib.SM_EPI_POLY_HILO | _lib.SM_EPI_SYMMETRIC,
+                         out0=out, out1=out_lo, aux=gh, aux_lo=gl, poly=(a, b, c))
+        gd = gh.double() + gl.double()
+        got, tol = out.float() + out_lo.float(), 2e-5
+    else:
+        engine.gemm_bf16(gh, gh, pair=True, epilogue=_lib.SM_EPI_POLY | _lib.SM_EPI_SYMMETRIC, out0=out, aux=gh,
+                         poly=(a, b, c))
+        gd = gh.double()
+        got, tol = out.float(), 4e-3
+    want = a * torch.eye(512, device=DEV, dtype=torch.float64) + b * gd + c * torch.bmm(gd, gd.transpose(1, 2))
+    assert rel(got, want) < tol
+    assert _lib.device_status(DEV) == 0
+
+
+def test_pair_rejects_unaligned_rows():
+    a = torch.zeros(1, 384, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="M%256"):
+        engine.gemm_bf16(a, a, pair=True, out0=torch.empty(1, 384, 384, device=DEV))
