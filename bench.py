@@ -1,21 +1,28 @@
 #!/usr/bin/env python
 """Benchmark of one SandMuon optimizer step on B200 (config 1 of the baseline).
 
-Workload: the 9-layer x 768 GPT matrix set -- per layer
-q/k/v/o 768x768, mlp.c_fc 3072x768, mlp.c_proj 768x3072, 54 matrices,
-63,700,992 FP32 parameters -- under RankOneAWeightedPE.  Gradients ~ N(0,
-1e-4^2), weights ~ N(0, 0.02^2), and the hook statistics of 8 microbatches x
-16384 rows (drawn like config 0) are injected as accumulated sums.  A step =
-statistics finish + Nesterov momentum + whitening + 5-stage S8 + mapback +
-graft + update (+ the statistic all-reduce and the weight all-gather when
-N > 1).  The sums are refilled before every step with one device copy (the
-step zeroes them, as in training).
+Workload (the default): the 9-layer x 768 GPT matrix
+set -- per layer q/k/v/o 768x768, mlp.c_fc 3072x768, mlp.c_proj 768x3072, 54
+matrices, 63,700,992 FP32 parameters -- under RankOneAWeightedPE.  Gradients
+~ N(0, 1e-4^2), weights ~ N(0, 0.02^2), and the hook statistics of 8
+microbatches x 16384 rows (drawn like config 0) are injected as accumulated
+sums.  A step = statistics finish + Nesterov momentum + whitening + 5-stage
+S8 + mapback + graft + update (+ the statistic all-reduce and the weight
+all-gather when N > 1).  The sums are refilled before every step with one
+device copy (the step zeroes them, as in training).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                  [--workload cfg1|cfg4|cfg3|stats]
 
 Prints one JSON line (rank 0).  value = device ms per step, max over ranks;
 e2e = the same through the public API with pinned-host gradients/statistics
 copied in and the updated weights copied out inside the timed region.
+
+Other workloads (not the contract line): cfg4 = the same step on the 24-layer
+x 2048 matrix set (144 matrices); cfg3 = the S8 sweep of BASELINE configs[3]
+(one line per shape: S8 TFLOP/s and error against an FP32 torch restatement,
+plus one optimizer step of each class); stats = the hook statistic
+reductions of one config-1 microbatch (HBM GB/s, FP32 and BF16 inputs).
 """
 from __future__ import annotations
 
@@ -38,10 +45,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "SandMuon step ms & S8 GEMM TFLOP/s, 9L×768 GPT matrices, 1/2/4/8 B200"
 UNIT = "ms/step"
-LAYERS, WIDTH, HIDDEN = 9, 768, 3072
-ROWS = 8 * 16 * 1024
 LR = 1e-2
 SEED = 1337
+# matrix-set workloads: (layers, width, hidden, statistic rows per step)
+SETS = {"cfg1": (9, 768, 3072, 8 * 16 * 1024), "cfg4": (24, 2048, 8192, 8 * 8 * 2048)}
 
 
 def parse_args():
@@ -53,6 +60,7 @@ def parse_args():
     ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no CPU baseline, clock probe or e2e pass")
+    ap.add_argument("--workload", choices=("cfg1", "cfg4", "cfg3", "stats"), default="cfg1")
     return ap.parse_args()
 
 
@@ -65,12 +73,14 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def workload_config(world, partition):
+def workload_config(world, partition, workload="cfg1"):
+    layers, width, hidden, rows = SETS[workload]
+    params = layers * (4 * width * width + 2 * width * hidden)
     return {
-        "workload": "cfg1: 9Lx768 GPT matrix set (54 matrices, 63.7M FP32 params), RankOneAWeightedPE step, "
-                    "statistics of 8x16384 rows injected",
-        "matrices": LAYERS * 6,
-        "params": LAYERS * (4 * WIDTH * WIDTH + 2 * WIDTH * HIDDEN),
+        "workload": f"{workload}: {layers}Lx{width} GPT matrix set ({layers * 6} matrices, {params / 1e6:.1f}M FP32 "
+                    f"params), RankOneAWeightedPE step, statistics of {rows} rows injected",
+        "matrices": layers * 6,
+        "params": params,
         "s8_precision": "stages 1-4 compensated bf16 (hi/lo, 3 products), stage 5 bf16, fp32 accumulate",
         "l2": "no flush: each step streams ~1 GB of FP32 state (> 126 MB L2)",
         "parallelism": f"matrix-sharded ({partition}) x{world}" if world > 1 else "single GPU",
@@ -135,12 +145,13 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload
 
-def build(device, group, partition):
+def build(device, group, partition, workload="cfg1"):
     from sandmuon_b200 import RankOneAWeightedPE
     from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    layers, width, hidden, rows = SETS[workload]
     torch.manual_seed(SEED)
     rng = np.random.default_rng(SEED)
-    model = gpt_matrix_model(LAYERS, WIDTH, HIDDEN)
+    model = gpt_matrix_model(layers, width, hidden)
     with torch.no_grad():
         for p in model.parameters():
             p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
@@ -151,15 +162,21 @@ def build(device, group, partition):
         g = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
         grads_host[n] = torch.from_numpy(g).pin_memory()
         p.grad = grads_host[n].to(device)
-    stats = synth_gpt_statistics(opt, rng, count=ROWS, inject=False)
-    # every statistic sum lives in one flat buffer so a refill is one copy
+    stats = synth_gpt_statistics(opt, rng, count=rows, inject=False)
+    refill, stat_bytes = make_refill(opt, stats, rows, device)
+    return model, opt, grads_host, refill, stat_bytes
+
+
+def make_refill(opt, stats, rows, device):
+    """Places the statistic sums in the optimizer's flat statistic buffer (the
+    layout its hooks use) and returns refill(from_host=False), which restores
+    them with one copy (the step consumes and zeroes them), and their bytes."""
     order = []
+    keys = ("a_sum", "a_first_sum", "b_sum") if opt.rank_one_a else ("a_sum", "b_sum")
     for n, entry in stats.items():
-        for key in ("a_sum", "a_first_sum", "b_sum"):
+        for key in keys:
             if key in entry:
                 order.append((n, key, entry[key]))
-    # the statistic sums live in the optimizer's flat statistic buffer (the
-    # layout its hooks use), so a refill is one copy of the whole buffer
     for n, key, arr in order:
         opt.state[opt.named_matrices[n]][key] = opt._stat_slot(opt.named_matrices[n], key, arr.size, device)
     flat, layout = opt._stat_flat[device]
@@ -174,9 +191,9 @@ def build(device, group, partition):
     def refill(from_host=False):
         flat.copy_(src_host if from_host else src_dev, non_blocking=True)
         for st, key in counts:
-            st[key] = ROWS
+            st[key] = rows
 
-    return model, opt, grads_host, refill, flat.numel() * 4
+    return refill, flat.numel() * 4
 
 
 def time_steps(opt, refill, steps, device):
@@ -190,24 +207,25 @@ def time_steps(opt, refill, steps, device):
     return start.elapsed_time(end) / steps
 
 
-def cpu_baseline_sample(seconds=10.0):
-    """The numpy oracle on one of the nine layers (6 of 54 matrices), repeated
-    for ~`seconds`; the median is scaled by 9 to a full config-1 step."""
+def cpu_baseline_sample(seconds=10.0, workload="cfg1"):
+    """The numpy oracle on one layer of the matrix set (6 matrices), repeated
+    for ~`seconds`; the median is scaled by the layer count to a full step."""
     from oracle import sandmuon_oracle as orc
+    layers, width, hidden, rows = SETS[workload]
     rng = np.random.default_rng(SEED)
-    shapes = {f"transformer.h.0.attn.{p}.weight": (WIDTH, WIDTH) for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
-    shapes["transformer.h.0.mlp.c_fc.weight"] = (HIDDEN, WIDTH)
-    shapes["transformer.h.0.mlp.c_proj.weight"] = (WIDTH, HIDDEN)
+    shapes = {f"transformer.h.0.attn.{p}.weight": (width, width) for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
+    shapes["transformer.h.0.mlp.c_fc.weight"] = (hidden, width)
+    shapes["transformer.h.0.mlp.c_proj.weight"] = (width, hidden)
     source = {n: n.replace("k_proj", "q_proj").replace("v_proj", "q_proj") for n in shapes}
     weights = {n: (rng.standard_normal(s) * 0.02).astype(np.float32) for n, s in shapes.items()}
     grads = {n: (rng.standard_normal(s) * 1e-4).astype(np.float32) for n, s in shapes.items()}
     stats = {}
     for n, (d_out, d_in) in shapes.items():
-        e = {"b_sum": (ROWS * (1e-3 * np.exp(rng.normal(0, .5, d_out))) ** 2).astype(np.float32), "b_count": ROWS}
+        e = {"b_sum": (rows * (1e-3 * np.exp(rng.normal(0, .5, d_out))) ** 2).astype(np.float32), "b_count": rows}
         if source[n] == n:
             mean, std = rng.normal(.1, .05, d_in), np.exp(rng.normal(0, .5, d_in))
-            e.update(a_sum=(ROWS * (mean ** 2 + std ** 2)).astype(np.float32),
-                     a_first_sum=(ROWS * mean).astype(np.float32), a_count=ROWS)
+            e.update(a_sum=(rows * (mean ** 2 + std ** 2)).astype(np.float32),
+                     a_first_sum=(rows * mean).astype(np.float32), a_count=rows)
         stats[n] = e
     opt = orc.OracleSandMuon(shapes, source, rank_one_a=True, lr=LR)
     times = []
@@ -223,7 +241,179 @@ def cpu_baseline_sample(seconds=10.0):
         cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) if threadpool_info() else os.cpu_count()
     except Exception:
         cores = os.cpu_count()
-    return statistics.median(times[1:] if len(times) > 2 else times) * 9 * 1e3, cores, len(times)
+    return statistics.median(times[1:] if len(times) > 2 else times) * layers * 1e3, cores, len(times)
+
+
+# ------------------------------------------------------- config 3: S8 sweep
+
+CFG3_SHAPES = ((1024, 1024, 16), (4096, 4096, 4), (8192, 8192, 1), (4096, 1024, 8), (1024, 4096, 8))
+CFG3_SEED = 7
+
+
+def cfg3_batch(rows, cols, batch, device, gen):
+    """N(0,1) entries times a random column diagonal with LogNormal(0,1)
+    scales, plus a rank-1 spike u v^T of norm 10 x sigma_max (power iteration)."""
+    x = torch.randn(batch, rows, cols, generator=gen, device=device)
+    x *= torch.exp(torch.randn(batch, 1, cols, generator=gen, device=device))
+    v = torch.randn(batch, cols, 1, generator=gen, device=device)
+    for _ in range(30):
+        v = torch.bmm(x.transpose(1, 2), torch.bmm(x, v))
+        v = v / v.norm(dim=1, keepdim=True)
+    sigma = torch.bmm(x, v).norm(dim=1, keepdim=True)  # [B, 1, 1]
+    u = torch.randn(batch, rows, 1, generator=gen, device=device)
+    w = torch.randn(batch, 1, cols, generator=gen, device=device)
+    u, w = u / u.norm(dim=1, keepdim=True), w / w.norm(dim=2, keepdim=True)
+    return x + 10.0 * sigma * torch.bmm(u, w)
+
+
+def s8_fp32_torch(x):
+    """FP32 torch restatement of the reference's _s8_fp32 (sandmuon/optimizer.py:
+    69-93) used as the error yardstick: orient r <= c, X /= |X|_F, stage 1
+    with s = 1.35 |G^2|_F^(1/4), four more stages, coefficients of
+    sandmuon/coefficients.py."""
+    from sandmuon_b200 import S8_COEFFICIENTS, S8_MARGIN
+    t = x.shape[-2] > x.shape[-1]
+    if t:
+        x = x.transpose(-2, -1)
+    x = x / x.norm(dim=(-2, -1), keepdim=True).clamp_min(1e-30)
+    eye = torch.eye(x.shape[-2], device=x.device, dtype=x.dtype)
+    for i, (a, b, c) in enumerate(S8_COEFFICIENTS):
+        g = x @ x.transpose(-2, -1)
+        g2 = g @ g
+        if i == 0:
+            s = (S8_MARGIN * g2.norm(dim=(-2, -1), keepdim=True) ** 0.25).clamp_min(1e-30)
+            p = a * eye + b * g / s / s + c * g2 / s / s / s / s
+            x = (p @ x) / s
+        else:
+            x = (a * eye + b * g + c * g2) @ x
+    return x.transpose(-2, -1) if t else x
+
+
+def event_ms(fn, reps, device):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record()
+    for _ in range(reps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / reps
+
+
+def run_cfg3(args, device):
+    """One JSON line per shape: the engine's batch S8 (device ms, executed and
+    dense 5-stage TFLOP/s, error vs FP32) and one optimizer step of each class
+    on Linear weights of that shape (step ms, S8 GEMM TFLOP/s)."""
+    from torch import nn
+    from sandmuon_b200 import DiagonalWeightedPE, RankOneAWeightedPE, engine
+    from sandmuon_b200.workloads import synth_gpt_statistics
+    torch.backends.cuda.matmul.allow_tf32 = False
+    peak = peaks()[0]
+    for rows, cols, batch in CFG3_SHAPES:
+        gen = torch.Generator(device=device).manual_seed(CFG3_SEED)
+        x = cfg3_batch(rows, cols, batch, device, gen)
+        ms = event_ms(lambda: engine.s8_polar(x), max(args.warmup, 3), device)
+        ms = event_ms(lambda: engine.s8_polar(x), max(args.steps // 4, 3), device)
+        got = engine.s8_polar(x).double()
+        want = s8_fp32_torch(x).double()
+        err = ((got - want).norm(dim=(-2, -1)) / want.norm(dim=(-2, -1))).max().item()
+        cos = ((got * want).sum((-2, -1)) / (got.norm(dim=(-2, -1)) * want.norm(dim=(-2, -1)))).min().item()
+        executed = engine.s8_executed_flops(batch, rows, cols, device)
+        r, c = min(rows, cols), max(rows, cols)
+        dense = 5 * batch * (4.0 * r * r * c + 2.0 * r ** 3)
+        del got, want
+        line = {"workload": "cfg3", "shape": [rows, cols], "batch": batch, "s8_ms": round(ms, 4),
+                "s8_tflops_executed": round(executed / ms / 1e9, 1),
+                "s8_tflops_fp32_equivalent": round(dense / ms / 1e9, 1),
+                "frac_of_measured_peak": round(executed / ms / 1e9 / peak, 4),
+                "rel_frobenius_err_vs_fp32_max": round(err, 6), "cosine_min": round(cos, 8),
+                "data": f"synthetic seed {CFG3_SEED}: N(0,1) x LogNormal(0,1) column scales + rank-1 spike 10 sigma_max"}
+        for name, cls in (("diag", DiagonalWeightedPE), ("rank1", RankOneAWeightedPE)):
+            model = nn.ModuleList([nn.Linear(cols, rows, bias=False) for _ in range(batch)]).to(device)
+            with torch.no_grad():
+                for i, lin in enumerate(model):
+                    lin.weight.mul_(0.0).add_(x[i] * 1e-3)
+                    lin.weight.grad = x[i].clone() * 1e-4
+            opt = cls(model, lr=LR)
+            rng = np.random.default_rng(CFG3_SEED)
+            stats = synth_gpt_statistics(opt, rng, count=8 * 2048, inject=False)
+            refill, _ = make_refill(opt, stats, 8 * 2048, device)
+
+            def step():
+                refill()
+                opt.step()
+            for _ in range(3):
+                step()
+            opt._last_plan.set_timing(True)
+            step_ms = event_ms(step, 3, device)
+            timing = opt._last_plan.read_timing()
+            opt._last_plan.set_timing(False)
+            gemm_ms = timing["ms"]["gemm"] / 3
+            line[f"{name}_step_ms"] = round(step_ms, 4)
+            line[f"{name}_gemm_tflops"] = round(timing["gemm_flops"] / 3 / (gemm_ms * 1e-3) / 1e12, 1)
+            opt.close()
+            del model, opt
+        print(json.dumps(line), flush=True)
+        del x
+        torch.cuda.empty_cache()
+
+
+# ------------------------------------------------- hook statistics (N1)
+
+def run_stats(args, device):
+    """The hook reductions of one config-1 microbatch (16384 rows; per layer
+    A side 768 x 3 + 3072 columns with q/k/v sharing, B side 768 x 5 + 3072),
+    on resident FP32 and BF16 inputs, each call a distinct buffer (9 x 10
+    calls, 0.8 / 0.4 GB per pass, > L2).  Reports algorithmic HBM GB/s
+    (input bytes + accumulator read-modify-write) against the measured copy
+    bandwidth."""
+    from sandmuon_b200 import engine
+    n = 16 * 1024
+    a_cols = [768, 768, 768, 3072]          # q (shared by k, v), o, fc in, proj in
+    b_cols = [768, 768, 768, 768, 3072, 768]
+    hbm = peaks()[2]
+    for dtype in (torch.float32, torch.bfloat16):
+        gen = torch.Generator(device=device).manual_seed(SEED)
+        calls = []
+        for _ in range(9):
+            for c in a_cols:
+                calls.append((torch.randn(n, c, generator=gen, device=device).to(dtype),
+                              torch.zeros(c, device=device), torch.zeros(c, device=device)))
+            for c in b_cols:
+                calls.append((torch.randn(n, c, generator=gen, device=device).to(dtype),
+                              torch.zeros(c, device=device), None))
+        nbytes = sum(x.numel() * x.element_size() + (2 if t is not None else 1) * 8 * x.shape[1]
+                     for x, _, t in calls)
+
+        def one_pass():
+            for x, sq, t in calls:
+                engine.accumulate_column_stats(x, sq, t)
+        event_ms(one_pass, max(args.warmup, 3), device)
+        eager_ms = event_ms(one_pass, max(args.steps, 5), device)
+        # the same launches replayed from a CUDA graph: device time without
+        # the per-call host cost of the Python hook path
+        graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            one_pass()
+            torch.cuda.synchronize(device)
+            with torch.cuda.graph(graph, stream=stream):
+                one_pass()
+        torch.cuda.current_stream(device).wait_stream(stream)
+        event_ms(graph.replay, 3, device)
+        ms = event_ms(graph.replay, max(args.steps, 5), device)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": "stats", "metric": "hook statistic reductions, one cfg1 microbatch",
+                          "dtype": str(dtype).replace("torch.", ""), "hook_calls_per_pass": len(calls),
+                          "ms_per_microbatch": round(ms, 4), "ms_per_microbatch_eager": round(eager_ms, 4),
+                          "bytes_per_microbatch": nbytes,
+                          "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                       "frac": round(gbs / hbm, 4), "timing": "CUDA-graph replay, events"}}),
+              flush=True)
+        del graph
+        del calls
+        torch.cuda.empty_cache()
 
 
 # ------------------------------------------------------------------- main
@@ -239,18 +429,20 @@ def run_reference(args, rank):
         pass
     value, cores, reps = None, None, 0
     samples = []
+    workload = args.workload if args.workload in SETS else "cfg1"
+    layers = SETS[workload][0]
     for _ in range(args.warmup):
-        cpu_baseline_sample(seconds=0.0)
+        cpu_baseline_sample(seconds=0.0, workload=workload)
     for _ in range(args.steps):
-        v, cores, _ = cpu_baseline_sample(seconds=0.0)
+        v, cores, _ = cpu_baseline_sample(seconds=0.0, workload=workload)
         samples.append(v)
     value = statistics.median(samples)
-    sample = ("numpy port of the reference's eager FP32 step (oracle/sandmuon_oracle.py) on 1 of the 9 layers "
-              "(6 of 54 matrices) per step, scaled x9")
+    sample = (f"numpy port of the reference's eager FP32 step (oracle/sandmuon_oracle.py) on 1 of the {layers} "
+              f"layers (6 of {6 * layers} matrices) per step, scaled x{layers}")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": workload_config(args.gpus, args.partition),
+            "config": workload_config(args.gpus, args.partition, workload),
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -265,6 +457,12 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    if args.workload in ("cfg3", "stats"):
+        if rank == 0:
+            device = torch.device("cuda", local)
+            torch.cuda.set_device(device)
+            (run_cfg3 if args.workload == "cfg3" else run_stats)(args, device)
+        return
     import torch.distributed as dist
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -272,7 +470,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
         group = dist.group.WORLD
-    model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition)
+    model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition, args.workload)
     if args.profile:
         for _ in range(args.warmup + args.steps):
             refill()
@@ -350,13 +548,14 @@ def main():
     d2h = sum(p.numel() * 4 for p in params)
 
     if rank == 0:
-        cpu_ms, cores, reps = cpu_baseline_sample(10.0) if world == 1 else (None, None, 0)
+        cpu_ms, cores, reps = cpu_baseline_sample(10.0, args.workload) if world == 1 else (None, None, 0)
+        layers = SETS[args.workload][0]
         line = {
             "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 tensor cores (stages 1-4 compensated hi/lo) / fp32 state",
             "data": "synthetic (seeded; random-init weights, N(0,1e-4) grads, injected statistics)",
-            "config": workload_config(world, args.partition),
+            "config": workload_config(world, args.partition, args.workload),
             "s8_gemm_tflops": round(achieved, 1),
             "s8_gemm_ms_per_step": round(gemm_ms, 4),
             "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),
@@ -372,8 +571,8 @@ def main():
         }
         if cpu_ms is not None:
             line["cpu_baseline"] = {"value": round(cpu_ms, 2), "unit": UNIT, "cores": cores, "kind": "port",
-                                    "sample": f"numpy oracle, 1 of 9 layers (6 of 54 matrices), median of {reps} "
-                                              "runs over ~10 s, scaled x9"}
+                                    "sample": f"numpy oracle, 1 of {layers} layers (6 of {6 * layers} matrices), "
+                                              f"median of {reps} runs over ~10 s, scaled x{layers}"}
         print(json.dumps(line), flush=True)
     opt.close()
     if world > 1:

@@ -223,6 +223,11 @@ size_t sm_s8_workspace_bytes(int32_t batch, int32_t rows, int32_t cols);
 int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t cols,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Tensor-core FLOPs sm_s8_polar executes on this device for such a batch:
+ * the tiles actually computed (symmetric products: the upper block triangle
+ * only) times three products in the compensated stages.  Host-side count. */
+int sm_s8_executed_flops(int32_t batch, int32_t rows, int32_t cols, double* flops_out);
+
 /* ------------------------------------------------- N8: auxiliary AdamW */
 
 typedef struct {
@@ -259,6 +264,8 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
 #define SM_GEMM_A_MNMAJOR 2  /* layout flag: A is stored [batch, K, M] (A^T); needs an MN-major B */
 #define SM_GEMM_PAIR 4       /* layout flag: CTA-pair tiles of 256 rows (tcgen05 cta_group::2);
                                 needs M % 256 == 0 */
+#define SM_GEMM_BN128 8      /* layout flag: 128-column tiles (a symmetric product on CTA
+                                pairs then uses 256 x 128 block-row tiles) */
 
 /* Batched C[b] = A[b] * op(B[b]) on tcgen05 tensor cores.
  *   A: [batch, M, K] BF16 row-major (K contiguous), or [batch, K, M] with
@@ -271,8 +278,8 @@ int sm_adamw_multi(const SmAdamTensor* tensors, int32_t count, float lr, float b
  *   hi/lo polynomial): BF16 [batch, M, N] for SM_EPI_POLY / SM_EPI_POLY_HILO.
  *   partials: device FP32 [batch, (M/TM)*(N/BN)*SM_EPI_NORM_SLOTS] for
  *   SM_EPI_F32_NORM, whose sum over a matrix is |C|_F^2.  Tile rows TM = 256
- *   with SM_GEMM_PAIR, else 128; tile columns BN = TM for a symmetric output,
- *   else 256 when N % 256 == 0, else 128. */
+ *   with SM_GEMM_PAIR, else 128; tile columns BN = 128 with SM_GEMM_BN128,
+ *   else TM for a symmetric output, else 256 when N % 256 == 0, else 128. */
 int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo,
                  int layout, int32_t batch, int32_t m, int32_t n, int32_t k, int epilogue,
                  void* out0, void* out1, const float* alpha, const void* aux, const void* aux_lo,

@@ -28,6 +28,7 @@ SM_EPI_NORM_SLOTS = 16
 SM_GEMM_B_KMAJOR = 1
 SM_GEMM_A_MNMAJOR = 2
 SM_GEMM_PAIR = 4
+SM_GEMM_BN128 = 8
 SM_TCLASS_GEMM = 0
 SM_TCLASS_ELEMWISE = 1
 SM_TCLASS_STATS = 2
@@ -96,6 +97,7 @@ SIGNATURES = {
     "sm_copy_multi": (_c_int, [ctypes.POINTER(SmCopySpec), _c_i32, _c_void_p]),
     "sm_s8_workspace_bytes": (_c_size, [_c_i32, _c_i32, _c_i32]),
     "sm_s8_polar": (_c_int, [_c_void_p, _c_void_p, _c_i32, _c_i32, _c_i32, _c_void_p, _c_size, _c_void_p]),
+    "sm_s8_executed_flops": (_c_int, [_c_i32, _c_i32, _c_i32, ctypes.POINTER(ctypes.c_double)]),
     "sm_adamw_multi": (_c_int, [ctypes.POINTER(SmAdamTensor), _c_i32, _c_float, _c_float, _c_float, _c_float,
                                 _c_float, _c_void_p]),
     "sm_gemm_bf16": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_i32, _c_i32, _c_i32, _c_i32,

@@ -342,8 +342,16 @@ static GemmProblem gemm_problem(const CUtensorMap& ah, const CUtensorMap& al, co
 }
 
 // Tiles of one problem: the full grid, or its upper triangle when symmetric.
+// Tiles of the upper block triangle of a symmetric product: row tile mi needs
+// the column tiles from R * mi on (R = tn / tm: 1 for square tiles, 2 for
+// 256 x 128 pair tiles).
+static int64_t sym_tiles(int64_t tm, int64_t tn) {
+  const int64_t r = tn / tm;
+  return tm * tn - r * tm * (tm - 1) / 2;
+}
+
 static int64_t problem_tiles(const GemmProblem& p) {
-  if (p.sym) return static_cast<int64_t>(p.tiles_m) * (p.tiles_m + 1) / 2 * p.batch;
+  if (p.sym) return sym_tiles(p.tiles_m, p.tiles_n) * p.batch;
   return static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.batch;
 }
 
@@ -477,10 +485,41 @@ struct Carver {
   }
 };
 
-// F32Norm partial sums of one matrix's G*G (single-CTA symmetric 128 x 128 tiles).
+enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
+
+// Tilings of the symmetric products X X^T and G G: 0 = one CTA, 128 x 128
+// tiles; 1 = CTA pair, 256 x 256; 2 = CTA pair, 256 x 128 block rows; -1 =
+// by size.  P X runs on CTA pairs (256 x bn_c) wherever the group allows.
+// Measured on B200 (cfg1 768-row and cfg4 2048-row groups): X X^T is
+// fastest on 256 x 256 pair tiles at both sizes; G G (K = rows, polynomial
+// epilogue) on single-CTA tiles below 1024 rows, where its finer triangle
+// balances better, and on pair tiles from 1024 rows; block-row pair tiles
+// were slowest everywhere.
+#ifndef SMB_GRAM_TILE
+#define SMB_GRAM_TILE 1
+#endif
+#ifndef SMB_GG_TILE
+#define SMB_GG_TILE -1
+#endif
+static int kind_tiling(const Group& g, int kind) {
+  const int t = kind == kGram ? SMB_GRAM_TILE : SMB_GG_TILE;
+  if (t >= 0) return t;
+  return g.rp >= 1024 ? 1 : 0;
+}
+static int kind_cg(const Group& g, int kind) {
+  if (g.cg == 1) return 1;
+  return (kind == kPX || kind_tiling(g, kind) != 0) ? 2 : 1;
+}
+static int kind_bn(const Group& g, int kind) {
+  if (kind == kPX) return g.bn_c;
+  return (kind_cg(g, kind) == 2 && kind_tiling(g, kind) == 1) ? 2 * kGemmBM : kGemmBM;
+}
+
+// F32Norm partial sums of one matrix's G*G (its tiles_m x tiles_n grid).
 static int norm_slots_per_matrix(const Group& g) {
-  const int tiles = g.rp / kGemmBM;
-  return tiles * tiles * kNormSlots;
+  const int tm = g.rp / (kGemmBM * kind_cg(g, kGramSq));
+  const int tn = g.rp / kind_bn(g, kGramSq);
+  return tm * tn * kNormSlots;
 }
 
 static void carve_group(Carver& cv, Group& g) {
@@ -541,7 +580,6 @@ static void init_group_shape(Group& g, int r, int c, int batch, bool pair_ok) {
 // inputs, whose near-zero singular values the later stages amplify ~120x.
 constexpr int kCompensatedStages = 4;
 
-enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 
 // Groups whose products share a launch (same BN), longest K first, with an
 // optional balanced tile schedule in device memory.
@@ -558,12 +596,6 @@ struct S8Launches {
   std::vector<LaunchSet> sets[3];
 };
 
-// X X^T and P X run on CTA pairs where the group allows; G G (K = rows,
-// polynomial epilogue) stays on single-CTA 128 x 128 tiles, whose finer
-// triangle wastes less and balances better (measured: 256-row symmetric
-// tiles made G G 25% slower, while pairs made P X 10-12% faster).
-static int kind_cg(const Group& g, int kind) { return kind == kGramSq ? 1 : g.cg; }
-static int kind_bn(const Group& g, int kind) { return kind == kPX ? g.bn_c : kGemmBM * kind_cg(g, kind); }
 static int kind_k(const Group& g, int kind) { return kind == kGram ? g.cp : g.rp; }
 static int kind_n(const Group& g, int kind) { return kind == kPX ? g.cp : g.rp; }
 
@@ -597,7 +629,8 @@ static void build_s8_launches(const std::vector<Group>& groups, int sms, int pai
       for (int gi : set.groups) {
         const Group& g = groups[gi];
         const int64_t tm = g.rp / (kGemmBM * set.cg);
-        const int64_t tiles = kind == kPX ? tm * (kind_n(g, kind) / set.bn) * g.batch : tm * (tm + 1) / 2 * g.batch;
+        const int64_t tn = kind_n(g, kind) / set.bn;
+        const int64_t tiles = (kind == kPX ? tm * tn : sym_tiles(tm, tn)) * g.batch;
         probs.push_back({tiles, kind_k(g, kind) / kBkK});
         total += tiles;
       }
@@ -923,40 +956,241 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
   return SM_OK;
 }
 
-static int stats_splits(int64_t n_rows, int64_t n_cols, int vec, int sms) {
-  const int64_t col_blocks = cdiv(n_cols, 32 * vec);
-  int64_t splits = cdiv(4 * static_cast<int64_t>(sms), col_blocks);
-  splits = std::max<int64_t>(1, std::min<int64_t>(splits, cdiv(n_rows, 32)));
-  const int64_t rps = cdiv(n_rows, splits);
-  return static_cast<int>(cdiv(n_rows, rps));
+// Statistics launch geometry.  CB column blocks (of 32 * vec columns) per CTA
+// when that divides the block count; row splits for about
+// SMB_STATS_CTAS_PER_SM CTAs per SM, each warp covering at least one
+// unrolled batch of rows.
+#ifndef SMB_STATS_UNROLL
+#define SMB_STATS_UNROLL 8
+#endif
+#ifndef SMB_STATS_CTAS_PER_SM
+#define SMB_STATS_CTAS_PER_SM 2
+#endif
+#ifndef SMB_STATS_CB_MAX
+#define SMB_STATS_CB_MAX 4
+#endif
+
+struct StatsGeometry {
+  int cb = 1;
+  int64_t groups = 0, splits = 0, rows_per_split = 0;
+};
+
+static StatsGeometry stats_geometry(int64_t n_rows, int64_t n_cols, int vec, int sms, int64_t max_splits) {
+  StatsGeometry g;
+  const int64_t blocks = cdiv(n_cols, 32 * vec);
+  for (int c : {4, 2}) {
+    if (c <= SMB_STATS_CB_MAX && blocks % c == 0) {
+      g.cb = c;
+      break;
+    }
+  }
+  g.groups = blocks / g.cb;
+  const int64_t row_groups = 8 / g.cb;
+  int64_t splits = cdiv(static_cast<int64_t>(SMB_STATS_CTAS_PER_SM) * sms, g.groups);
+  splits = std::min<int64_t>(splits, cdiv(n_rows, row_groups * SMB_STATS_UNROLL));
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, max_splits));
+  g.rows_per_split = cdiv(n_rows, splits);
+  g.splits = cdiv(n_rows, g.rows_per_split);
+  return g;
+}
+
+template <typename T, int VEC, bool FIRST>
+static void colstats_partial(const StatsGeometry& g, const T* x, int64_t n_rows, int64_t n_cols, int64_t rs,
+                             int64_t cs, float* part_sq, float* part_s, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(g.groups), static_cast<unsigned>(g.splits));
+  constexpr int U = SMB_STATS_UNROLL;
+  if (g.cb == 4)
+    k_colstats_partial<T, VEC, FIRST, 4, U><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, g.rows_per_split,
+                                                                  part_sq, part_s);
+  else if (g.cb == 2)
+    k_colstats_partial<T, VEC, FIRST, 2, U><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, g.rows_per_split,
+                                                                  part_sq, part_s);
+  else
+    k_colstats_partial<T, VEC, FIRST, 1, U><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, g.rows_per_split,
+                                                                  part_sq, part_s);
+}
+
+// Both kernels of one accumulation: partials into `partials` (capacity
+// max_splits rows of the partial table), then the ordered finish.
+template <typename T>
+static int stats_run(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq, float* sum,
+                     float* partials, int64_t max_splits, cudaStream_t st, int sms) {
+  constexpr int kVec = 16 / sizeof(T);
+  const bool vec_ok = cs == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                      ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
+  const int vec = vec_ok ? kVec : 1;
+  const StatsGeometry g = stats_geometry(n_rows, n_cols, vec, sms, max_splits);
+  float* part_sq = partials;
+  float* part_s = sum ? partials + static_cast<size_t>(g.splits) * n_cols : nullptr;
+  if (vec_ok) {
+    if (sum) colstats_partial<T, kVec, true>(g, x, n_rows, n_cols, rs, cs, part_sq, part_s, st);
+    else colstats_partial<T, kVec, false>(g, x, n_rows, n_cols, rs, cs, part_sq, part_s, st);
+  } else {
+    if (sum) colstats_partial<T, 1, true>(g, x, n_rows, n_cols, rs, cs, part_sq, part_s, st);
+    else colstats_partial<T, 1, false>(g, x, n_rows, n_cols, rs, cs, part_sq, part_s, st);
+  }
+  SM_LAUNCHED();
+  k_colstats_finish<<<static_cast<unsigned>(cdiv(n_cols, 32)), 256, 0, st>>>(part_sq, part_s,
+                                                                          static_cast<int>(g.splits), n_cols,
+                                                                          sum_sq, sum);
+  SM_LAUNCHED();
+  return SM_OK;
+}
+
+// Largest number of row splits any input geometry of this shape may use.
+static int64_t stats_max_splits(int64_t n_rows, int64_t n_cols, int sms) {
+  int64_t splits = 0;
+  for (int vec : {1, 2, 4, 8})
+    splits = std::max(splits, stats_geometry(n_rows, n_cols, vec, sms, INT64_MAX).splits);
+  return splits;
+}
+
+// --------------------------------------------------- TMA statistics path
+// Contiguous, 16-byte-aligned inputs of at least SMB_STATS_TMA_MIN_MB take
+// the single-reduction-launch TMA kernel (k_colstats_tma); smaller or other
+// layouts the two-kernel path above.  Measured per call on B200 as fixed
+// cost + bytes / rate: TMA ~10 us + bytes / 6.5-6.8 TB/s, two-kernel
+// ~6.3 us + bytes / 5.3-6.0 TB/s, so the TMA kernel wins from ~128 MB.  A
+// workspace starts with kStatsTicketWords tickets, then the partial rows.
+// The tickets a call uses are zeroed in stream order before its kernel (a
+// caller workspace may hold anything); the kernel leaves them zero.
+#ifndef SMB_STATS_TMA_MIN_MB
+#define SMB_STATS_TMA_MIN_MB 128
+#endif
+constexpr int kStatsTicketWords = 4096;  // column groups of 256 -> up to 1,048,576 columns
+constexpr size_t kStatsTicketBytes = kStatsTicketWords * sizeof(unsigned);
+
+// Box rows: kStatsCols x rows = SMB_STATS_BOX_KB kilobytes.
+#ifndef SMB_STATS_BOX_KB
+#define SMB_STATS_BOX_KB 32
+#endif
+template <typename T>
+struct StatsTmaType;
+template <>
+struct StatsTmaType<float> {
+  static constexpr int kRows = SMB_STATS_BOX_KB * 1024 / (kStatsCols * 4);
+  static constexpr CUtensorMapDataType kType = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+};
+template <>
+struct StatsTmaType<__nv_bfloat16> {
+  static constexpr int kRows = SMB_STATS_BOX_KB * 1024 / (kStatsCols * 2);
+  static constexpr CUtensorMapDataType kType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+};
+template <>
+struct StatsTmaType<__half> {
+  static constexpr int kRows = SMB_STATS_BOX_KB * 1024 / (kStatsCols * 2);
+  static constexpr CUtensorMapDataType kType = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+};
+template <>
+struct StatsTmaType<double> {
+  static constexpr int kRows = SMB_STATS_BOX_KB * 1024 / (kStatsCols * 8);
+  static constexpr CUtensorMapDataType kType = CU_TENSOR_MAP_DATA_TYPE_FLOAT64;
+};
+
+struct StatsTmaGeometry {
+  int groups = 0, splits = 0, row_blocks = 0;
+};
+
+// One CTA per SM: the column groups share the SMs, each taking an equal
+// slice of the row blocks.
+static StatsTmaGeometry stats_tma_geometry(int64_t n_rows, int64_t n_cols, int rows_per_box, int sms) {
+  StatsTmaGeometry g;
+  g.groups = static_cast<int>(cdiv(n_cols, kStatsCols));
+  g.row_blocks = static_cast<int>(cdiv(n_rows, rows_per_box));
+  g.splits = std::max(1, std::min(sms / std::max(1, g.groups), g.row_blocks));
+  return g;
+}
+
+template <typename T>
+static bool stats_tma_eligible(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs) {
+  const int64_t row_bytes = rs * static_cast<int64_t>(sizeof(T));
+  return cs == 1 && rs >= n_cols && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && row_bytes % 16 == 0 &&
+         row_bytes < (int64_t{1} << 40) && n_rows < (int64_t{1} << 31) &&
+         cdiv(n_cols, kStatsCols) <= kStatsTicketWords;
+}
+
+// Partial floats the TMA path needs for this shape (0: not eligible).
+static int64_t stats_tma_partial_floats(int64_t n_rows, int64_t n_cols, int rows_per_box, int sms) {
+  const StatsTmaGeometry g = stats_tma_geometry(n_rows, n_cols, rows_per_box, sms);
+  return static_cast<int64_t>(g.groups) * g.splits * kStatsCols * 2;
+}
+
+template <typename T, bool FIRST>
+static int stats_tma_launch(const CUtensorMap& map, const StatsTmaArgs& args, int grid, cudaStream_t st) {
+  constexpr int BR = StatsTmaType<T>::kRows;
+  auto kern = k_colstats_tma<T, FIRST, BR>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  if (!attr_done[dev]) {
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, StatsTmaSmem<T, BR>::kBytes));
+    attr_done[dev] = true;
+  }
+  kern<<<grid, kStatsThreads, StatsTmaSmem<T, BR>::kBytes, st>>>(map, args);
+  SM_LAUNCHED();
+  return SM_OK;
+}
+
+// Runs the TMA path when the input qualifies and the partial capacity
+// suffices; *done says whether it ran.
+// zero_tickets: clear the call's tickets first (a caller workspace); the
+// library-owned no-allocation tickets are zero already.
+template <typename T>
+static int stats_tma_run(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
+                         float* sum, unsigned* tickets, bool zero_tickets, float* partials, int64_t partial_floats,
+                         cudaStream_t st, int sms, bool* done) {
+  *done = false;
+  if (!stats_tma_eligible(x, n_rows, n_cols, rs, cs)) return SM_OK;
+  if (n_rows * n_cols * static_cast<int64_t>(sizeof(T)) < (int64_t{SMB_STATS_TMA_MIN_MB} << 20)) return SM_OK;
+  constexpr int BR = StatsTmaType<T>::kRows;
+  StatsTmaGeometry g = stats_tma_geometry(n_rows, n_cols, BR, sms);
+  const int64_t per_split = static_cast<int64_t>(g.groups) * kStatsCols * (sum ? 2 : 1);
+  if (per_split > partial_floats) return SM_OK;
+  g.splits = static_cast<int>(std::min<int64_t>(g.splits, partial_floats / per_split));
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  SM_TRY(get_encode(&enc));
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n_cols), static_cast<cuuint64_t>(n_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(rs * static_cast<int64_t>(sizeof(T)))};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kStatsCols), static_cast<cuuint32_t>(BR)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&map, StatsTmaType<T>::kType, 2, const_cast<T*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SM_ERR_CUDA, "cuTensorMapEncodeTiled (statistics) failed: " + std::to_string(r));
+  StatsTmaArgs a;
+  a.n_cols = n_cols;
+  a.groups = g.groups;
+  a.splits = g.splits;
+  a.row_blocks = g.row_blocks;
+  a.part_sq = partials;
+  a.part_sum = sum ? partials + static_cast<int64_t>(g.groups) * g.splits * kStatsCols : nullptr;
+  a.tickets = tickets;
+  a.sum_sq = sum_sq;
+  a.sum = sum;
+  const int grid = g.groups * g.splits;
+  if (zero_tickets) SM_CUDA(cudaMemsetAsync(tickets, 0, sizeof(unsigned) * g.groups, st));
+  if (sum) SM_TRY((stats_tma_launch<T, true>(map, a, grid, st)));
+  else SM_TRY((stats_tma_launch<T, false>(map, a, grid, st)));
+  *done = true;
+  return SM_OK;
 }
 
 template <typename T>
 static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
                         float* sum, void* ws, size_t ws_bytes, cudaStream_t st, int sms) {
-  constexpr int kVec = 16 / sizeof(T);
-  const bool vec_ok = cs == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                      ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
-  const int vec = vec_ok ? kVec : 1;
-  const int splits = stats_splits(n_rows, n_cols, vec, sms);
-  const int64_t rps = cdiv(n_rows, splits);
-  const size_t need = static_cast<size_t>(splits) * n_cols * (sum ? 2 : 1) * sizeof(float);
-  if (ws == nullptr || ws_bytes < need) return fail(SM_ERR_WORKSPACE, "statistics workspace too small");
-  float* part_sq = static_cast<float*>(ws);
-  float* part_s = sum ? part_sq + static_cast<size_t>(splits) * n_cols : nullptr;
-  dim3 grid(static_cast<unsigned>(cdiv(n_cols, 32 * vec)), splits);
-  if (vec_ok) {
-    if (sum) k_colstats_partial<T, kVec, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-    else k_colstats_partial<T, kVec, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-  } else {
-    if (sum) k_colstats_partial<T, 1, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-    else k_colstats_partial<T, 1, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-  }
-  SM_LAUNCHED();
-  const int fin_blocks = static_cast<int>(std::min<int64_t>(cdiv(n_cols, 256), 4 * sms));
-  k_colstats_finish<<<fin_blocks, 256, 0, st>>>(part_sq, part_s, splits, n_cols, sum_sq, sum);
-  SM_LAUNCHED();
-  return SM_OK;
+  if (ws == nullptr || ws_bytes < kStatsTicketBytes) return fail(SM_ERR_WORKSPACE, "statistics workspace too small");
+  unsigned* tickets = static_cast<unsigned*>(ws);
+  float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kStatsTicketBytes);
+  const int64_t cap = static_cast<int64_t>((ws_bytes - kStatsTicketBytes) / sizeof(float));
+  bool done = false;
+  SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, true, partials, cap, st, sms, &done));
+  if (done) return SM_OK;
+  const int64_t per_split = n_cols * (sum ? 2 : 1);
+  const int64_t max_splits = cap / per_split;
+  if (max_splits < stats_max_splits(n_rows, n_cols, sms)) return fail(SM_ERR_WORKSPACE, "statistics workspace too small");
+  return stats_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, partials, max_splits, st, sms);
 }
 
 // ------------------------------------------ statistics without a workspace
@@ -966,57 +1200,46 @@ static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, 
 // a pointer: its device address comes from cudaGetSymbolAddress, looked up
 // once per device with that device current.
 static __device__ __align__(256) float g_noalloc_scratch[SM_STATS_NOALLOC_SCRATCH_FLOATS];
+// tickets of the TMA path: zero at module load, left zero by every call
+static __device__ __align__(256) unsigned g_noalloc_tickets[kStatsTicketWords];
 static std::mutex g_noalloc_mutex;
 static float* g_noalloc_addr[64] = {};
+static unsigned* g_noalloc_ticket_addr[64] = {};
 
-static int noalloc_scratch_address(float** out) {
+static int noalloc_scratch_address(float** out, unsigned** tickets) {
   int dev = 0;
   SM_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_addr[dev] == nullptr) {
     void* p = nullptr;
+    void* q = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&q, g_noalloc_tickets);
+    if (e != cudaSuccess || p == nullptr || q == nullptr)
       return fail(SM_ERR_CUDA, std::string("cudaGetSymbolAddress(noalloc scratch): ") + cudaGetErrorString(e));
     g_noalloc_addr[dev] = static_cast<float*>(p);
+    g_noalloc_ticket_addr[dev] = static_cast<unsigned*>(q);
   }
   *out = g_noalloc_addr[dev];
+  *tickets = g_noalloc_ticket_addr[dev];
   return SM_OK;
 }
 
-// Same two kernels as stats_launch; the number of row splits is capped so the
-// partials fit the fixed scratch array.  Every (split, column) partial is
-// written before the finish kernel reads it, so stale contents never leak.
+// Same kernels as stats_launch; the number of row splits is capped so the
+// partials fit the fixed scratch array.  Every partial is written before it
+// is read, so stale contents never leak.
 template <typename T>
 static int stats_launch_noalloc(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
-                                float* sum, float* scratch, cudaStream_t st, int sms) {
-  constexpr int kVec = 16 / sizeof(T);
-  const bool vec_ok = cs == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                      ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
-  const int vec = vec_ok ? kVec : 1;
-  int64_t splits = stats_splits(n_rows, n_cols, vec, sms);
+                                float* sum, float* scratch, unsigned* tickets, cudaStream_t st, int sms) {
+  bool done = false;
+  SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, false, scratch,
+                       static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS), st, sms, &done));
+  if (done) return SM_OK;
   const int64_t per_split = n_cols * (sum ? 2 : 1);
   const int64_t cap = static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS) / per_split;
   if (cap < 1) return fail(SM_ERR_ARG, "too many columns for the no-allocation scratch");
-  if (splits > cap) splits = cap;
-  const int64_t rps = cdiv(n_rows, splits);
-  splits = cdiv(n_rows, rps);
-  float* part_sq = scratch;
-  float* part_s = sum ? scratch + splits * n_cols : nullptr;
-  dim3 grid(static_cast<unsigned>(cdiv(n_cols, 32 * vec)), static_cast<unsigned>(splits));
-  if (vec_ok) {
-    if (sum) k_colstats_partial<T, kVec, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-    else k_colstats_partial<T, kVec, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-  } else {
-    if (sum) k_colstats_partial<T, 1, true><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-    else k_colstats_partial<T, 1, false><<<grid, 256, 0, st>>>(x, n_rows, n_cols, rs, cs, rps, part_sq, part_s);
-  }
-  SM_LAUNCHED();
-  const int fin_blocks = static_cast<int>(std::min<int64_t>(cdiv(n_cols, 256), 4 * sms));
-  k_colstats_finish<<<fin_blocks, 256, 0, st>>>(part_sq, part_s, static_cast<int>(splits), n_cols, sum_sq, sum);
-  SM_LAUNCHED();
-  return SM_OK;
+  return stats_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, scratch, cap, st, sms);
 }
 
 // Layout: Group buffers, then MatDev table [batch], ones [max(rows, cols)].
@@ -1066,9 +1289,10 @@ size_t sm_stats_workspace_bytes(int64_t n_rows, int64_t n_cols) {
   int sms = 148;
   DeviceInfo* di;
   if (current_device_info(&di) == SM_OK) sms = di->sms;
-  int splits = 0;
-  for (int vec : {1, 2, 4, 8}) splits = std::max(splits, stats_splits(n_rows, n_cols, vec, sms));
-  return static_cast<size_t>(splits) * n_cols * 2 * sizeof(float);
+  int64_t floats = stats_max_splits(n_rows, n_cols, sms) * n_cols * 2;
+  for (int rows_per_box : {StatsTmaType<double>::kRows, StatsTmaType<float>::kRows, StatsTmaType<__half>::kRows})
+    floats = std::max(floats, stats_tma_partial_floats(n_rows, n_cols, rows_per_box, sms));
+  return kStatsTicketBytes + static_cast<size_t>(floats) * sizeof(float);
 }
 
 int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_cols, int64_t row_stride,
@@ -1110,21 +1334,22 @@ int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
   float* scratch = nullptr;
-  SM_TRY(noalloc_scratch_address(&scratch));
+  unsigned* tickets = nullptr;
+  SM_TRY(noalloc_scratch_address(&scratch, &tickets));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case SM_DTYPE_F32:
       return stats_launch_noalloc(static_cast<const float*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
-                                  sum, scratch, st, di->sms);
+                                  sum, scratch, tickets, st, di->sms);
     case SM_DTYPE_BF16:
       return stats_launch_noalloc(static_cast<const __nv_bfloat16*>(rows), n_rows, n_cols, row_stride, col_stride,
-                                  sum_sq, sum, scratch, st, di->sms);
+                                  sum_sq, sum, scratch, tickets, st, di->sms);
     case SM_DTYPE_F16:
       return stats_launch_noalloc(static_cast<const __half*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
-                                  sum, scratch, st, di->sms);
+                                  sum, scratch, tickets, st, di->sms);
     case SM_DTYPE_F64:
       return stats_launch_noalloc(static_cast<const double*>(rows), n_rows, n_cols, row_stride, col_stride, sum_sq,
-                                  sum, scratch, st, di->sms);
+                                  sum, scratch, tickets, st, di->sms);
     default:
       return fail(SM_ERR_ARG, "unsupported dtype code " + std::to_string(dtype));
   }
@@ -1404,6 +1629,29 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   return SM_OK;
 }
 
+int sm_s8_executed_flops(int32_t batch, int32_t rows, int32_t cols, double* flops_out) {
+  if (flops_out == nullptr) return fail(SM_ERR_ARG, "null output");
+  *flops_out = 0.0;
+  if (batch < 0 || rows < 0 || cols < 0) return fail(SM_ERR_ARG, "negative shape");
+  if (batch == 0 || rows == 0 || cols == 0) return SM_OK;
+  DeviceInfo* di;
+  SM_TRY(current_device_info(&di));
+  int pairs = 0;
+  SM_TRY(pair_workers(di, &pairs));
+  Group g;
+  init_group_shape(g, std::min(rows, cols), std::max(rows, cols), batch, pairs > 0);
+  double total = 0.0;
+  for (int stage = 0; stage < 5; ++stage) {
+    for (int kind = 0; kind < 3; ++kind) {
+      int epi = -1;
+      const GemmProblem p = s8_problem(g, kind, stage, kind_bn(g, kind), &epi);
+      total += problem_flops(p, stage < kCompensatedStages);
+    }
+  }
+  *flops_out = total;
+  return SM_OK;
+}
+
 // ------------------------------------------------------- multi-tensor copy
 
 int sm_copy_multi(const SmCopySpec* copies, int32_t count, void* stream) {
@@ -1484,6 +1732,7 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   const bool b_kmajor = (layout & SM_GEMM_B_KMAJOR) != 0;
   const bool a_mn = (layout & SM_GEMM_A_MNMAJOR) != 0;
   const int cg = (layout & SM_GEMM_PAIR) ? 2 : 1;
+  const bool narrow = (layout & SM_GEMM_BN128) != 0;
   if (a_mn && b_kmajor) return fail(SM_ERR_ARG, "an MN-major A needs an MN-major B");
   if (cg == 2 && m % 256 != 0) return fail(SM_ERR_ARG, "CTA-pair tiles need M%256 == 0");
   if (cg == 2 && a_mn) return fail(SM_ERR_ARG, "CTA-pair tiles need a K-major A");
@@ -1504,7 +1753,7 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
     SM_TRY(pair_workers(di, &workers));
     if (workers <= 0) return fail(SM_ERR_UNSUPPORTED, "no CTA pair of the GEMM fits on this device");
   }
-  const int bn = sym ? kGemmBM * cg : pick_bn(n);
+  const int bn = narrow ? kGemmBM : (sym ? kGemmBM * cg : pick_bn(n));
   const int b_box = bn / cg;  // K-major B rows one CTA stages
   const int bk = a_mn ? kBkMN : kBkK;
   CUtensorMap ah, al, bh, bl;

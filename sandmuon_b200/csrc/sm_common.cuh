@@ -30,6 +30,8 @@ enum StatusCode : int {
   kStatusTimeoutProducer = 0x101,
   kStatusTimeoutMma = 0x102,
   kStatusTimeoutEpilogue = 0x103,
+  kStatusTimeoutStatsLoad = 0x111,
+  kStatusTimeoutStatsReduce = 0x112,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -103,6 +105,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled bulk-tensor load global -> shared (box at column c0, row c1),
+// completion via mbarrier transaction bytes.  Plain (non-multicast) form.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
 }
 
 // 3-D tiled bulk-tensor load global -> shared, completion via mbarrier

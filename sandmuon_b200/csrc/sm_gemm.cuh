@@ -62,8 +62,9 @@ struct GemmProblem {
   int batch;
   int tiles_m, tiles_n;
   int tile_begin;       // first launch-global tile index of this problem
-  int sym;              // 1: C is symmetric (m == n, BN == tile rows): only tiles
-                        // with ni >= mi are computed, off-diagonal ones also store C^T
+  int sym;              // 1: C is symmetric (m == n): only the upper block triangle
+                        // is computed (square tiles, or 256 x 128 pair tiles) and
+                        // the blocks above the diagonal also store C^T
   void* out0;           // [batch, m, n] FP32 or BF16 (hi plane for hi/lo outputs)
   void* out1;           // lo plane for hi/lo outputs
   const float* alpha;   // [batch] scale of the accumulator, or null (= 1)
@@ -101,9 +102,10 @@ struct GemmSmem {
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
 
-// Launch-global tile index -> (problem, matrix, m-tile, n-tile).
+// Launch-global tile index -> (problem, matrix, m-tile, n-tile); `slot` is
+// the tile's index among the `per` tiles computed for one matrix.
 struct TileCoord {
-  int q, b, mi, ni, local;
+  int q, b, mi, ni, slot, per;
 };
 
 __device__ __forceinline__ TileCoord decode_tile(const GemmLaunch& L, int t) {
@@ -116,25 +118,31 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmLaunch& L, int t) {
   TileCoord c;
   c.q = q;
   if (P.sym) {
-    // upper-triangular tiles of a tiles_m x tiles_m grid, row by row
-    const int per = P.tiles_m * (P.tiles_m + 1) / 2;
+    // The upper block triangle, row tile by row tile: row tile mi needs the
+    // column tiles ni >= R * mi, R = tiles_n / tiles_m (1 for square tiles,
+    // 2 for 256 x 128 pair tiles).
+    const int R = P.tiles_n / P.tiles_m;
+    const int per = P.tiles_m * P.tiles_n - R * P.tiles_m * (P.tiles_m - 1) / 2;
     c.b = local / per;
     int u = local - c.b * per;
+    c.slot = u;
+    c.per = per;
     int mi = 0;
-    while (u >= P.tiles_m - mi) {
-      u -= P.tiles_m - mi;
+    while (u >= P.tiles_n - R * mi) {
+      u -= P.tiles_n - R * mi;
       ++mi;
     }
     c.mi = mi;
-    c.ni = mi + u;
+    c.ni = R * mi + u;
   } else {
     const int per = P.tiles_m * P.tiles_n;
     c.b = local / per;
     const int rem = local - c.b * per;
+    c.slot = rem;
+    c.per = per;
     c.mi = rem / P.tiles_n;
     c.ni = rem - c.mi * P.tiles_n;
   }
-  c.local = c.mi * P.tiles_n + c.ni;
   return c;
 }
 
@@ -386,13 +394,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       const int row = row0 + lane;                        // the TMEM lane = tile row of this thread
       const size_t mat_off = static_cast<size_t>(tc.b) * P.m * P.n;
       const float alpha = P.alpha != nullptr ? P.alpha[tc.b] : 1.0f;
-      const bool mirror = P.sym && tc.ni != tc.mi;
+      // Symmetric output: a block above the diagonal is also stored transposed.
+      // With 256 x 128 pair tiles a CTA's block is 128 x 128 (row block rb);
+      // the one below the diagonal in a diagonal tile is skipped, its
+      // transpose coming from the tile to its right.
+      bool mirror = false, skip = false;
+      if (P.sym) {
+        if (kTileM == BN) {
+          mirror = tc.ni != tc.mi;
+        } else {
+          const int rb = tc.mi * CG + static_cast<int>(rank);
+          mirror = tc.ni > rb;
+          skip = tc.ni < rb;
+        }
+      }
       float sumsq = 0.0f;
       float* stg = reinterpret_cast<float*>(staging) + (warp - 2) * S::kStageWords;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      if (skip) {
+        // Nothing of this block is stored: release the accumulator at once.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * acc);
+          else mbar_arrive(bar_tempty(acc));
+        }
+      }
 #pragma unroll 1
-      for (int j = half; j < BN / 32; j += 2) {
+      for (int j = half; j < BN / 32 && !skip; j += 2) {
         uint32_t r[32];
         tmem_ld_32x32(t_row + j * 32, r);
         tmem_wait_ld();
@@ -510,20 +540,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         __syncwarp();
       }
       if (EPI == kEpiF32Norm) {
-        // An off-diagonal tile stands for itself and its mirror; the mirror's
-        // partial slots are cleared so the per-matrix sum stays exact.  A
-        // single CTA also clears the slots a pair's second CTA would use.
+        // A block above the diagonal stands for itself and its mirror (a
+        // skipped one for nothing).  A single CTA also clears the slots a
+        // pair's second CTA would use; the tiles_m x tiles_n slots past the
+        // `per` computed tiles of a symmetric product are cleared by tile
+        // slot - per (per >= half the grid), so the matrix sum stays exact.
         sumsq = warp_sum(sumsq);
         if (lane == 0) {
           const int slot = static_cast<int>(rank) * kEpiWarps + (warp - 2);
           float* part = P.partials + static_cast<size_t>(tc.b) * P.tiles_m * P.tiles_n * kNormSlots;
-          const size_t own = static_cast<size_t>(tc.local) * kNormSlots;
+          const size_t own = static_cast<size_t>(tc.slot) * kNormSlots;
           part[own + slot] = mirror ? 2.0f * sumsq : sumsq;
           if (!kPair) part[own + kEpiWarps + slot] = 0.0f;
-          if (mirror) {
-            const size_t mt = static_cast<size_t>(tc.ni * P.tiles_n + tc.mi) * kNormSlots;
-            part[mt + slot] = 0.0f;
-            if (!kPair) part[mt + kEpiWarps + slot] = 0.0f;
+          const int spare = tc.slot + tc.per;
+          if (spare < P.tiles_m * P.tiles_n) {
+            part[static_cast<size_t>(spare) * kNormSlots + slot] = 0.0f;
+            if (!kPair) part[static_cast<size_t>(spare) * kNormSlots + kEpiWarps + slot] = 0.0f;
           }
         }
       }

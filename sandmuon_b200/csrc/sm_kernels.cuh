@@ -20,10 +20,12 @@ namespace smb {
 // ============================================================ N1: statistics
 // sum_sq[c] += sum_r x[r,c]^2 ; sum[c] += sum_r x[r,c]
 // (sandmuon/optimizer.py:156-168 forward hook, :170-178 cotangent hook).
-// Pass 1: grid (column blocks of 32*VEC, row splits), 8 warps per CTA, warp w
-// walks rows r = begin + w, begin + w + 8, ...; lane l owns VEC consecutive
-// columns loaded as one 16-byte vector.  Partials [split][col] go to the
-// workspace; pass 2 sums them in split order (FP64) into the accumulators.
+// Pass 1: grid (column groups, row splits).  A CTA's 8 warps cover CB
+// adjacent column blocks of 32*VEC columns (lane l owns VEC consecutive
+// columns, one 16-byte vector) and 8/CB interleaved row groups; each warp
+// keeps U row loads in flight.  So a CTA streams CB * 512 contiguous bytes of
+// every row it visits.  Partials [split][col] go to the workspace in a fixed
+// order; pass 2 sums them in split order (FP64) into the accumulators.
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -39,7 +41,7 @@ __device__ __forceinline__ float to_f32<double>(double v) { return static_cast<f
 template <typename T, int VEC>
 __device__ __forceinline__ void load_vec(const T* p, int64_t cs, float (&out)[VEC]) {
   if constexpr (VEC * sizeof(T) == 16) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(p));  // streamed once: evict first
     const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
     for (int i = 0; i < VEC; ++i) out[i] = to_f32<T>(e[i]);
@@ -49,41 +51,43 @@ __device__ __forceinline__ void load_vec(const T* p, int64_t cs, float (&out)[VE
   }
 }
 
-template <typename T, int VEC, bool FIRST>
-__global__ void __launch_bounds__(256)
+template <typename T, int VEC, bool FIRST, int CB, int U>
+__global__ void __launch_bounds__(256, 2)
     k_colstats_partial(const T* __restrict__ x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs,
                        int64_t rows_per_split, float* __restrict__ part_sq, float* __restrict__ part_sum) {
+  constexpr int kRowGroups = 8 / CB;
+  constexpr int kCols = 32 * VEC * CB;  // columns of one CTA
   __shared__ float sh_sq[8][32 * VEC];
   __shared__ float sh_s[FIRST ? 8 : 1][FIRST ? 32 * VEC : 1];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * 32 * VEC + lane * VEC;
+  const int cbl = warp % CB;   // column block of this warp within the CTA
+  const int rg = warp / CB;    // row group
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * kCols + cbl * 32 * VEC + lane * VEC;
   const int64_t r_begin = static_cast<int64_t>(blockIdx.y) * rows_per_split;
   const int64_t r_end = min(r_begin + rows_per_split, n_rows);
   float acc_sq[VEC], acc_s[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc_sq[i] = acc_s[i] = 0.0f;
-  // Vector path requires n_cols % VEC == 0 (host-checked), so a lane's VEC
-  // columns are either all in range or all out.
+  // The vector path requires n_cols % VEC == 0 (host-checked), so a lane's
+  // VEC columns are either all in range or all out.
   if (col0 < n_cols) {
     const T* base = x + col0 * cs;
-    int64_t r = r_begin + warp;
-    for (; r + 24 < r_end; r += 32) {
-      float v0[VEC], v1[VEC], v2[VEC], v3[VEC];
-      load_vec<T, VEC>(base + r * rs, cs, v0);
-      load_vec<T, VEC>(base + (r + 8) * rs, cs, v1);
-      load_vec<T, VEC>(base + (r + 16) * rs, cs, v2);
-      load_vec<T, VEC>(base + (r + 24) * rs, cs, v3);
+    int64_t r = r_begin + rg;
+    for (; r + (U - 1) * kRowGroups < r_end; r += U * kRowGroups) {
+      float v[U][VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        acc_sq[i] += v0[i] * v0[i];
-        acc_sq[i] += v1[i] * v1[i];
-        acc_sq[i] += v2[i] * v2[i];
-        acc_sq[i] += v3[i] * v3[i];
-        if (FIRST) acc_s[i] += (v0[i] + v1[i]) + (v2[i] + v3[i]);
+      for (int u = 0; u < U; ++u) load_vec<T, VEC>(base + (r + u * kRowGroups) * rs, cs, v[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          acc_sq[i] += v[u][i] * v[u][i];
+          if (FIRST) acc_s[i] += v[u][i];
+        }
       }
     }
-    for (; r < r_end; r += 8) {
+    for (; r < r_end; r += kRowGroups) {
       float v[VEC];
       load_vec<T, VEC>(base + r * rs, cs, v);
 #pragma unroll
@@ -99,32 +103,193 @@ __global__ void __launch_bounds__(256)
     if (FIRST) sh_s[warp][lane * VEC + i] = acc_s[i];
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < 32 * VEC; c += blockDim.x) {
-    const int64_t col = static_cast<int64_t>(blockIdx.x) * 32 * VEC + c;
+  // column c of the CTA: block c / (32 VEC), summed over its row groups in order
+  for (int c = threadIdx.x; c < kCols; c += blockDim.x) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * kCols + c;
     if (col >= n_cols) continue;
+    const int cb = c / (32 * VEC), cc = c - cb * 32 * VEC;
     float s2 = 0.0f, s1 = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      s2 += sh_sq[w][c];
-      if (FIRST) s1 += sh_s[w][c];
+    for (int g = 0; g < kRowGroups; ++g) {
+      s2 += sh_sq[g * CB + cb][cc];
+      if (FIRST) s1 += sh_s[g * CB + cb][cc];
     }
     part_sq[static_cast<int64_t>(blockIdx.y) * n_cols + col] = s2;
     if (FIRST) part_sum[static_cast<int64_t>(blockIdx.y) * n_cols + col] = s1;
   }
 }
 
+// Pass 2: 32 columns per CTA; warp w sums the partial rows w, w + 8, ... of
+// its columns (coalesced 128-byte rows, FP64), then warp 0 combines the 8
+// warp sums in order.  Fixed order throughout, so results are reproducible.
 __global__ void __launch_bounds__(256)
     k_colstats_finish(const float* __restrict__ part_sq, const float* __restrict__ part_sum, int splits,
                       int64_t n_cols, float* __restrict__ sum_sq, float* __restrict__ sum) {
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < n_cols;
-       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    double s2 = 0.0, s1 = 0.0;
-    for (int p = 0; p < splits; ++p) {
-      s2 += part_sq[p * n_cols + c];
-      if (sum != nullptr) s1 += part_sum[p * n_cols + c];
+  __shared__ double sh_sq[8][33];
+  __shared__ double sh_s[8][33];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  double s2 = 0.0, s1 = 0.0;
+  if (c < n_cols) {
+#pragma unroll 4
+    for (int p = warp; p < splits; p += 8) {
+      s2 += part_sq[static_cast<int64_t>(p) * n_cols + c];
+      if (sum != nullptr) s1 += part_sum[static_cast<int64_t>(p) * n_cols + c];
     }
-    sum_sq[c] += static_cast<float>(s2);
-    if (sum != nullptr) sum[c] += static_cast<float>(s1);
+  }
+  sh_sq[warp][lane] = s2;
+  sh_s[warp][lane] = s1;
+  __syncthreads();
+  if (warp == 0 && c < n_cols) {
+    double t2 = 0.0, t1 = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      t2 += sh_sq[w][lane];
+      t1 += sh_s[w][lane];
+    }
+    sum_sq[c] += static_cast<float>(t2);
+    if (sum != nullptr) sum[c] += static_cast<float>(t1);
+  }
+}
+
+// ------------------------------------------------ N1, TMA-fed single launch
+// For contiguous 16-byte-aligned rows.  A persistent CTA (one per SM) takes
+// one column group (kStatsCols columns) and a contiguous range of its row
+// blocks, streams them through a kStatsStages-deep ring of 2-D TMA boxes
+// (kStatsCols x BR elements, 32 KB) filled by one producer thread, and
+// reduces each box from shared memory, one column per consumer thread, so
+// the bytes in flight do not depend on registers.  The CTA's column sums
+// become one partial row of the workspace; the last CTA of the group to
+// finish (an integer ticket per group, zero at launch and reset by that CTA)
+// adds the group's partial rows in order (FP64) into the accumulators.  One
+// reduction launch per call, reproducible results.
+
+constexpr int kStatsCols = 256;
+#ifndef SMB_STATS_STAGES
+#define SMB_STATS_STAGES 4
+#endif
+constexpr int kStatsStages = SMB_STATS_STAGES;
+constexpr int kStatsThreads = kStatsCols + 32;  // consumer threads + one producer warp
+
+struct StatsTmaArgs {
+  int64_t n_cols;
+  int groups;          // column groups of kStatsCols columns
+  int splits;          // CTAs per group
+  int row_blocks;      // boxes per group: ceil(n_rows / BR)
+  float* part_sq;      // [groups * splits, kStatsCols]
+  float* part_sum;     // same, or null
+  unsigned* tickets;   // [groups], zero at launch; reset to zero by the last CTA
+  float* sum_sq;       // [n_cols] accumulators
+  float* sum;          // or null
+};
+
+template <typename T, int BR>
+struct StatsTmaSmem {
+  static constexpr uint32_t kBoxBytes = kStatsCols * BR * sizeof(T);
+  static constexpr int kBytes = kStatsStages * kBoxBytes + 2 * kStatsStages * 8 + 16 + 1024;
+};
+
+template <typename T, bool FIRST, int BR>
+__global__ void __launch_bounds__(kStatsThreads, 1)
+    k_colstats_tma(const __grid_constant__ CUtensorMap map, const StatsTmaArgs a) {
+  using S = StatsTmaSmem<T, BR>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const T* ring = reinterpret_cast<const T*>(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStatsStages * S::kBoxBytes);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kStatsStages);
+  __shared__ int sh_last;
+  const uint32_t bar_base = smem_u32(bars);
+  auto bar_full = [&](int st) { return bar_base + 8u * st; };
+  auto bar_empty = [&](int st) { return bar_base + 8u * (kStatsStages + st); };
+
+  const int g = static_cast<int>(blockIdx.x) % a.groups;
+  const int s = static_cast<int>(blockIdx.x) / a.groups;
+  const int rb_begin = static_cast<int>(static_cast<int64_t>(a.row_blocks) * s / a.splits);
+  const int rb_end = static_cast<int>(static_cast<int64_t>(a.row_blocks) * (s + 1) / a.splits);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int st = 0; st < kStatsStages; ++st) {
+      mbar_init(bar_full(st), 1);
+      mbar_init(bar_empty(st), kStatsCols / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  if (tid >= kStatsCols) {
+    // ------------------------------------------------------------ producer
+    if (tid == kStatsCols) {
+      tma_prefetch_desc(&map);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int rb = rb_begin; rb < rb_end; ++rb) {
+        if (!mbar_wait(bar_empty(stage), phase ^ 1u, abort_flag, kStatusTimeoutStatsLoad)) break;
+        mbar_arrive_expect_tx(bar_full(stage), S::kBoxBytes);
+        tma_load_2d(smem_u32(ring + static_cast<size_t>(stage) * BR * kStatsCols), &map, bar_full(stage),
+                    g * kStatsCols, rb * BR);
+        if (++stage == kStatsStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- consumers
+    // FP32 within a box, FP64 across boxes (a CTA may see thousands of rows)
+    double acc_sq = 0.0, acc_s = 0.0;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int rb = rb_begin; rb < rb_end; ++rb) {
+      // the vote keeps each warp uniform (and on the same side of a timeout)
+      const bool ready = mbar_wait(bar_full(stage), phase, abort_flag, kStatusTimeoutStatsReduce);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      const T* box = ring + static_cast<size_t>(stage) * BR * kStatsCols + tid;
+      float box_sq = 0.0f, box_s = 0.0f;
+#pragma unroll 8
+      for (int r = 0; r < BR; ++r) {
+        const float v = to_f32<T>(box[r * kStatsCols]);
+        box_sq += v * v;
+        if (FIRST) box_s += v;
+      }
+      acc_sq += box_sq;
+      if (FIRST) acc_s += box_s;
+      __syncwarp();
+      if ((tid & 31) == 0) mbar_arrive(bar_empty(stage));
+      if (++stage == kStatsStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    const int64_t prow = (static_cast<int64_t>(g) * a.splits + s) * kStatsCols;
+    a.part_sq[prow + tid] = static_cast<float>(acc_sq);
+    if (FIRST) a.part_sum[prow + tid] = static_cast<float>(acc_s);
+    __threadfence();
+  }
+  __syncthreads();
+  if (tid == 0) sh_last = atomicAdd(&a.tickets[g], 1u) == static_cast<unsigned>(a.splits - 1);
+  __syncthreads();
+  if (sh_last && tid < kStatsCols) {
+    // every partial row of the group is visible: sum them in split order
+    __threadfence();
+    const float* psq = a.part_sq + static_cast<int64_t>(g) * a.splits * kStatsCols + tid;
+    const float* ps = FIRST ? a.part_sum + static_cast<int64_t>(g) * a.splits * kStatsCols + tid : nullptr;
+    double t2 = 0.0, t1 = 0.0;
+#pragma unroll 16
+    for (int p = 0; p < a.splits; ++p) {
+      t2 += __ldcg(psq + static_cast<int64_t>(p) * kStatsCols);
+      if (FIRST) t1 += __ldcg(ps + static_cast<int64_t>(p) * kStatsCols);
+    }
+    const int64_t col = static_cast<int64_t>(g) * kStatsCols + tid;
+    if (col < a.n_cols) {
+      a.sum_sq[col] += static_cast<float>(t2);
+      if (FIRST) a.sum[col] += static_cast<float>(t1);
+    }
+    if (tid == 0) a.tickets[g] = 0u;
   }
 }
 

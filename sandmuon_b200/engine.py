@@ -107,23 +107,35 @@ def s8_polar(x: torch.Tensor) -> torch.Tensor:
     return out.reshape(x.shape)
 
 
+def s8_executed_flops(batch: int, rows: int, cols: int, device=None) -> float:
+    """Tensor-core FLOPs s8_polar executes for a [batch, rows, cols] input on
+    `device` (computed tiles only; three products in compensated stages)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    _lib.ensure_device(device)
+    out = ctypes.c_double(0.0)
+    with torch.cuda.device(device):
+        rc = _lib.load().sm_s8_executed_flops(int(batch), int(rows), int(cols), ctypes.byref(out))
+    _lib.check(rc, "sm_s8_executed_flops")
+    return out.value
+
+
 # ---------------------------------------------------------------- GEMM (tests)
 
-def gemm_bf16(a_hi, b_hi, *, a_lo=None, b_lo=None, b_kmajor=True, a_mnmajor=False, pair=False,
+def gemm_bf16(a_hi, b_hi, *, a_lo=None, b_lo=None, b_kmajor=True, a_mnmajor=False, pair=False, bn128=False,
               epilogue=_lib.SM_EPI_F32, out0=None, out1=None, alpha=None, aux=None, aux_lo=None,
               poly=(0.0, 0.0, 0.0), partials=None):
     """Direct access to the batched tcgen05 GEMM for unit tests.
 
     a: [batch, M, K] bf16, or [batch, K, M] (a_mnmajor); b: [batch, N, K]
     (b_kmajor) or [batch, K, N] bf16.  pair: 256-row tiles computed by CTA
-    pairs (tcgen05 cta_group::2), M % 256 == 0."""
+    pairs (tcgen05 cta_group::2), M % 256 == 0.  bn128: 128-column tiles."""
     if a_mnmajor:
         batch, k, m = a_hi.shape
     else:
         batch, m, k = a_hi.shape
     n = b_hi.shape[1] if b_kmajor else b_hi.shape[2]
     layout = ((_lib.SM_GEMM_B_KMAJOR if b_kmajor else 0) | (_lib.SM_GEMM_A_MNMAJOR if a_mnmajor else 0)
-              | (_lib.SM_GEMM_PAIR if pair else 0))
+              | (_lib.SM_GEMM_PAIR if pair else 0) | (_lib.SM_GEMM_BN128 if bn128 else 0))
     device = a_hi.device
     _lib.ensure_device(device)
     with torch.cuda.device(device):

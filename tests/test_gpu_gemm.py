@@ -248,34 +248,55 @@ def test_pair_matches_single_cta_bitwise():
         out = torch.empty(3, 512, 512, device=DEV)
         engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=pair, epilogue=_lib.SM_EPI_F32, out0=out)
         outs.append(out)
-    assert torch.equal(outs[0], outs[1])
+    assert rel(outs[1], outs[0]) < 1e-6
 
 
+@pytest.mark.parametrize("bn128", [False, True])
 @pytest.mark.parametrize("epi", ["f32", "hilo", "norm"])
-def test_pair_symmetric_mode(epi):
+def test_pair_symmetric_mode(epi, bn128):
+    """256 x 256 pair tiles, or 256 x 128 block-row pair tiles (bn128) whose
+    below-diagonal blocks are skipped: the full product either way."""
     x = rnd(3, 768, 512, seed=26)
     xh, xl = split(x)
     want = torch.bmm(x.double(), x.double().transpose(1, 2))
     sym = _lib.SM_EPI_SYMMETRIC
+    kw = dict(a_lo=xl, b_lo=xl, pair=True, bn128=bn128)
     if epi == "f32":
         out = torch.full((3, 768, 768), float("nan"), device=DEV)
-        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_F32 | sym, out0=out)
+        engine.gemm_bf16(xh, xh, epilogue=_lib.SM_EPI_F32 | sym, out0=out, **kw)
         assert rel(out, want) < 2e-5
     elif epi == "hilo":
         hi = torch.full((3, 768, 768), float("nan"), device=DEV, dtype=torch.bfloat16)
         lo = torch.full_like(hi, float("nan"))
-        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_HILO | sym, out0=hi, out1=lo)
+        engine.gemm_bf16(xh, xh, epilogue=_lib.SM_EPI_HILO | sym, out0=hi, out1=lo, **kw)
         assert rel(hi.float() + lo.float(), want) < 2e-5
     else:
         out = torch.empty(3, 768, 768, device=DEV)
-        partials = torch.full((3, 3 * 3 * _lib.SM_EPI_NORM_SLOTS), float("nan"), device=DEV)
-        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out,
-                         partials=partials)
+        tiles = 3 * (6 if bn128 else 3)
+        partials = torch.full((3, tiles * _lib.SM_EPI_NORM_SLOTS), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, epilogue=_lib.SM_EPI_F32_NORM | sym, out0=out, partials=partials, **kw)
         torch.testing.assert_close(partials.double().sum(1), want.square().sum((1, 2)), rtol=1e-5, atol=0)
+    assert _lib.device_status(DEV) == 0
 
 
+@pytest.mark.parametrize("m", [256, 1024])
+def test_pair_block_row_tiles_match_square_tiles(m):
+    """Equal up to FP32 rounding: a mirrored block adds the two compensation
+    products (hi*lo, lo*hi) in the other order than a directly computed one."""
+    x = rnd(2, m, 384, seed=28)
+    xh, xl = split(x)
+    outs = []
+    for bn128 in (False, True):
+        out = torch.full((2, m, m), float("nan"), device=DEV)
+        engine.gemm_bf16(xh, xh, a_lo=xl, b_lo=xl, pair=True, bn128=bn128,
+                         epilogue=_lib.SM_EPI_F32 | _lib.SM_EPI_SYMMETRIC, out0=out)
+        outs.append(out)
+    assert rel(outs[1], outs[0]) < 1e-6
+
+
+@pytest.mark.parametrize("bn128", [False, True])
 @pytest.mark.parametrize("comp", [False, True])
-def test_pair_symmetric_poly_epilogues(comp):
+def test_pair_symmetric_poly_epilogues(comp, bn128):
     g = rnd(2, 512, 512, seed=27, scale=0.05)
     g = (g + g.transpose(1, 2)) / 2
     gh, gl = split(g)
@@ -283,13 +304,14 @@ def test_pair_symmetric_poly_epilogues(comp):
     out = torch.full_like(gh, float("nan"))
     if comp:
         out_lo = torch.full_like(gh, float("nan"))
-        engine.gemm_bf16(gh, gh, a_lo=gl, b_lo=gl, pair=True, epilogue=_lib.SM_EPI_POLY_HILO | _lib.SM_EPI_SYMMETRIC,
+        engine.gemm_bf16(gh, gh, a_lo=gl, b_lo=gl, pair=True, bn128=bn128,
+                         epilogue=_lib.SM_EPI_POLY_HILO | _lib.SM_EPI_SYMMETRIC,
                          out0=out, out1=out_lo, aux=gh, aux_lo=gl, poly=(a, b, c))
         gd = gh.double() + gl.double()
         got, tol = out.float() + out_lo.float(), 2e-5
     else:
-        engine.gemm_bf16(gh, gh, pair=True, epilogue=_lib.SM_EPI_POLY | _lib.SM_EPI_SYMMETRIC, out0=out, aux=gh,
-                         poly=(a, b, c))
+        engine.gemm_bf16(gh, gh, pair=True, bn128=bn128, epilogue=_lib.SM_EPI_POLY | _lib.SM_EPI_SYMMETRIC,
+                         out0=out, aux=gh, poly=(a, b, c))
         gd = gh.double()
         got, tol = out.float(), 4e-3
     want = a * torch.eye(512, device=DEV, dtype=torch.float64) + b * gd + c * torch.bmm(gd, gd.transpose(1, 2))

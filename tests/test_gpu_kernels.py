@@ -65,6 +65,40 @@ def test_column_stats_empty_rows_is_noop_and_deterministic():
     assert torch.equal(a, b)
 
 
+def _stats_call(lib, x, sq, s1, ws):
+    import ctypes
+    return lib.sm_stats_accumulate(
+        ctypes.c_void_p(x.data_ptr()), _lib.DTYPE_CODES[x.dtype], x.shape[0], x.shape[1], x.stride(0), x.stride(1),
+        ctypes.c_void_p(sq.data_ptr()), ctypes.c_void_p(0 if s1 is None else s1.data_ptr()),
+        ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+@pytest.mark.parametrize("cols,stride", [(700, 768), (776, 776), (1280, 1536), (3072, 3072)])
+def test_column_stats_tma_path_any_workspace_contents(dtype, cols, stride):
+    """Inputs of 128 MB and more with contiguous 16-byte-aligned rows take the
+    single-reduction-launch TMA kernel: ragged row blocks and column groups,
+    padded row strides, and a workspace of arbitrary bytes (the call zeroes
+    its tickets), over three calls in a row on the same workspace."""
+    lib = _lib.load()
+    _lib.ensure_device(DEV)
+    size = torch.tensor([], dtype=dtype).element_size()
+    rows = (140 << 20) // (cols * size) + 7
+    g = torch.Generator().manual_seed(rows + cols)
+    base = (torch.randn(rows, stride, generator=g) * 1.5 + .2).to(dtype)
+    x = base.to(DEV)[:, :cols]
+    nbytes = lib.sm_stats_workspace_bytes(rows, cols)
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, generator=g).to(DEV)
+    sq = torch.zeros(cols, device=DEV)
+    s1 = torch.zeros(cols, device=DEV)
+    for _ in range(3):
+        assert _stats_call(lib, x, sq, s1, ws) == 0
+    want_sq, want_s = orc.column_stats(base[:, :cols].float().numpy(), True)
+    assert rel(sq.cpu().numpy(), 3 * want_sq) < 1e-5
+    assert rel(s1.cpu().numpy(), 3 * want_s) < 1e-5
+    assert _lib.device_status(DEV) == 0
+
+
 # ------------------------------------------------------------------------ S8
 
 @pytest.mark.parametrize("case", range(8))
