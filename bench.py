@@ -16,7 +16,9 @@ device copy (the step zeroes them, as in training).
 
 Prints one JSON line (rank 0).  value = device ms per step, max over ranks;
 e2e = the same through the public API with pinned-host gradients/statistics
-copied in and the updated weights copied out inside the timed region.
+copied in and the updated weights copied out inside the timed region, copies
+of neighbouring steps overlapped on separate streams (e2e.serial_value: the
+same with every copy and step on one stream).
 
 Other workloads (not the contract line): cfg4 = the same step on the 24-layer
 x 2048 matrix set (144 matrices); cfg3 = the S8 sweep of BASELINE configs[3]
@@ -61,6 +63,8 @@ def parse_args():
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no CPU baseline, clock probe or e2e pass")
     ap.add_argument("--workload", choices=("cfg1", "cfg4", "cfg3", "stats"), default="cfg1")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="omit the ~10 s CPU baseline sample (tuning runs); the contract line keeps it")
     return ap.parse_args()
 
 
@@ -188,11 +192,13 @@ def make_refill(opt, stats, rows, device):
     counts = [(opt.state[opt.named_matrices[n]], key.replace("_sum", "_count").replace("a_first_count", "a_count"))
               for n, key, _ in order]
 
-    def refill(from_host=False):
-        flat.copy_(src_host if from_host else src_dev, non_blocking=True)
+    def refill(from_host=False, from_device=None):
+        src = from_device if from_device is not None else (src_host if from_host else src_dev)
+        flat.copy_(src, non_blocking=True)
         for st, key in counts:
             st[key] = rows
 
+    refill.host, refill.flat = src_host, flat
     return refill, flat.numel() * 4
 
 
@@ -204,6 +210,94 @@ def time_steps(opt, refill, steps, device):
         opt.step()
     end.record()
     torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / steps
+
+
+def e2e_serial(opt, params, host_g, refill, steps, device):
+    """Per step on one stream: pinned-host gradients and statistic sums in,
+    opt.step(), updated weights out to pinned host memory."""
+    host_w = [torch.empty(tuple(p.shape), dtype=torch.float32).pin_memory() for p in params]
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        for p, hg in zip(params, host_g):
+            p.grad.copy_(hg, non_blocking=True)
+        refill(from_host=True)
+        opt.step()
+        for p, hw in zip(params, host_w):
+            hw.copy_(p.detach(), non_blocking=True)
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / steps
+
+
+def e2e_pipelined(opt, params, host_g, refill, steps, device):
+    """The same per-step bytes and calls, overlapped across steps the way a
+    host-offloaded training loop would run them: step k+1's host-to-device
+    copy (gradients and statistic sums, copy-in stream) runs during step k's
+    optimizer step (compute stream) and step k-1's device-to-host copy of the
+    updated weights (copy-out stream).  Gradients land in two alternating
+    device buffer sets (p.grad is re-pointed each step); the updated weights
+    are first copied into one of two flat device buffers (sm_copy_multi, on
+    the compute stream) so the next step may update them while they stream
+    out.  Every step's full input and output cross PCIe inside the timed
+    region; steady-state ms per step = (last event - first event) / steps."""
+    from sandmuon_b200 import engine
+    total = sum(p.numel() for p in params)
+    compute = torch.cuda.current_stream(device)
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    grad_flat = [torch.empty(total, dtype=torch.float32, device=device) for _ in range(2)]
+    grad_sets, off = [[], []], 0
+    for p in params:
+        for s in range(2):
+            grad_sets[s].append(grad_flat[s][off:off + p.numel()].view(p.shape))
+        off += p.numel()
+    stat_host = refill.host
+    stat_dev = [torch.empty_like(refill.flat) for _ in range(2)]
+    w_flat = [torch.empty(total, dtype=torch.float32, device=device) for _ in range(2)]
+    w_views = [[], []]
+    off = 0
+    for p in params:
+        for s in range(2):
+            w_views[s].append(w_flat[s][off:off + p.numel()])
+        off += p.numel()
+    host_w = torch.empty(total, dtype=torch.float32).pin_memory()
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    grads_free, w_free = [ev(), ev()], [ev(), ev()]
+    in_ready, w_ready = [ev() for _ in range(2)], [ev() for _ in range(2)]
+    for e in grads_free + w_free:
+        e.record(compute)
+    saved = [p.grad for p in params]
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(compute)
+    for k in range(steps):
+        s = k % 2
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(grads_free[s])
+            for g, hg in zip(grad_sets[s], host_g):
+                g.copy_(hg, non_blocking=True)
+            stat_dev[s].copy_(stat_host, non_blocking=True)
+            in_ready[s].record(copy_in)
+        compute.wait_event(in_ready[s])
+        for p, g in zip(params, grad_sets[s]):
+            p.grad = g
+        refill(from_device=stat_dev[s])
+        opt.step()
+        grads_free[s].record(compute)
+        compute.wait_event(w_free[s])
+        engine.copy_multi([(v, p.detach().view(-1)) for v, p in zip(w_views[s], params)], device)
+        w_ready[s].record(compute)
+        with torch.cuda.stream(copy_out):
+            copy_out.wait_event(w_ready[s])
+            host_w.copy_(w_flat[s], non_blocking=True)
+            w_free[s].record(copy_out)
+    compute.wait_stream(copy_out)
+    end.record(compute)
+    torch.cuda.synchronize(device)
+    for p, g in zip(params, saved):
+        p.grad = g
     return start.elapsed_time(end) / steps
 
 
@@ -372,10 +466,12 @@ def run_stats(args, device):
     a_cols = [768, 768, 768, 3072]          # q (shared by k, v), o, fc in, proj in
     b_cols = [768, 768, 768, 768, 3072, 768]
     hbm = peaks()[2]
+    # --profile: one layer's 10 calls (0.4 GB FP32 inputs, > L2), plain launches only
+    layers = 1 if args.profile else 9
     for dtype in (torch.float32, torch.bfloat16):
         gen = torch.Generator(device=device).manual_seed(SEED)
         calls = []
-        for _ in range(9):
+        for _ in range(layers):
             for c in a_cols:
                 calls.append((torch.randn(n, c, generator=gen, device=device).to(dtype),
                               torch.zeros(c, device=device), torch.zeros(c, device=device)))
@@ -388,6 +484,15 @@ def run_stats(args, device):
         def one_pass():
             for x, sq, t in calls:
                 engine.accumulate_column_stats(x, sq, t)
+        if args.profile:
+            for _ in range(args.warmup + args.steps):
+                one_pass()
+            torch.cuda.synchronize(device)
+            print(json.dumps({"profile_passes": args.warmup + args.steps, "dtype": str(dtype),
+                              "hook_calls_per_pass": len(calls), "bytes_per_pass": nbytes}), flush=True)
+            del calls
+            torch.cuda.empty_cache()
+            continue
         event_ms(one_pass, max(args.warmup, 3), device)
         eager_ms = event_ms(one_pass, max(args.steps, 5), device)
         # the same launches replayed from a CUDA graph: device time without
@@ -508,25 +613,17 @@ def main():
 
     # end to end through the public API with host buffers
     params = list(opt.named_matrices.values())
-    host_w = [torch.empty(tuple(p.shape), dtype=torch.float32).pin_memory() for p in params]
     host_g = [grads_host[n] for n in opt.named_matrices]
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.monotonic()
-    start.record()
-    for _ in range(args.steps):
-        for p, hg in zip(params, host_g):
-            p.grad.copy_(hg, non_blocking=True)
-        refill(from_host=True)
-        opt.step()
-        for p, hw in zip(params, host_w):
-            hw.copy_(p.detach(), non_blocking=True)
-    end.record()
-    torch.cuda.synchronize(device)
+    e2e_serial_ms = e2e_serial(opt, params, host_g, refill, args.steps, device)
     sampler.mark(t0, time.monotonic())
-    e2e_ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        dist.barrier()
+    t0 = time.monotonic()
+    e2e_ms = e2e_pipelined(opt, params, host_g, refill, args.steps, device)
+    sampler.mark(t0, time.monotonic())
 
     # keep the GPU under the same load for ~1 s more so clocks are sampled
     t0 = time.monotonic()
@@ -535,20 +632,31 @@ def main():
     sampler.mark(t0, time.monotonic())
     clocks = sampler.summary()
 
-    vals = torch.tensor([ms, e2e_ms, timing["ms"]["gemm"], timing["gemm_flops"]], dtype=torch.float64, device=device)
+    # a bounded device-side wait that ran out makes every number above meaningless
+    from sandmuon_b200 import _lib
+    status = _lib.device_status(device)
+    if status != 0:
+        raise RuntimeError(f"a kernel reported a device-side timeout (status {status}): no bench line")
+
+    # [max: ms, e2e, gemm ms] [sum: gemm flops, gemm ms]: each rank executes only the S8
+    # work of the matrices it owns, so the per-GPU tensor rate is sum(flops) / sum(GEMM ms)
+    vals = torch.tensor([ms, e2e_ms, e2e_serial_ms, timing["ms"]["gemm"], timing["gemm_flops"], timing["ms"]["gemm"]],
+                        dtype=torch.float64, device=device)
     if world > 1:
-        dist.all_reduce(vals[:3], op=dist.ReduceOp.MAX)
-        dist.all_reduce(vals[3:], op=dist.ReduceOp.SUM)
-    ms, e2e_ms, gemm_ms, gemm_flops = vals.tolist()
+        dist.all_reduce(vals[:4], op=dist.ReduceOp.MAX)
+        dist.all_reduce(vals[4:], op=dist.ReduceOp.SUM)
+    ms, e2e_ms, e2e_serial_ms, gemm_ms, gemm_flops, gemm_ms_sum = vals.tolist()
     gemm_ms /= args.steps
     gemm_flops /= args.steps
+    gemm_ms_sum /= args.steps
     peak, peak_sustained, hbm, peak_kind = peaks()
-    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
+    achieved = gemm_flops / (gemm_ms_sum * 1e-3) / 1e12 if gemm_ms_sum > 0 else 0.0
     h2d = sum(g.numel() * 4 for g in host_g) + stat_bytes
     d2h = sum(p.numel() * 4 for p in params)
 
     if rank == 0:
-        cpu_ms, cores, reps = cpu_baseline_sample(10.0, args.workload) if world == 1 else (None, None, 0)
+        cpu_ms, cores, reps = (cpu_baseline_sample(10.0, args.workload) if world == 1 and not args.no_cpu_baseline
+                               else (None, None, 0))
         layers = SETS[args.workload][0]
         line = {
             "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -563,8 +671,12 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "peak_kind": f"{peak_kind} burst bf16 (sustained {peak_sustained})",
-                         "kernel": "k_gemm_bf16 (all S8 GEMM launches of a step)"},
-            "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                         "kernel": "k_gemm_bf16 (all S8 GEMM launches of a step)"
+                                   + (", per GPU: sum of rank FLOPs / sum of rank GEMM time" if world > 1 else "")},
+            "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "mode": "pipelined: step k+1 host-to-device copy and step k-1 device-to-host copy overlap "
+                            "step k (copy-in / compute / copy-out streams)",
+                    "serial_value": round(e2e_serial_ms, 4)},
             "gpu_launches": int(launches * args.steps),
             "launches_per_step": launches,
             "clocks": clocks,

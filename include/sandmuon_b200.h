@@ -182,6 +182,15 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
  *   -> mapback -> Frobenius graft to sqrt(d_out) -> W -= lr * direction. */
 int sm_plan_step(SmPlan* plan, const SmStepArgs* args, void* stream);
 
+/* Graph replay (default on): from a plan's second step on, sm_plan_step
+ * launches its kernels as one CUDA graph, captured once on a private stream
+ * and re-captured only when the gradients' 16-byte alignment pattern changes;
+ * the per-step arguments travel in a descriptor table uploaded from host
+ * memory before each replay.  Results are identical either way.  A step
+ * issued on a stream that is itself being captured returns
+ * SM_ERR_UNSUPPORTED.  enabled = 0 launches every kernel individually. */
+int sm_plan_set_replay(SmPlan* plan, int enabled);
+
 /* Optional per-kernel-class timing with CUDA events (for the benchmark).
  * When enabled, sm_plan_step records an event pair around each launch;
  * sm_plan_timing_read synchronises, returns totals in ms per class and the

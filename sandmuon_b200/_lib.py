@@ -6,12 +6,15 @@ device is not an sm_100 GPU, every entry point raises instead of falling back.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libsandmuon_b200.so"
+# SANDMUON_B200_LIB names another build of the library (for example one
+# compiled with different SMB_* tuning macros); default: the in-tree build.
+LIB_PATH = Path(os.environ.get("SANDMUON_B200_LIB") or Path(__file__).resolve().parent / "libsandmuon_b200.so")
 
 SM_OK = 0
 SM_STAT_A_DIAG = 0
@@ -89,6 +92,7 @@ SIGNATURES = {
     "sm_plan_workspace_bytes": (_c_int, [ctypes.POINTER(SmPlanSpec), ctypes.POINTER(_c_size)]),
     "sm_plan_create": (_c_int, [ctypes.POINTER(SmPlanSpec), _c_void_p, _c_size, _c_void_p, ctypes.POINTER(_c_void_p)]),
     "sm_plan_step": (_c_int, [_c_void_p, ctypes.POINTER(SmStepArgs), _c_void_p]),
+    "sm_plan_set_replay": (_c_int, [_c_void_p, _c_int]),
     "sm_plan_set_timing": (_c_int, [_c_void_p, _c_int]),
     "sm_plan_timing_read": (_c_int, [_c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_c_i64),
                                      ctypes.POINTER(ctypes.c_double)]),

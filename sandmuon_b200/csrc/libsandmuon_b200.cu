@@ -68,6 +68,55 @@ static int fail(int code, const std::string& msg) {
     if (rc_ != SM_OK) return rc_; \
   } while (0)
 
+// Launches issued while t_pdl is set (the kernels of an optimizer step after
+// its first) carry the programmatic-stream-serialization attribute: each may
+// start launching while its predecessor drains, and waits in grid_dep_wait()
+// before it reads or writes global memory.
+thread_local bool t_pdl = false;
+
+struct PdlScope {
+  bool saved;
+  explicit PdlScope(bool on) : saved(t_pdl) { t_pdl = on; }
+  ~PdlScope() { t_pdl = saved; }
+};
+
+// Fills `attrs` with the attributes of the current launch mode plus an
+// optional cluster of `cluster` CTAs; returns how many were written.
+static unsigned launch_attrs(cudaLaunchAttribute* attrs, int cluster) {
+  unsigned n = 0;
+  if (cluster > 1) {
+    memset(&attrs[n], 0, sizeof(attrs[n]));
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (t_pdl) {
+    memset(&attrs[n], 0, sizeof(attrs[n]));
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  return n;
+}
+
+template <typename... KArgs, typename... Args>
+static int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                         Args... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchAttribute attrs[2];
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attrs;
+  cfg.numAttrs = launch_attrs(attrs, 1);
+  SM_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+  return SM_OK;
+}
+
 static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 static inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 
@@ -207,20 +256,17 @@ static int gemm_kernel(void (**out)(GemmLaunch), int* smem_bytes) {
   return SM_OK;
 }
 
+// `attr` holds room for two attributes: the pair cluster and, in a plan
+// step, programmatic serialisation.
 static void pair_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int grid, int smem,
                                cudaStream_t st) {
   memset(cfg, 0, sizeof(*cfg));
-  memset(attr, 0, sizeof(*attr));
-  attr->id = cudaLaunchAttributeClusterDimension;
-  attr->val.clusterDim.x = 2;
-  attr->val.clusterDim.y = 1;
-  attr->val.clusterDim.z = 1;
   cfg->gridDim = dim3(static_cast<unsigned>(grid));
   cfg->blockDim = dim3(kGemmThreads);
   cfg->dynamicSmemBytes = static_cast<size_t>(smem);
   cfg->stream = st;
   cfg->attrs = attr;
-  cfg->numAttrs = 1;
+  cfg->numAttrs = launch_attrs(attr, 2);
 }
 
 template <int BN, int BK, bool COMP, bool A_MN, bool B_MN, int EPI, int CG>
@@ -230,12 +276,12 @@ static int launch_gemm_t(const GemmLaunch& L, int grid, cudaStream_t st) {
   SM_TRY((gemm_kernel<BN, BK, COMP, A_MN, B_MN, EPI, CG>(&kern, &smem)));
   if (L.total_tiles == 0 || grid == 0) return SM_OK;
   if (CG == 1) {
-    kern<<<grid, kGemmThreads, smem, st>>>(L);
+    SM_TRY(launch_kernel(kern, dim3(grid), dim3(kGemmThreads), static_cast<size_t>(smem), st, L));
   } else {
     if (grid % 2 != 0) return fail(SM_ERR_ARG, "a CTA-pair GEMM needs an even grid");
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr;
-    pair_launch_config(&cfg, &attr, grid, smem, st);
+    cudaLaunchAttribute attr[2];
+    pair_launch_config(&cfg, attr, grid, smem, st);
     SM_CUDA(cudaLaunchKernelEx(&cfg, kern, L));
   }
   SM_LAUNCHED();
@@ -253,8 +299,9 @@ static int pair_workers(DeviceInfo* di, int* out) {
       int smem = 0;
       SM_TRY((gemm_kernel<256, 64, true, false, false, kEpiF32, 2>(&kern, &smem)));
       cudaLaunchConfig_t cfg;
-      cudaLaunchAttribute attr;
-      pair_launch_config(&cfg, &attr, 2 * std::max(1, di->sms / 2), smem, nullptr);
+      cudaLaunchAttribute attr[2];
+      PdlScope plain(false);
+      pair_launch_config(&cfg, attr, 2 * std::max(1, di->sms / 2), smem, nullptr);
       SM_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
     }
     di->pair_workers = std::max(0, n);
@@ -462,11 +509,15 @@ struct Group {
   float *inv_norm = nullptr, *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
   float2 *rs_white = nullptr, *rs_map = nullptr;
   int* tmask = nullptr;  // [B] 1 = transposed matrix: its FP32 Q is stored in param layout
+  unsigned *tk_white = nullptr, *tk_map = nullptr;  // [B] last-CTA tickets (zero between launches)
   std::vector<int> host_tmask;
   // K-major boxes {64, 128}: the iterate as both operands of X X^T, and G / P
   // (128-row tiles of A; G also as the 128-row B tiles of G G)
   CUtensorMap xh_K, xl_K, xa_K, xb_K;
   CUtensorMap gh_K, gl_K, ph_K, pl_K;
+  // K-major boxes {64, 64}: the B operand of a symmetric product on 256 x 128
+  // CTA-pair tiles, where each CTA stages 64 B rows
+  CUtensorMap xh_K64, xl_K64, xa_K64, xb_K64, gh_K64, gl_K64;
   // MN-major boxes {64, 64}: the iterate as the B of P X
   CUtensorMap xh_MN, xl_MN, xa_MN, xb_MN;
 };
@@ -488,8 +539,8 @@ struct Carver {
 enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 
 // Tilings of the symmetric products X X^T and G G: 0 = one CTA, 128 x 128
-// tiles; 1 = CTA pair, 256 x 256; 2 = CTA pair, 256 x 128 block rows; -1 =
-// by size.  P X runs on CTA pairs (256 x bn_c) wherever the group allows.
+// tiles; 1 = CTA pair, 256 x 256; 2 = CTA pair, 256 x 128 block rows (each
+// CTA stages 64 B rows: the *_K64 tensor maps); -1 = by size.  P X runs on CTA pairs (256 x bn_c) wherever the group allows.
 // Measured on B200 (cfg1 768-row and cfg4 2048-row groups): X X^T is
 // fastest on 256 x 256 pair tiles at both sizes; G G (K = rows, polynomial
 // epilogue) on single-CTA tiles below 1024 rows, where its finer triangle
@@ -501,6 +552,8 @@ enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 #ifndef SMB_GG_TILE
 #define SMB_GG_TILE -1
 #endif
+static_assert(SMB_GRAM_TILE >= -1 && SMB_GRAM_TILE <= 2 && SMB_GG_TILE >= -1 && SMB_GG_TILE <= 2,
+              "plan tilings: -1 (by size), 0, 1 or 2");
 static int kind_tiling(const Group& g, int kind) {
   const int t = kind == kGram ? SMB_GRAM_TILE : SMB_GG_TILE;
   if (t >= 0) return t;
@@ -543,6 +596,8 @@ static void carve_group(Carver& cv, Group& g) {
   g.rs_white = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
   g.rs_map = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
   g.tmask = cv.take<int>(g.batch);
+  g.tk_white = cv.take<unsigned>(g.batch);
+  g.tk_map = cv.take<unsigned>(g.batch);
 }
 
 static int encode_group_maps(Group& g) {
@@ -554,6 +609,12 @@ static int encode_group_maps(Group& g) {
   SM_TRY(make_map(&g.gl_K, g.gl, g.rp, g.rp, g.batch, kBkK, kGemmBM));
   SM_TRY(make_map(&g.ph_K, g.ph, g.rp, g.rp, g.batch, kBkK, kGemmBM));
   SM_TRY(make_map(&g.pl_K, g.pl, g.rp, g.rp, g.batch, kBkK, kGemmBM));
+  SM_TRY(make_map(&g.xh_K64, g.xh, g.cp, g.rp, g.batch, kBkK, kGemmBM / 2));
+  SM_TRY(make_map(&g.xl_K64, g.xl, g.cp, g.rp, g.batch, kBkK, kGemmBM / 2));
+  SM_TRY(make_map(&g.xa_K64, g.xa, g.cp, g.rp, g.batch, kBkK, kGemmBM / 2));
+  SM_TRY(make_map(&g.xb_K64, g.xb, g.cp, g.rp, g.batch, kBkK, kGemmBM / 2));
+  SM_TRY(make_map(&g.gh_K64, g.gh, g.rp, g.rp, g.batch, kBkK, kGemmBM / 2));
+  SM_TRY(make_map(&g.gl_K64, g.gl, g.rp, g.rp, g.batch, kBkK, kGemmBM / 2));
   SM_TRY(make_map(&g.xh_MN, g.xh, g.cp, g.rp, g.batch, kChunk, kBkK));
   SM_TRY(make_map(&g.xl_MN, g.xl, g.cp, g.rp, g.batch, kChunk, kBkK));
   SM_TRY(make_map(&g.xa_MN, g.xa, g.cp, g.rp, g.batch, kChunk, kBkK));
@@ -654,16 +715,22 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
   const CUtensorMap& xMN_h = in_a ? g.xa_MN : g.xh_MN;
   const CUtensorMap& xMN_l = in_a ? g.xb_MN : g.xl_MN;
   GemmProblem p;
+  // B rows staged per CTA: 64 on 256 x 128 pair tiles, else 128
+  const bool b64 = kind_cg(g, kind) == 2 && bn == kGemmBM;
   if (kind == kGram) {
-    // X X^T: A = B = X, K-major, symmetric 128 x 128 tiles
-    p = gemm_problem(xK_h, comp ? xK_l : xK_h, xK_h, comp ? xK_l : xK_h, g.rp, g.rp, g.cp, g.batch, bn,
+    // X X^T: A = B = X, K-major, symmetric tiles
+    const CUtensorMap& bK_h = b64 ? (in_a ? g.xa_K64 : g.xh_K64) : xK_h;
+    const CUtensorMap& bK_l = b64 ? (in_a ? g.xb_K64 : g.xl_K64) : xK_l;
+    p = gemm_problem(xK_h, comp ? xK_l : xK_h, bK_h, comp ? bK_l : bK_h, g.rp, g.rp, g.cp, g.batch, bn,
                      kind_cg(g, kind), 1);
     p.out0 = g.gh;
     p.out1 = g.gl;
     *epi = comp ? kEpiHiLo : kEpiBF16;
   } else if (kind == kGramSq) {
     // G G with G symmetric: B = G read K-major as G^T
-    p = gemm_problem(g.gh_K, comp ? g.gl_K : g.gh_K, g.gh_K, comp ? g.gl_K : g.gh_K, g.rp, g.rp, g.rp, g.batch,
+    const CUtensorMap& bG_h = b64 ? g.gh_K64 : g.gh_K;
+    const CUtensorMap& bG_l = b64 ? g.gl_K64 : g.gl_K;
+    p = gemm_problem(g.gh_K, comp ? g.gl_K : g.gh_K, bG_h, comp ? bG_l : bG_h, g.rp, g.rp, g.rp, g.batch,
                      bn, kind_cg(g, kind), 1);
     if (stage == 0) {
       p.out0 = g.g2;
@@ -750,12 +817,11 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
         const int64_t per = static_cast<int64_t>(g.rp) * g.rp;
         const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 4, 1024), 512));
         SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-                   k_reduce_s8scale<<<g.batch, 256, 0, st>>>(g.partials, per_mat, kS8Margin, g.s, g.s_inv);
-                   SM_LAUNCHED();
-                   k_poly_stage1<<<dim3(blocks, g.batch), 256, 0, st>>>(
-                       g.gh, g.gl, g.g2, g.s, g.rp, (float)kS8Coeff[0][0], (float)kS8Coeff[0][1],
-                       (float)kS8Coeff[0][2]);
-                   SM_LAUNCHED();
+                   SM_TRY(launch_kernel(k_reduce_s8scale, dim3(g.batch), dim3(256), 0, st, g.partials, per_mat,
+                                        kS8Margin, g.s, g.s_inv));
+                   SM_TRY(launch_kernel(k_poly_stage1, dim3(blocks, g.batch), dim3(256), 0, st, g.gh, g.gl, g.g2,
+                                        g.s, g.rp, (float)kS8Coeff[0][0], (float)kS8Coeff[0][1],
+                                        (float)kS8Coeff[0][2]));
                    return SM_OK;
                  }()));
         *launches += 2;
@@ -774,31 +840,21 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
   const MatDev* mats = d_mats + g.mat_off;
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
              dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
-             if (g.rank1) {
-               if (vec4) k_whiten_rowstats<4, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
-               else k_whiten_rowstats<1, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
-             } else {
-               if (vec4) k_whiten_rowstats<4, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
-               else k_whiten_rowstats<1, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld);
-             }
-             SM_LAUNCHED();
-             k_reduce_invnorm<<<B, 256, 0, st>>>(mats, g.rs_white, ld, g.inv_norm);
-             SM_LAUNCHED();
+             auto kern = g.rank1 ? (vec4 ? k_whiten_rowstats<4, true> : k_whiten_rowstats<1, true>)
+                                 : (vec4 ? k_whiten_rowstats<4, false> : k_whiten_rowstats<1, false>);
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
+                                  g.inv_norm, g.tk_white));
              return SM_OK;
            }()));
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
              dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), B);
-             if (g.rank1) {
-               if (vec4) k_whiten_write<true, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
-               else k_whiten_write<true, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
-             } else {
-               if (vec4) k_whiten_write<false, true><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
-               else k_whiten_write<false, false><<<grid, 256, 0, st>>>(mats, mom_beta, mom_omb, g.rs_white, ld, g.inv_norm, g.xh, g.xl, g.rp, g.cp);
-             }
-             SM_LAUNCHED();
+             auto kern = g.rank1 ? (vec4 ? k_whiten_write<true, true> : k_whiten_write<true, false>)
+                                 : (vec4 ? k_whiten_write<false, true> : k_whiten_write<false, false>);
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
+                                  g.inv_norm, g.xh, g.xl, static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp)));
              return SM_OK;
            }()));
-  *launches += 3;
+  *launches += 2;
   return SM_OK;
 }
 
@@ -810,11 +866,9 @@ static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cu
   const MatDev* mats = d_mats + g.mat_off;
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
              dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
-             if (g.rank1) k_mapback_rowstats<true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-             else k_mapback_rowstats<false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld);
-             SM_LAUNCHED();
-             k_reduce_graft<<<B, 256, 0, st>>>(mats, g.rs_map, ld, g.gamma);
-             SM_LAUNCHED();
+             auto kern = g.rank1 ? k_mapback_rowstats<true> : k_mapback_rowstats<false>;
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, g.q, static_cast<int64_t>(g.rp),
+                                  static_cast<int64_t>(g.cp), g.rs_map, ld, g.gamma, g.tk_map));
              return SM_OK;
            }()));
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
@@ -822,17 +876,13 @@ static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cu
              const int64_t per = static_cast<int64_t>(g.r) * g.c / (vec4 ? 4 : 1);
              const unsigned gx = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(per, 1024), 8 * sms)));
              dim3 grid(gx, B);
-             if (g.rank1) {
-               if (vec4) k_mapback_apply<true, true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
-               else k_mapback_apply<true, false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
-             } else {
-               if (vec4) k_mapback_apply<false, true><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
-               else k_mapback_apply<false, false><<<grid, 256, 0, st>>>(mats, g.q, g.rp, g.cp, g.rs_map, ld, g.gamma);
-             }
-             SM_LAUNCHED();
+             auto kern = g.rank1 ? (vec4 ? k_mapback_apply<true, true> : k_mapback_apply<true, false>)
+                                 : (vec4 ? k_mapback_apply<false, true> : k_mapback_apply<false, false>);
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, g.q, static_cast<int64_t>(g.rp),
+                                  static_cast<int64_t>(g.cp), g.rs_map, ld, g.gamma));
              return SM_OK;
            }()));
-  *launches += 3;
+  *launches += 2;
   return SM_OK;
 }
 
@@ -841,6 +891,10 @@ static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cu
 using namespace smb;
 
 // ==================================================================== plan
+
+#ifndef SMB_PDL
+#define SMB_PDL 1
+#endif
 
 struct SmPlan {
   int device = 0;
@@ -861,6 +915,17 @@ struct SmPlan {
   S8Launches s8;
   Timer timer;
   int64_t launches_last = 0;
+  // Graph replay: from the second step on, the step's launches run as one
+  // CUDA graph (captured on a private stream; kernel choices depend only on
+  // the plan and on the per-group vec4 flags, which key the capture).  The
+  // per-step descriptor table is uploaded before each replay.
+  bool replay = true;
+  bool pdl = SMB_PDL != 0;  // programmatic dependent launch between the step's kernels
+  int64_t steps_done = 0;
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::vector<uint8_t> exec_vec4;
+  int64_t exec_launches = 0;
 };
 
 namespace smb {
@@ -1420,14 +1485,20 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
       }
     }
     p->h_table.resize(p->table_bytes);
+    if (rc == SM_OK) {
+      e = cudaStreamCreateWithFlags(&p->cap_stream, cudaStreamNonBlocking);
+      if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("capture stream: ") + cudaGetErrorString(e));
+    }
   }
   if (rc != SM_OK) {
-    delete p;
+    sm_plan_destroy(p);
     return rc;
   }
   *plan_out = p;
   return SM_OK;
 }
+
+static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, cudaStream_t st, Timer* tm, int64_t* out);
 
 int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
   if (p == nullptr || args == nullptr || args->grads == nullptr || args->lrs == nullptr || args->counts == nullptr ||
@@ -1489,18 +1560,69 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     d.kind = sp.kind;
     d.init = args->ema_init[s] ? 1 : 0;
   }
-  // Pageable source: the runtime stages it before returning, so h_table may
-  // be rewritten by the next step immediately.
+  // A caller's graph capture would freeze this step's arguments (uploaded
+  // from host memory below) into every replay: refuse it.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  SM_CUDA(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone)
+    return fail(SM_ERR_UNSUPPORTED, "sm_plan_step cannot be captured into a CUDA graph: its per-step "
+                                    "arguments are uploaded from host memory at call time");
+  // Pageable source on purpose: the runtime stages this small table through
+  // the command stream before returning (so h_table may be rewritten at
+  // once), where a pinned source would queue on a copy engine behind any
+  // bulk host-to-device copy the caller has in flight on another stream.
   SM_CUDA(cudaMemcpyAsync(p->d_mats, p->h_table.data(), p->table_bytes, cudaMemcpyHostToDevice, st));
 
+  const bool use_graph = p->replay && tm == nullptr && p->steps_done > 0;
+  ++p->steps_done;
+  if (use_graph) {
+    if (p->exec != nullptr && p->exec_vec4 != vec4) {
+      SM_CUDA(cudaGraphExecDestroy(p->exec));
+      p->exec = nullptr;
+    }
+    if (p->exec == nullptr) {
+      int64_t n = 0;
+      SM_CUDA(cudaStreamBeginCapture(p->cap_stream, cudaStreamCaptureModeThreadLocal));
+      const int rc = launch_step(p, vec4, p->cap_stream, nullptr, &n);
+      cudaGraph_t graph = nullptr;
+      const cudaError_t e = cudaStreamEndCapture(p->cap_stream, &graph);
+      if (rc != SM_OK) {
+        if (graph != nullptr) cudaGraphDestroy(graph);
+        return rc;
+      }
+      if (e != cudaSuccess) return fail(SM_ERR_CUDA, std::string("step capture: ") + cudaGetErrorString(e));
+      const cudaError_t ei = cudaGraphInstantiate(&p->exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (ei != cudaSuccess) {
+        p->exec = nullptr;
+        return fail(SM_ERR_CUDA, std::string("step graph instantiate: ") + cudaGetErrorString(ei));
+      }
+      p->exec_vec4 = vec4;
+      p->exec_launches = n;
+    }
+    SM_CUDA(cudaGraphLaunch(p->exec, st));
+    p->launches_last = p->exec_launches;
+    return SM_OK;
+  }
+  SM_TRY(launch_step(p, vec4, st, tm, &launches));
+  p->launches_last = launches;
+  return SM_OK;
+}
+
+// Every kernel of one step, in stream order on `st`.
+static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, cudaStream_t st, Timer* tm, int64_t* out) {
+  const int ns = static_cast<int>(p->stats.size());
+  int64_t launches = 0;
+  // The first kernel follows the descriptor upload in plain stream order;
+  // every later one may launch early (programmatic dependent launch).
+  PdlScope first(false);
   SM_TIMED(tm, SM_TCLASS_STATS, 0.0, st, ([&]() -> int {
-             if (ns > 0) {
-               k_stats_finish<<<ns, 256, 0, st>>>(p->d_stats, p->stat_beta, p->stat_omb);
-               SM_LAUNCHED();
-             }
+             if (ns > 0) SM_TRY(launch_kernel(k_stats_finish, dim3(ns), dim3(256), 0, st, p->d_stats,
+                                              p->stat_beta, p->stat_omb));
              return SM_OK;
            }()));
   ++launches;
+  PdlScope rest(p->pdl);
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
     SM_TRY(run_front(p->groups[gi], p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
   SM_TRY(run_s8(p->groups, p->s8, st, tm, &launches));
@@ -1508,7 +1630,13 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
   SM_TRY(current_device_info(&di));
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
     SM_TRY(run_back(p->groups[gi], p->d_mats, vec4[gi] != 0, di->sms, st, tm, &launches));
-  p->launches_last = launches;
+  *out = launches;
+  return SM_OK;
+}
+
+int sm_plan_set_replay(SmPlan* p, int enabled) {
+  if (p == nullptr) return fail(SM_ERR_ARG, "null plan");
+  p->replay = enabled != 0;
   return SM_OK;
 }
 
@@ -1548,6 +1676,8 @@ int sm_plan_launches_per_step(const SmPlan* p, int64_t* out) {
 int sm_plan_destroy(SmPlan* p) {
   if (p == nullptr) return SM_OK;
   for (cudaEvent_t e : p->timer.pool) cudaEventDestroy(e);
+  if (p->exec != nullptr) cudaGraphExecDestroy(p->exec);
+  if (p->cap_stream != nullptr) cudaStreamDestroy(p->cap_stream);
   delete p;
   return SM_OK;
 }

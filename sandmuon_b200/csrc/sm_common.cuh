@@ -298,6 +298,18 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic-stream-serialization attribute may
+// begin before its predecessor in the stream has finished.  grid_dep_wait()
+// blocks until every prerequisite grid has completed and its memory
+// operations are visible (for a kernel launched without the attribute it
+// returns at once); grid_dep_launch() lets the next such kernel begin
+// launching once every CTA of this grid has issued it or exited.  Every
+// kernel the optimizer plan launches calls both, in that order, before it
+// touches global memory.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- numerics
 
 __device__ __forceinline__ float warp_sum(float v) {

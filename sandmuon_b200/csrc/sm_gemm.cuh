@@ -239,6 +239,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above is private to this CTA; operands and outputs may belong
+  // to the previous kernel of the stream until here.
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

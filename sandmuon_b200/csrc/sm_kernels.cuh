@@ -332,6 +332,8 @@ __device__ __forceinline__ double block_sum_d(double v, double* sh) {
 constexpr float kFltTiny = 1.17549435e-38f;  // torch.finfo(torch.float32).tiny
 
 __global__ void __launch_bounds__(256) k_stats_finish(const StatDev* __restrict__ stats, float beta, float omb) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ double sh[8];
   const StatDev d = stats[blockIdx.x];
   const int n = d.n;
@@ -442,70 +444,107 @@ struct MatDev {
 //   rs[o] = { y . z_a , |y|^2 }
 // The rank-one whitening correction V = Y + c (Y z) z^T acts along d_in in
 // both orientations, so its dot products are row dots of the param layout.
+// The last CTA of a matrix to finish (an integer ticket per matrix, zero
+// between launches: that CTA resets it) also reduces the matrix's |y|^2 row
+// sums, in row order, into
+//   inv_norm[b] = 1 / max(|Y_b|_F, 1e-30).
+// The S8 map is invariant to the scale of its input (stage 1 divides by
+// s = 1.35 |G^2|_F^(1/4)), so any norm that keeps X in range reproduces
+// x / |x|_F (sandmuon/optimizer.py:77-78); |Y|_F bounds |V|_F within the
+// factor rho = sqrt(1 + |z|^2) of the rank-one whitener and never cancels.
+
+// The last of `count` CTAs to arrive on `ticket` returns true (after a fence
+// that makes every other CTA's prior global writes visible to it) and resets
+// the ticket to zero.  Call from all threads after the CTA's writes.
+__device__ __forceinline__ bool last_cta_of(unsigned* ticket, unsigned count) {
+  __shared__ unsigned s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(ticket, 1u);
+    s_last = (t + 1u == count) ? 1u : 0u;
+    if (s_last) {
+      __threadfence();
+      *ticket = 0u;
+    }
+  }
+  __syncthreads();
+  return s_last != 0u;
+}
+
+// Sum over rows 0..n of rs[row].y in a fixed order (FP64), whole CTA.
+__device__ __forceinline__ double rows_sum_y(const float2* rs, int n, double* sh) {
+  double acc = 0.0;
+  for (int o = threadIdx.x; o < n; o += blockDim.x) acc += static_cast<double>(__ldcg(&rs[o].y));
+  acc = warp_sum_d(acc);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += sh[w];
+  return t;
+}
+
 template <int VEC, bool RANK1>
 __global__ void __launch_bounds__(256)
     k_whiten_rowstats(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs,
-                      int ld_rs) {
+                      int ld_rs, float* __restrict__ inv_norm, unsigned* __restrict__ tickets) {
+  grid_dep_wait();
+  grid_dep_launch();
+  __shared__ double sh[8];
   const MatDev md = mats[blockIdx.y];
-  const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int o0 = blockIdx.x * 8;
+  if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
+  const int o = o0 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (o >= md.d_out) return;
-  const float* g = md.grad + static_cast<int64_t>(o) * md.d_in;
-  // A null momentum means "use the input as is" (the batch S8 entry point).
-  const bool has_mom = md.mom != nullptr;
-  const float* m = has_mom ? md.mom + static_cast<int64_t>(o) * md.d_in : g;
-  const float ib = md.inv_b[o];
-  float dot = 0.0f, sq = 0.0f;
-  for (int i = lane * VEC; i < md.d_in; i += 32 * VEC) {
-    float gv[VEC], mv[VEC], av[VEC], zv[VEC];
-    if constexpr (VEC == 4) {
-      const float4 g4 = *reinterpret_cast<const float4*>(g + i);
-      const float4 m4 = *reinterpret_cast<const float4*>(m + i);
-      const float4 a4 = *reinterpret_cast<const float4*>(md.inv_a + i);
-      gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
-      mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
-      av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
-      if (RANK1) {
-        const float4 z4 = *reinterpret_cast<const float4*>(md.z_a + i);
-        zv[0] = z4.x; zv[1] = z4.y; zv[2] = z4.z; zv[3] = z4.w;
+  float2* rsb = rs + static_cast<int64_t>(blockIdx.y) * ld_rs;
+  if (o < md.d_out) {
+    const float* g = md.grad + static_cast<int64_t>(o) * md.d_in;
+    // A null momentum means "use the input as is" (the batch S8 entry point).
+    const bool has_mom = md.mom != nullptr;
+    const float* m = has_mom ? md.mom + static_cast<int64_t>(o) * md.d_in : g;
+    const float ib = md.inv_b[o];
+    float dot = 0.0f, sq = 0.0f;
+#pragma unroll 2
+    for (int i = lane * VEC; i < md.d_in; i += 32 * VEC) {
+      float gv[VEC], mv[VEC], av[VEC], zv[VEC];
+      if constexpr (VEC == 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(g + i);
+        const float4 m4 = *reinterpret_cast<const float4*>(m + i);
+        const float4 a4 = *reinterpret_cast<const float4*>(md.inv_a + i);
+        gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+        mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+        av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
+        if (RANK1) {
+          const float4 z4 = *reinterpret_cast<const float4*>(md.z_a + i);
+          zv[0] = z4.x; zv[1] = z4.y; zv[2] = z4.z; zv[3] = z4.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          gv[e] = g[i + e];
+          mv[e] = m[i + e];
+          av[e] = md.inv_a[i + e];
+          if (RANK1) zv[e] = md.z_a[i + e];
+        }
       }
-    } else {
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        gv[e] = g[i + e];
-        mv[e] = m[i + e];
-        av[e] = md.inv_a[i + e];
-        if (RANK1) zv[e] = md.z_a[i + e];
+        const float mn = mom_beta * mv[e] + omb * gv[e];
+        const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
+        const float y = (src * ib) * av[e];
+        sq += y * y;
+        if (RANK1) dot += y * zv[e];
       }
     }
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float mn = mom_beta * mv[e] + omb * gv[e];
-      const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
-      const float y = (src * ib) * av[e];
-      sq += y * y;
-      if (RANK1) dot += y * zv[e];
-    }
+    sq = warp_sum(sq);
+    if (RANK1) dot = warp_sum(dot);
+    if (lane == 0) rsb[o] = make_float2(dot, sq);
   }
-  sq = warp_sum(sq);
-  if (RANK1) dot = warp_sum(dot);
-  if (lane == 0) rs[static_cast<int64_t>(blockIdx.y) * ld_rs + o] = make_float2(dot, sq);
-}
-
-// inv_norm[b] = 1 / max(|Y_b|_F, 1e-30).  The S8 map is invariant to the
-// scale of its input (stage 1 divides by s = 1.35 |G^2|_F^(1/4)), so any
-// norm that keeps X in range reproduces x / |x|_F (sandmuon/optimizer.py:77-78);
-// |Y|_F bounds |V|_F within the factor rho = sqrt(1 + |z|^2) of the rank-one
-// whitener and never cancels.
-__global__ void __launch_bounds__(256)
-    k_reduce_invnorm(const MatDev* __restrict__ mats, const float2* __restrict__ rs, int ld_rs,
-                     float* __restrict__ inv_norm) {
-  __shared__ double sh[8];
-  const MatDev md = mats[blockIdx.x];
-  double acc = 0.0;
-  for (int o = threadIdx.x; o < md.d_out; o += blockDim.x) acc += rs[static_cast<int64_t>(blockIdx.x) * ld_rs + o].y;
-  const double t = block_sum_d<256>(acc, sh);
-  if (threadIdx.x == 0) inv_norm[blockIdx.x] = 1.0f / fmaxf(static_cast<float>(sqrt(t)), 1e-30f);
+  if (last_cta_of(tickets + blockIdx.y, static_cast<unsigned>((md.d_out + 7) / 8))) {
+    const double t = rows_sum_y(rsb, md.d_out, sh);
+    if (threadIdx.x == 0) inv_norm[blockIdx.y] = 1.0f / fmaxf(static_cast<float>(sqrt(t)), 1e-30f);
+  }
 }
 
 // ========================================== N3 pass 2: whiten + split write
@@ -518,6 +557,8 @@ __global__ void __launch_bounds__(256)
     k_whiten_write(const MatDev* __restrict__ mats, float mom_beta, float omb, const float2* __restrict__ rs, int ld_rs,
                    const float* __restrict__ inv_norm, __nv_bfloat16* __restrict__ xh,
                    __nv_bfloat16* __restrict__ xl, int64_t rp, int64_t cp) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ uint32_t sh_hi[64][17];  // [i][o/2] packed bf16 pairs, transposed staging
   __shared__ uint32_t sh_lo[64][17];
   const int b = blockIdx.z;
@@ -650,6 +691,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     k_reduce_s8scale(const float* __restrict__ partials, int per_mat, float margin, float* __restrict__ s,
                      float* __restrict__ s_inv) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ double sh[8];
   double acc = 0.0;
   for (int p = threadIdx.x; p < per_mat; p += blockDim.x)
@@ -669,6 +712,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     k_poly_stage1(__nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ gl, const float* __restrict__ g2,
                   const float* __restrict__ s, int rp, float pa, float pb, float pc) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int b = blockIdx.y;
   const int64_t per4 = static_cast<int64_t>(rp) * rp / 4;
   // Multiplications by 1/s, one at a time: for a zero matrix (s = 1e-30, so
@@ -716,74 +761,73 @@ __device__ __forceinline__ int64_t q_ld(const MatDev& md, int64_t rp, int64_t cp
 template <bool RANK1>
 __global__ void __launch_bounds__(256)
     k_mapback_rowstats(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
-                       float2* __restrict__ out, int ld_out) {
+                       float2* __restrict__ out, int ld_out, float* __restrict__ gamma,
+                       unsigned* __restrict__ tickets) {
+  grid_dep_wait();
+  grid_dep_launch();
+  __shared__ double sh[8];
   const int b = blockIdx.y;
   const MatDev md = mats[b];
-  const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int o0 = blockIdx.x * 8;
+  if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
+  const int o = o0 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (o >= md.d_out) return;
-  const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * q_ld(md, rp, cp);
-  float t = 0.f, s1 = 0.f, s2 = 0.f;
-  const int n4 = md.d_in & ~3;
-  for (int i = lane * 4; i < n4; i += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(qr + i);
-    const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
-    const float vv[4] = {v.x, v.y, v.z, v.w};
-    const float aa[4] = {a.x, a.y, a.z, a.w};
-    float zz[4] = {0.f, 0.f, 0.f, 0.f};
-    if (RANK1) {
-      const float4 z = *reinterpret_cast<const float4*>(md.z_a + i);
-      zz[0] = z.x; zz[1] = z.y; zz[2] = z.z; zz[3] = z.w;
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float a2 = aa[e] * aa[e];
-      s1 += a2 * vv[e] * vv[e];
+  float2* outb = out + static_cast<int64_t>(b) * ld_out;
+  if (o < md.d_out) {
+    const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * q_ld(md, rp, cp);
+    float t = 0.f, s1 = 0.f, s2 = 0.f;
+    const int n4 = md.d_in & ~3;
+#pragma unroll 4
+    for (int i = lane * 4; i < n4; i += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(qr + i);
+      const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      const float aa[4] = {a.x, a.y, a.z, a.w};
+      float zz[4] = {0.f, 0.f, 0.f, 0.f};
       if (RANK1) {
-        t += zz[e] * vv[e];
-        s2 += a2 * zz[e] * vv[e];
+        const float4 z = *reinterpret_cast<const float4*>(md.z_a + i);
+        zz[0] = z.x; zz[1] = z.y; zz[2] = z.z; zz[3] = z.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a2 = aa[e] * aa[e];
+        s1 += a2 * vv[e] * vv[e];
+        if (RANK1) {
+          t += zz[e] * vv[e];
+          s2 += a2 * zz[e] * vv[e];
+        }
       }
     }
-  }
-  for (int i = n4 + lane; i < md.d_in; i += 32) {
-    const float v = qr[i];
-    const float a2 = md.inv_a[i] * md.inv_a[i];
-    s1 += a2 * v * v;
+    for (int i = n4 + lane; i < md.d_in; i += 32) {
+      const float v = qr[i];
+      const float a2 = md.inv_a[i] * md.inv_a[i];
+      s1 += a2 * v * v;
+      if (RANK1) {
+        const float z = md.z_a[i];
+        t += z * v;
+        s2 += a2 * z * v;
+      }
+    }
+    s1 = warp_sum(s1);
     if (RANK1) {
-      const float z = md.z_a[i];
-      t += z * v;
-      s2 += a2 * z * v;
+      t = warp_sum(t);
+      s2 = warp_sum(s2);
+    }
+    if (lane == 0) {
+      const double ib = md.inv_b[o];
+      double row = s1;
+      if (RANK1) {
+        const double c = md.scal_a[0], k2 = md.scal_a[1];
+        row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
+      }
+      outb[o] = make_float2(t, static_cast<float>(ib * ib * row));
     }
   }
-  s1 = warp_sum(s1);
-  if (RANK1) {
-    t = warp_sum(t);
-    s2 = warp_sum(s2);
-  }
-  if (lane == 0) {
-    const double ib = md.inv_b[o];
-    double row = s1;
-    if (RANK1) {
-      const double c = md.scal_a[0], k2 = md.scal_a[1];
-      row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
-    }
-    out[static_cast<int64_t>(b) * ld_out + o] = make_float2(t, static_cast<float>(ib * ib * row));
-  }
-}
-
-// gamma[b] = sqrt(d_out) / max(|U_b|_F, tiny)  (_graft_direction,
-// sandmuon/optimizer.py:63-66)
-__global__ void __launch_bounds__(256)
-    k_reduce_graft(const MatDev* __restrict__ mats, const float2* __restrict__ rs, int ld_rs,
-                   float* __restrict__ gamma) {
-  __shared__ double sh[8];
-  const MatDev md = mats[blockIdx.x];
-  double acc = 0.0;
-  for (int o = threadIdx.x; o < md.d_out; o += blockDim.x) acc += rs[static_cast<int64_t>(blockIdx.x) * ld_rs + o].y;
-  const double t = block_sum_d<256>(acc, sh);
-  if (threadIdx.x == 0) {
-    const float nrm = static_cast<float>(sqrt(t));
-    gamma[blockIdx.x] = md.sqrt_rows / fmaxf(nrm, kFltTiny);
+  // gamma[b] = sqrt(d_out) / max(|U_b|_F, tiny)  (_graft_direction,
+  // sandmuon/optimizer.py:63-66), by the matrix's last CTA
+  if (last_cta_of(tickets + b, static_cast<unsigned>((md.d_out + 7) / 8))) {
+    const double total = rows_sum_y(outb, md.d_out, sh);
+    if (threadIdx.x == 0) gamma[b] = md.sqrt_rows / fmaxf(static_cast<float>(sqrt(total)), kFltTiny);
   }
 }
 
@@ -795,6 +839,8 @@ template <bool RANK1, bool VEC4>
 __global__ void __launch_bounds__(256)
     k_mapback_apply(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
                     const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int b = blockIdx.y;
   const MatDev md = mats[b];
   const float* qb = q + static_cast<int64_t>(b) * rp * cp;

@@ -253,6 +253,10 @@ class StepPlan:
             rc = _lib.load().sm_plan_step(self._handle, ctypes.byref(args), _stream(self.device))
         _lib.check(rc, "sm_plan_step")
 
+    def set_replay(self, enabled: bool) -> None:
+        """Graph replay of the step's launches (on by default; identical results)."""
+        _lib.check(_lib.load().sm_plan_set_replay(self._handle, int(enabled)), "sm_plan_set_replay")
+
     def set_timing(self, enabled: bool) -> None:
         _lib.check(_lib.load().sm_plan_set_timing(self._handle, int(enabled)), "sm_plan_set_timing")
 
