@@ -12,7 +12,7 @@ all-gather when N > 1).  The sums are refilled before every step with one
 device copy (the step zeroes them, as in training).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-                  [--workload cfg1|cfg4|cfg3|stats]
+                  [--workload cfg1|cfg4|cfg2|cfg3|stats]
 
 Prints one JSON line (rank 0).  value = device ms per step, max over ranks;
 e2e = the same through the public API with pinned-host gradients/statistics
@@ -23,7 +23,9 @@ same with every copy and step on one stream).
 Other workloads (not the contract line): cfg4 = the same step on the 24-layer
 x 2048 matrix set (144 matrices); cfg3 = the S8 sweep of BASELINE configs[3]
 (one line per shape: S8 TFLOP/s and error against an FP32 torch restatement,
-plus one optimizer step of each class); stats = the hook statistic
+plus one optimizer step of each class); cfg2 = the GPT-2 training step of
+BASELINE configs[2] (tokens/s, hooks on real activations, fused AdamW beside
+it); stats = the hook statistic
 reductions of one config-1 microbatch (HBM GB/s, FP32 and BF16 inputs).
 """
 from __future__ import annotations
@@ -62,7 +64,7 @@ def parse_args():
     ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no CPU baseline, clock probe or e2e pass")
-    ap.add_argument("--workload", choices=("cfg1", "cfg4", "cfg3", "stats"), default="cfg1")
+    ap.add_argument("--workload", choices=("cfg1", "cfg4", "cfg2", "cfg3", "stats"), default="cfg1")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="omit the ~10 s CPU baseline sample (tuning runs); the contract line keeps it")
     return ap.parse_args()
@@ -202,13 +204,18 @@ def make_refill(opt, stats, rows, device):
     return refill, flat.numel() * 4
 
 
-def time_steps(opt, refill, steps, device):
+def time_steps(opt, refill, steps, device, host=None):
+    """Device ms per step (CUDA events); `host`, a list, receives the host
+    ms per step spent issuing the steps (before the final synchronise)."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
     start.record()
     for _ in range(steps):
         refill()
         opt.step()
     end.record()
+    if host is not None:
+        host.append((time.perf_counter() - t0) * 1e3 / steps)
     torch.cuda.synchronize(device)
     return start.elapsed_time(end) / steps
 
@@ -452,6 +459,78 @@ def run_cfg3(args, device):
         torch.cuda.empty_cache()
 
 
+# ------------------------------------------- config 2: GPT-2 training step
+
+def run_cfg2(args, device):
+    """a GPT-2-style decoder (9 layers, width 768, 12 heads,
+    vocab 50257, context 1024) trained on uniform random tokens, batch 128 as
+    8 microbatches of 16, BF16 autocast forward/backward, FP32 weights.
+    RankOneAWeightedPE takes the 54 block Linear weights (its hooks reduce the
+    real activations and cotangents on the GPU), AdamW auxiliaries the
+    embeddings and LayerNorms.  Reports tokens/s, step ms and the optimizer
+    step's share (CUDA events around opt.step()), and the same loop with
+    torch's fused AdamW on every parameter for context."""
+    from sandmuon_b200 import RankOneAWeightedPE
+    from sandmuon_b200.workloads import GPT2, gpt2_matrix_filter
+    micro, rows, ctx, vocab = 8, 16, 1024, 50257
+    gen = torch.Generator(device=device).manual_seed(SEED)
+    batches = [torch.randint(0, vocab, (rows, ctx), generator=gen, device=device) for _ in range(micro)]
+    targets = [torch.randint(0, vocab, (rows, ctx), generator=gen, device=device) for _ in range(micro)]
+    tokens = micro * rows * ctx
+    results = {}
+    for name in ("sandmuon", "adamw"):
+        torch.manual_seed(SEED)
+        model = GPT2(9, 768, 12, vocab, ctx).to(device)
+        if name == "sandmuon":
+            opt = RankOneAWeightedPE(model, lr=LR, module_filter=gpt2_matrix_filter)
+        else:
+            opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.01, fused=True)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        losses = []
+
+        def step(marks=None):
+            total = torch.zeros((), device=device)
+            if marks is not None:
+                marks[0].record()
+            for idx, tgt in zip(batches, targets):
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    logits = model(idx)
+                    loss = torch.nn.functional.cross_entropy(logits.view(-1, vocab), tgt.view(-1)) / micro
+                loss.backward()
+                total += loss.detach()
+            if marks is not None:
+                marks[1].record()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            if marks is not None:
+                marks[2].record()
+            return total
+
+        for _ in range(max(args.warmup, 3)):
+            losses.append(step())
+        torch.cuda.synchronize(device)
+        for k in range(args.steps):
+            losses.append(step(ev[k]))
+        torch.cuda.synchronize(device)
+        step_ms = statistics.median(e[0].elapsed_time(e[2]) for e in ev)
+        opt_ms = statistics.median(e[1].elapsed_time(e[2]) for e in ev)
+        results[name] = {"ms_per_step": round(step_ms, 3), "tokens_per_s": round(tokens / (step_ms * 1e-3), 1),
+                         "optimizer_ms_per_step": round(opt_ms, 3),
+                         "loss_first_last": [round(float(losses[0]), 4), round(float(losses[-1]), 4)]}
+        if name == "sandmuon":
+            opt.close()
+        del model, opt
+        torch.cuda.empty_cache()
+    s = results["sandmuon"]
+    print(json.dumps({"workload": "cfg2", "metric": "GPT-2 9Lx768 training step (tokens/s)",
+                      "value": s["tokens_per_s"], "unit": "tokens/s", "ms_per_step": s["ms_per_step"],
+                      "optimizer_ms_per_step": s["optimizer_ms_per_step"], "tokens_per_step": tokens,
+                      "steps": args.steps, "warmup": max(args.warmup, 3), "dtype": "bf16 autocast / fp32 weights",
+                      "data": "synthetic uniform random tokens", "sandmuon": s, "torch_fused_adamw": results["adamw"],
+                      "timing": "CUDA events, median over timed steps (hooks run inside forward/backward)"}),
+          flush=True)
+
+
 # ------------------------------------------------- hook statistics (N1)
 
 def run_stats(args, device):
@@ -562,11 +641,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.workload in ("cfg3", "stats"):
+    if args.workload in ("cfg2", "cfg3", "stats"):
         if rank == 0:
             device = torch.device("cuda", local)
             torch.cuda.set_device(device)
-            (run_cfg3 if args.workload == "cfg3" else run_stats)(args, device)
+            {"cfg2": run_cfg2, "cfg3": run_cfg3, "stats": run_stats}[args.workload](args, device)
         return
     import torch.distributed as dist
     device = torch.device("cuda", local)
@@ -596,7 +675,8 @@ def main():
     if world > 1:
         dist.barrier()
     t0 = time.monotonic()
-    ms = time_steps(opt, refill, args.steps, device)
+    host_ms = []
+    ms = time_steps(opt, refill, args.steps, device, host_ms)
     sampler.mark(t0, time.monotonic())
     if world > 1:
         dist.barrier()
@@ -677,6 +757,7 @@ def main():
                     "mode": "pipelined: step k+1 host-to-device copy and step k-1 device-to-host copy overlap "
                             "step k (copy-in / compute / copy-out streams)",
                     "serial_value": round(e2e_serial_ms, 4)},
+            "host_issue_ms_per_step": round(host_ms[0], 4),
             "gpu_launches": int(launches * args.steps),
             "launches_per_step": launches,
             "clocks": clocks,

@@ -97,3 +97,89 @@ def s8_executed_flops(shapes) -> float:
         r, c = min(rows, cols), max(rows, cols)
         total += 7.0 * (4.0 * r * r * c + 2.0 * r ** 3)
     return total
+
+
+# ------------------------------------------------------------ config 2: GPT-2
+
+class CausalSelfAttention(nn.Module):
+    """Bias-free q/k/v/o projections around torch's fused causal attention."""
+
+    def __init__(self, width: int, heads: int):
+        super().__init__()
+        self.heads = heads
+        for proj in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            setattr(self, proj, nn.Linear(width, width, bias=False))
+
+    def forward(self, x):
+        b, t, c = x.shape
+        q, k, v = (p(x).view(b, t, self.heads, c // self.heads).transpose(1, 2)
+                   for p in (self.q_proj, self.k_proj, self.v_proj))
+        y = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return self.o_proj(y.transpose(1, 2).reshape(b, t, c))
+
+
+class GPT2Block(nn.Module):
+    def __init__(self, width: int, heads: int, hidden: int):
+        super().__init__()
+        self.ln_1 = nn.LayerNorm(width)
+        self.attn = CausalSelfAttention(width, heads)
+        self.ln_2 = nn.LayerNorm(width)
+        self.mlp = nn.Module()
+        self.mlp.c_fc = nn.Linear(width, hidden, bias=False)
+        self.mlp.c_proj = nn.Linear(hidden, width, bias=False)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln_1(x))
+        return x + self.mlp.c_proj(torch.nn.functional.gelu(self.mlp.c_fc(self.ln_2(x))))
+
+
+class GPT2(nn.Module):
+    """GPT-2-style decoder of BASELINE config 2 (historical parameter names, so
+    q/k/v statistic sharing applies): token and position embeddings, pre-LN
+    blocks of bias-free Linear layers, final LayerNorm, and an output head
+    tied to the token embedding.  Random initialisation (N(0, 0.02^2)); the
+    SandMuon matrices are the transformer.h.* Linear weights, everything else
+    (embeddings, LayerNorms) trains with the AdamW auxiliaries."""
+
+    def __init__(self, layers: int = 9, width: int = 768, heads: int = 12, vocab: int = 50257,
+                 context: int = 1024):
+        super().__init__()
+        self.transformer = nn.Module()
+        self.transformer.wte = nn.Embedding(vocab, width)
+        self.transformer.wpe = nn.Embedding(context, width)
+        self.transformer.h = nn.ModuleList([GPT2Block(width, heads, 4 * width) for _ in range(layers)])
+        self.transformer.ln_f = nn.LayerNorm(width)
+        for name, p in self.named_parameters():
+            if p.ndim == 2:
+                nn.init.normal_(p, std=0.02)
+
+    def forward(self, idx):
+        t = idx.shape[1]
+        pos = torch.arange(t, device=idx.device)
+        x = self.transformer.wte(idx) + self.transformer.wpe(pos)
+        for block in self.transformer.h:
+            x = block(x)
+        return self.transformer.ln_f(x) @ self.transformer.wte.weight.t()
+
+
+def gpt2_matrix_filter(name: str, module: nn.Module) -> bool:
+    """module_filter of the config-2 run: the Linear layers of the blocks."""
+    return name.startswith("transformer.h.") and isinstance(module, nn.Linear)
+
+
+def gpt2_train_step(model: nn.Module, opt, batches, targets) -> torch.Tensor:
+    """One optimizer step over microbatches (BF16 autocast forward/backward,
+    FP32 weights): mean cross-entropy over the microbatches, backward per
+    microbatch (the hooks accumulate statistics), opt.step(), zero_grad.
+    Returns the step's summed loss as a device tensor."""
+    total = torch.zeros((), device=batches[0].device)
+    n = len(batches)
+    for idx, tgt in zip(batches, targets):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = model(idx)
+            loss = torch.nn.functional.cross_entropy(logits.view(-1, logits.shape[-1]), tgt.view(-1)) / n
+        loss.backward()
+        total += loss.detach()
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    return total

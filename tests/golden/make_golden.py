@@ -150,14 +150,54 @@ def uneven_stats(ref_pkg):
     return out
 
 
+def gpt2_run(ref_pkg, *, steps=6, seed=3, lr=2e-2):
+    """The reference RankOneAWeightedPE training a small GPT-2-style decoder
+    (2 layers, width 128, 4 heads, vocab 512; the config-2 model family of
+    sandmuon_b200.workloads.GPT2) in FP32 on two fixed batches of next-token
+    prediction: initial weights, tokens, the summed loss of every step, and
+    two SandMuon matrices after the last step."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from sandmuon_b200.workloads import GPT2, gpt2_matrix_filter
+    torch.manual_seed(seed)
+    model = GPT2(layers=2, width=128, heads=4, vocab=512, context=64)
+    opt = ref_pkg.RankOneAWeightedPE(model, lr=lr, module_filter=gpt2_matrix_filter)
+    g = torch.Generator().manual_seed(seed + 2)
+    batches = [torch.randint(0, 512, (4, 64), generator=g) for _ in range(2)]
+    out = {"lr": np.float32(lr), "steps": np.int64(steps)}
+    for name, p in model.named_parameters():
+        out[f"init/{name}"] = np32(p)
+    for i, b in enumerate(batches):
+        out[f"tokens/{i}"] = b.numpy().astype(np.int64)
+    for s in range(steps):
+        total = 0.0
+        for b in batches:
+            logits = model(b[:, :-1])
+            loss = torch.nn.functional.cross_entropy(logits.reshape(-1, 512), b[:, 1:].reshape(-1)) / len(batches)
+            loss.backward()
+            total += float(loss.detach())
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        out[f"loss/{s}"] = np.float64(total)
+    for name in ("transformer.h.0.attn.q_proj.weight", "transformer.h.1.mlp.c_fc.weight"):
+        out[f"final/{name}"] = np32(dict(model.named_parameters())[name])
+    opt.close()
+    return out
+
+
 def main():
+    """python tests/golden/make_golden.py [fixture ...]  (default: all)."""
     ref_pkg, ref_opt = load_reference()
     torch.set_num_threads(1)
-    np.savez_compressed(HERE / "primitives.npz", **primitives(ref_opt))
-    np.savez_compressed(HERE / "s8.npz", **s8_cases(ref_opt))
-    np.savez_compressed(HERE / "mini_gpt_rank1.npz", **mini_gpt_run(ref_pkg, rank_one=True))
-    np.savez_compressed(HERE / "mini_gpt_diag.npz", **mini_gpt_run(ref_pkg, rank_one=False))
-    np.savez_compressed(HERE / "uneven_stats.npz", **uneven_stats(ref_pkg))
+    fixtures = {
+        "primitives": lambda: primitives(ref_opt),
+        "s8": lambda: s8_cases(ref_opt),
+        "mini_gpt_rank1": lambda: mini_gpt_run(ref_pkg, rank_one=True),
+        "mini_gpt_diag": lambda: mini_gpt_run(ref_pkg, rank_one=False),
+        "uneven_stats": lambda: uneven_stats(ref_pkg),
+        "gpt2_small": lambda: gpt2_run(ref_pkg),
+    }
+    for name in sys.argv[1:] or list(fixtures):
+        np.savez_compressed(HERE / f"{name}.npz", **fixtures[name]())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
