@@ -70,6 +70,22 @@ def parse_args():
     return ap.parse_args()
 
 
+def gemm_traffic_per_launch():
+    """DRAM bytes (read + write) per S8 GEMM launch from the committed ncu
+    launch list of a config-1 step (profiles/launches_cfg1_step.md, line
+    `traffic_per_launch_bytes: N`), or None when the summary has no figure."""
+    path = ROOT / "profiles" / "launches_cfg1_step.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_per_launch_bytes:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -749,7 +765,10 @@ def main():
             "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),
             "phase_ms_per_step": {k: round(v / args.steps, 4) for k, v in timing["ms"].items()},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": gemm_traffic_per_launch() if args.workload == "cfg1" else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the "
+                                           "S8 GEMM launches of a config-1 step (profiles/launches_cfg1_step.md)",
                          "peak_kind": f"{peak_kind} burst bf16 (sustained {peak_sustained})",
                          "kernel": "k_gemm_bf16 (all S8 GEMM launches of a step)"
                                    + (", per GPU: sum of rank FLOPs / sum of rank GEMM time" if world > 1 else "")},

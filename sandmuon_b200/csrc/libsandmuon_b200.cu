@@ -385,6 +385,7 @@ static GemmProblem gemm_problem(const CUtensorMap& ah, const CUtensorMap& al, co
   p.batch = batch;
   p.tiles_m = m / (kGemmBM * cg);
   p.tiles_n = n / bn;
+  p.scale = 1.0f;
   return p;
 }
 
@@ -540,17 +541,17 @@ enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 
 // Tilings of the symmetric products X X^T and G G: 0 = one CTA, 128 x 128
 // tiles; 1 = CTA pair, 256 x 256; 2 = CTA pair, 256 x 128 block rows (each
-// CTA stages 64 B rows: the *_K64 tensor maps); -1 = by size.  P X runs on CTA pairs (256 x bn_c) wherever the group allows.
-// Measured on B200 (cfg1 768-row and cfg4 2048-row groups): X X^T is
-// fastest on 256 x 256 pair tiles at both sizes; G G (K = rows, polynomial
-// epilogue) on single-CTA tiles below 1024 rows, where its finer triangle
-// balances better, and on pair tiles from 1024 rows; block-row pair tiles
-// were slowest everywhere.
+// CTA stages 64 B rows: the *_K64 tensor maps); -1 = by size (pairs from 1024
+// rows, one CTA below).  Measured on B200 (config-1 768-row groups, ncu launch
+// lists): X X^T is fastest on 256 x 256 pair tiles; so is G G now that its
+// epilogue only scales and shifts the diagonal (compensated 79 vs 89 us per
+// launch on single-CTA tiles, plain 43 vs 48 us); with the old polynomial
+// epilogue, which re-read the gram, single-CTA tiles had been faster.
 #ifndef SMB_GRAM_TILE
 #define SMB_GRAM_TILE 1
 #endif
 #ifndef SMB_GG_TILE
-#define SMB_GG_TILE -1
+#define SMB_GG_TILE 1
 #endif
 static_assert(SMB_GRAM_TILE >= -1 && SMB_GRAM_TILE <= 2 && SMB_GG_TILE >= -1 && SMB_GG_TILE <= 2,
               "plan tilings: -1 (by size), 0, 1 or 2");
@@ -657,6 +658,10 @@ struct S8Launches {
   std::vector<LaunchSet> sets[3];
 };
 
+// beta = b / (2c) of S8 stage `stage` (0-based, stages 1-4): the shift that
+// turns a I + b G + c G^2 into c (G + beta I)^2 + (a - c beta^2) I.
+static double s8_shift(int stage) { return kS8Coeff[stage][1] / (2.0 * kS8Coeff[stage][2]); }
+
 static int kind_k(const Group& g, int kind) { return kind == kGram ? g.cp : g.rp; }
 static int kind_n(const Group& g, int kind) { return kind == kPX ? g.cp : g.rp; }
 
@@ -726,6 +731,8 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
     p.out0 = g.gh;
     p.out1 = g.gl;
     *epi = comp ? kEpiHiLo : kEpiBF16;
+    // stages 2-5 store the shifted gram H = G + beta I (see the G H product)
+    if (stage > 0) p.diag = static_cast<float>(s8_shift(stage));
   } else if (kind == kGramSq) {
     // G G with G symmetric: B = G read K-major as G^T
     const CUtensorMap& bG_h = b64 ? g.gh_K64 : g.gh_K;
@@ -737,18 +744,20 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
       p.partials = g.partials;
       *epi = kEpiF32Norm;
     } else {
-      p.pa = static_cast<float>(kS8Coeff[stage][0]);
-      p.pb = static_cast<float>(kS8Coeff[stage][1]);
-      p.pc = static_cast<float>(kS8Coeff[stage][2]);
-      p.aux = g.gh;
+      // Stages 2-5: with H = G + beta I and beta = b / (2c), the polynomial
+      //   P = a I + b G + c G^2 = c H^2 + (a - c beta^2) I,
+      // so this product squares the shifted gram the X X^T epilogue stored and
+      // its epilogue only scales and adds to the diagonal: no gram re-read.
+      const double a = kS8Coeff[stage][0], c = kS8Coeff[stage][2], beta = s8_shift(stage);
+      p.scale = static_cast<float>(c);
+      p.diag = static_cast<float>(a - c * beta * beta);
       if (comp) {
-        p.aux_lo = g.gl;
         p.out0 = g.ph;
         p.out1 = g.pl;
-        *epi = kEpiPolyHiLo;
+        *epi = kEpiHiLo;
       } else {
         p.out0 = g.gl;
-        *epi = kEpiPoly;
+        *epi = kEpiBF16;
       }
     }
   } else {
@@ -839,7 +848,7 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8 * kWhitenRows)), B);
              auto kern = g.rank1 ? (vec4 ? k_whiten_rowstats<4, true> : k_whiten_rowstats<1, true>)
                                  : (vec4 ? k_whiten_rowstats<4, false> : k_whiten_rowstats<1, false>);
              SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
@@ -847,7 +856,9 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
              return SM_OK;
            }()));
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 64)), static_cast<unsigned>(cdiv(g.dmax, 32)), B);
+             // 32 x 64 tiles of a matrix in either orientation of the group's shape
+             const int64_t tiles = std::max(cdiv(g.c, 64) * cdiv(g.r, 32), cdiv(g.r, 64) * cdiv(g.c, 32));
+             dim3 grid(static_cast<unsigned>(tiles), B);
              auto kern = g.rank1 ? (vec4 ? k_whiten_write<true, true> : k_whiten_write<true, false>)
                                  : (vec4 ? k_whiten_write<false, true> : k_whiten_write<false, false>);
              SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
@@ -865,7 +876,7 @@ static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cu
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8)), B);
+             dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8 * kMapbackRows)), B);
              auto kern = g.rank1 ? k_mapback_rowstats<true> : k_mapback_rowstats<false>;
              SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, g.q, static_cast<int64_t>(g.rp),
                                   static_cast<int64_t>(g.cp), g.rs_map, ld, g.gamma, g.tk_map));

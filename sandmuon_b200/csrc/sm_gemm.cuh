@@ -71,6 +71,8 @@ struct GemmProblem {
   const __nv_bfloat16* aux;     // [batch, m, n] BF16 gram (hi plane) for the poly epilogues
   const __nv_bfloat16* aux_lo;  // lo plane of the gram for the hi/lo poly epilogue
   float pa, pb, pc;     // poly coefficients: out = pa*I + pb*gram + pc*acc
+  float scale;          // F32 / BF16 / hi-lo epilogues: out = scale*alpha*acc + diag*I
+  float diag;
   float* partials;      // [batch, tiles_m*tiles_n*kNormSlots] sum of squares (F32Norm)
   const int* tmask;     // [batch] or null: 1 = store this matrix's FP32 result
                         // transposed ([n, m], row stride m) -- F32 epilogue only
@@ -397,7 +399,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
       const int row0 = tc.mi * kTileM + static_cast<int>(rank) * kGemmBM + quarter * 32;
       const int row = row0 + lane;                        // the TMEM lane = tile row of this thread
       const size_t mat_off = static_cast<size_t>(tc.b) * P.m * P.n;
-      const float alpha = P.alpha != nullptr ? P.alpha[tc.b] : 1.0f;
+      const float alpha = (P.alpha != nullptr ? P.alpha[tc.b] : 1.0f) * P.scale;
       // Symmetric output: a block above the diagonal is also stored transposed.
       // With 256 x 128 pair tiles a CTA's block is 128 x 128 (row block rb);
       // the one below the diagonal in a diagonal tile is skipped, its
@@ -477,8 +479,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
           }
           __syncwarp();
         } else {
+          // the chunk's columns col0 .. col0+31 hold this row's diagonal element
+          const bool diag_here = P.diag != 0.0f && row >= col0 && row < col0 + 32;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = alpha * __uint_as_float(r[c]);
+          for (int c = 0; c < 32; ++c) {
+            v[c] = alpha * __uint_as_float(r[c]);
+            if (diag_here && col0 + c == row) v[c] += P.diag;
+          }
         }
 #pragma unroll
         for (int c = 0; c < 32; ++c) {

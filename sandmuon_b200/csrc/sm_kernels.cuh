@@ -485,6 +485,15 @@ __device__ __forceinline__ double rows_sum_y(const float2* rs, int n, double* sh
   return t;
 }
 
+// Each warp reduces ROWS consecutive param rows, so one CTA covers 8 * ROWS
+// rows and the whitening vectors loaded per column group serve all of a
+// warp's rows.  Rows past d_out repeat the last row and are not stored.
+// Measured on B200 (config 1, ncu): mapback row statistics 111 -> 105 us
+// with 4 rows per warp; the whitening pass, which streams two arrays per
+// row, 106 -> 141 us, so it keeps one row per warp.
+constexpr int kWhitenRows = 1;
+constexpr int kMapbackRows = 4;
+
 template <int VEC, bool RANK1>
 __global__ void __launch_bounds__(256)
     k_whiten_rowstats(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs,
@@ -493,27 +502,30 @@ __global__ void __launch_bounds__(256)
   grid_dep_launch();
   __shared__ double sh[8];
   const MatDev md = mats[blockIdx.y];
-  const int o0 = blockIdx.x * 8;
+  const int o0 = blockIdx.x * 8 * kWhitenRows;
   if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
-  const int o = o0 + (threadIdx.x >> 5);
+  const int obase = o0 + (threadIdx.x >> 5) * kWhitenRows;
   const int lane = threadIdx.x & 31;
   float2* rsb = rs + static_cast<int64_t>(blockIdx.y) * ld_rs;
-  if (o < md.d_out) {
-    const float* g = md.grad + static_cast<int64_t>(o) * md.d_in;
+  if (obase < md.d_out) {
     // A null momentum means "use the input as is" (the batch S8 entry point).
     const bool has_mom = md.mom != nullptr;
-    const float* m = has_mom ? md.mom + static_cast<int64_t>(o) * md.d_in : g;
-    const float ib = md.inv_b[o];
-    float dot = 0.0f, sq = 0.0f;
-#pragma unroll 2
+    const float* g[kWhitenRows];
+    const float* m[kWhitenRows];
+    float ib[kWhitenRows], dot[kWhitenRows], sq[kWhitenRows];
+#pragma unroll
+    for (int r = 0; r < kWhitenRows; ++r) {
+      const int o = min(obase + r, md.d_out - 1);
+      g[r] = md.grad + static_cast<int64_t>(o) * md.d_in;
+      m[r] = has_mom ? md.mom + static_cast<int64_t>(o) * md.d_in : g[r];
+      ib[r] = md.inv_b[o];
+      dot[r] = 0.0f;
+      sq[r] = 0.0f;
+    }
     for (int i = lane * VEC; i < md.d_in; i += 32 * VEC) {
-      float gv[VEC], mv[VEC], av[VEC], zv[VEC];
+      float av[VEC], zv[VEC];
       if constexpr (VEC == 4) {
-        const float4 g4 = *reinterpret_cast<const float4*>(g + i);
-        const float4 m4 = *reinterpret_cast<const float4*>(m + i);
         const float4 a4 = *reinterpret_cast<const float4*>(md.inv_a + i);
-        gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
-        mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
         av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
         if (RANK1) {
           const float4 z4 = *reinterpret_cast<const float4*>(md.z_a + i);
@@ -522,33 +534,51 @@ __global__ void __launch_bounds__(256)
       } else {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
-          gv[e] = g[i + e];
-          mv[e] = m[i + e];
           av[e] = md.inv_a[i + e];
           if (RANK1) zv[e] = md.z_a[i + e];
         }
       }
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const float mn = mom_beta * mv[e] + omb * gv[e];
-        const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
-        const float y = (src * ib) * av[e];
-        sq += y * y;
-        if (RANK1) dot += y * zv[e];
+      for (int r = 0; r < kWhitenRows; ++r) {
+        float gv[VEC], mv[VEC];
+        if constexpr (VEC == 4) {
+          const float4 g4 = *reinterpret_cast<const float4*>(g[r] + i);
+          const float4 m4 = *reinterpret_cast<const float4*>(m[r] + i);
+          gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+          mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            gv[e] = g[r][i + e];
+            mv[e] = m[r][i + e];
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float mn = mom_beta * mv[e] + omb * gv[e];
+          const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
+          const float y = (src * ib[r]) * av[e];
+          sq[r] += y * y;
+          if (RANK1) dot[r] += y * zv[e];
+        }
       }
     }
-    sq = warp_sum(sq);
-    if (RANK1) dot = warp_sum(dot);
-    if (lane == 0) rsb[o] = make_float2(dot, sq);
+#pragma unroll
+    for (int r = 0; r < kWhitenRows; ++r) {
+      const float s_r = warp_sum(sq[r]);
+      const float d_r = RANK1 ? warp_sum(dot[r]) : 0.0f;
+      if (lane == 0 && obase + r < md.d_out) rsb[obase + r] = make_float2(d_r, s_r);
+    }
   }
-  if (last_cta_of(tickets + blockIdx.y, static_cast<unsigned>((md.d_out + 7) / 8))) {
+  if (last_cta_of(tickets + blockIdx.y, static_cast<unsigned>((md.d_out + 8 * kWhitenRows - 1) / (8 * kWhitenRows)))) {
     const double t = rows_sum_y(rsb, md.d_out, sh);
     if (threadIdx.x == 0) inv_norm[blockIdx.y] = 1.0f / fmaxf(static_cast<float>(sqrt(t)), 1e-30f);
   }
 }
 
 // ========================================== N3 pass 2: whiten + split write
-// Tile of 32 param rows x 64 param columns per CTA (256 threads).
+// Tile of 32 param rows x 64 param columns per CTA (256 threads); grid
+// (tiles of the group's largest matrix, matrices).
 //   m' written back ; v = y + c * dot[o] * z[i] ; x = v * inv_norm
 //   X_hi/X_lo at the oriented position: (o, i), or (i, o) when transposed
 //   (staged through shared memory so both reads and writes are coalesced).
@@ -561,11 +591,14 @@ __global__ void __launch_bounds__(256)
   grid_dep_launch();
   __shared__ uint32_t sh_hi[64][17];  // [i][o/2] packed bf16 pairs, transposed staging
   __shared__ uint32_t sh_lo[64][17];
-  const int b = blockIdx.z;
+  // blockIdx.x numbers this matrix's 32 x 64 tiles row-major; a grid sized
+  // for the group's largest tile count leaves the surplus CTAs idle.
+  const int b = blockIdx.y;
   const MatDev md = mats[b];
-  const int o0 = blockIdx.y * 32;
-  const int i0 = blockIdx.x * 64;
-  if (o0 >= md.d_out || i0 >= md.d_in) return;
+  const int tiles_x = (md.d_in + 63) / 64;
+  const int o0 = static_cast<int>(blockIdx.x / tiles_x) * 32;
+  const int i0 = static_cast<int>(blockIdx.x % tiles_x) * 64;
+  if (o0 >= md.d_out) return;
   const float scale = inv_norm[b];
   const float coef = RANK1 ? md.scal_a[0] : 0.0f;
   const bool has_mom = md.mom != nullptr;
@@ -768,64 +801,78 @@ __global__ void __launch_bounds__(256)
   __shared__ double sh[8];
   const int b = blockIdx.y;
   const MatDev md = mats[b];
-  const int o0 = blockIdx.x * 8;
+  const int o0 = blockIdx.x * 8 * kMapbackRows;
   if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
-  const int o = o0 + (threadIdx.x >> 5);
+  const int obase = o0 + (threadIdx.x >> 5) * kMapbackRows;
   const int lane = threadIdx.x & 31;
   float2* outb = out + static_cast<int64_t>(b) * ld_out;
-  if (o < md.d_out) {
-    const float* qr = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * q_ld(md, rp, cp);
-    float t = 0.f, s1 = 0.f, s2 = 0.f;
+  if (obase < md.d_out) {
+    const float* qr[kMapbackRows];
+    float t[kMapbackRows], s1[kMapbackRows], s2[kMapbackRows];
+#pragma unroll
+    for (int r = 0; r < kMapbackRows; ++r) {
+      const int o = min(obase + r, md.d_out - 1);
+      qr[r] = q + static_cast<int64_t>(b) * rp * cp + static_cast<int64_t>(o) * q_ld(md, rp, cp);
+      t[r] = 0.f;
+      s1[r] = 0.f;
+      s2[r] = 0.f;
+    }
     const int n4 = md.d_in & ~3;
-#pragma unroll 4
     for (int i = lane * 4; i < n4; i += 128) {
-      const float4 v = *reinterpret_cast<const float4*>(qr + i);
       const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
-      const float vv[4] = {v.x, v.y, v.z, v.w};
-      const float aa[4] = {a.x, a.y, a.z, a.w};
+      const float aa[4] = {a.x * a.x, a.y * a.y, a.z * a.z, a.w * a.w};
       float zz[4] = {0.f, 0.f, 0.f, 0.f};
       if (RANK1) {
         const float4 z = *reinterpret_cast<const float4*>(md.z_a + i);
         zz[0] = z.x; zz[1] = z.y; zz[2] = z.z; zz[3] = z.w;
       }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a2 = aa[e] * aa[e];
-        s1 += a2 * vv[e] * vv[e];
-        if (RANK1) {
-          t += zz[e] * vv[e];
-          s2 += a2 * zz[e] * vv[e];
+      for (int r = 0; r < kMapbackRows; ++r) {
+        const float4 v = *reinterpret_cast<const float4*>(qr[r] + i);
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s1[r] += aa[e] * vv[e] * vv[e];
+          if (RANK1) {
+            t[r] += zz[e] * vv[e];
+            s2[r] += aa[e] * zz[e] * vv[e];
+          }
         }
       }
     }
     for (int i = n4 + lane; i < md.d_in; i += 32) {
-      const float v = qr[i];
       const float a2 = md.inv_a[i] * md.inv_a[i];
-      s1 += a2 * v * v;
-      if (RANK1) {
-        const float z = md.z_a[i];
-        t += z * v;
-        s2 += a2 * z * v;
+      const float z = RANK1 ? md.z_a[i] : 0.f;
+#pragma unroll
+      for (int r = 0; r < kMapbackRows; ++r) {
+        const float v = qr[r][i];
+        s1[r] += a2 * v * v;
+        if (RANK1) {
+          t[r] += z * v;
+          s2[r] += a2 * z * v;
+        }
       }
     }
-    s1 = warp_sum(s1);
-    if (RANK1) {
-      t = warp_sum(t);
-      s2 = warp_sum(s2);
-    }
-    if (lane == 0) {
-      const double ib = md.inv_b[o];
-      double row = s1;
-      if (RANK1) {
-        const double c = md.scal_a[0], k2 = md.scal_a[1];
-        row = s1 + 2.0 * c * t * s2 + c * c * static_cast<double>(t) * t * k2;
+#pragma unroll
+    for (int r = 0; r < kMapbackRows; ++r) {
+      const float s1r = warp_sum(s1[r]);
+      const float tr = RANK1 ? warp_sum(t[r]) : 0.f;
+      const float s2r = RANK1 ? warp_sum(s2[r]) : 0.f;
+      const int o = obase + r;
+      if (lane == 0 && o < md.d_out) {
+        const double ib = md.inv_b[o];
+        double row = s1r;
+        if (RANK1) {
+          const double c = md.scal_a[0], k2 = md.scal_a[1];
+          row = s1r + 2.0 * c * tr * s2r + c * c * static_cast<double>(tr) * tr * k2;
+        }
+        outb[o] = make_float2(tr, static_cast<float>(ib * ib * row));
       }
-      outb[o] = make_float2(t, static_cast<float>(ib * ib * row));
     }
   }
   // gamma[b] = sqrt(d_out) / max(|U_b|_F, tiny)  (_graft_direction,
   // sandmuon/optimizer.py:63-66), by the matrix's last CTA
-  if (last_cta_of(tickets + b, static_cast<unsigned>((md.d_out + 7) / 8))) {
+  if (last_cta_of(tickets + b, static_cast<unsigned>((md.d_out + 8 * kMapbackRows - 1) / (8 * kMapbackRows)))) {
     const double total = rows_sum_y(outb, md.d_out, sh);
     if (threadIdx.x == 0) gamma[b] = md.sqrt_rows / fmaxf(static_cast<float>(sqrt(total)), kFltTiny);
   }
