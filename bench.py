@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
+    ap.add_argument("--exchange", choices=("weights", "bf16_delta"), default="weights",
+                    help="N > 1: all-gather FP32 updated weights (default) or BF16 update deltas")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no CPU baseline, clock probe or e2e pass")
     ap.add_argument("--workload", choices=("cfg1", "cfg4", "cfg2", "cfg3", "stats"), default="cfg1")
@@ -95,7 +97,7 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def workload_config(world, partition, workload="cfg1"):
+def workload_config(world, partition, workload="cfg1", exchange="weights"):
     layers, width, hidden, rows = SETS[workload]
     params = layers * (4 * width * width + 2 * width * hidden)
     return {
@@ -105,7 +107,8 @@ def workload_config(world, partition, workload="cfg1"):
         "params": params,
         "s8_precision": "stages 1-4 compensated bf16 (hi/lo, 3 products), stage 5 bf16, fp32 accumulate",
         "l2": "no flush: each step streams ~1 GB of FP32 state (> 126 MB L2)",
-        "parallelism": f"matrix-sharded ({partition}) x{world}" if world > 1 else "single GPU",
+        "parallelism": (f"matrix-sharded ({partition}, {exchange} exchange) x{world}" if world > 1
+                        else "single GPU"),
     }
 
 
@@ -167,7 +170,7 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload
 
-def build(device, group, partition, workload="cfg1"):
+def build(device, group, partition, workload="cfg1", exchange="weights"):
     from sandmuon_b200 import RankOneAWeightedPE
     from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
     layers, width, hidden, rows = SETS[workload]
@@ -178,7 +181,7 @@ def build(device, group, partition, workload="cfg1"):
         for p in model.parameters():
             p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
     model.to(device)
-    opt = RankOneAWeightedPE(model, lr=LR, process_group=group, partition=partition)
+    opt = RankOneAWeightedPE(model, lr=LR, process_group=group, partition=partition, exchange=exchange)
     grads_host = {}
     for n, p in opt.named_matrices.items():
         g = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
@@ -670,7 +673,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
         group = dist.group.WORLD
-    model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition, args.workload)
+    model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition, args.workload,
+                                                       args.exchange)
     if args.profile:
         for _ in range(args.warmup + args.steps):
             refill()
@@ -759,7 +763,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 tensor cores (stages 1-4 compensated hi/lo) / fp32 state",
             "data": "synthetic (seeded; random-init weights, N(0,1e-4) grads, injected statistics)",
-            "config": workload_config(world, args.partition, args.workload),
+            "config": workload_config(world, args.partition, args.workload, args.exchange),
             "s8_gemm_tflops": round(achieved, 1),
             "s8_gemm_ms_per_step": round(gemm_ms, 4),
             "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),

@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define SM_ABI_VERSION 1
+#define SM_ABI_VERSION 2
 
 /* status codes */
 #define SM_OK 0
@@ -142,6 +142,12 @@ typedef struct {
 #define SM_STAT_A_RANK1 1
 #define SM_STAT_B 2
 
+/* What the step writes to SmMatrixSpec.export_to (when not NULL). */
+#define SM_EXPORT_WEIGHTS 0     /* float [d_out, d_in]: the updated weight                   */
+#define SM_EXPORT_BF16_DELTA 1  /* bf16 [d_out, d_in]: D = bf16(lr * direction); the weight is
+                                   updated as W -= float(D), exactly what
+                                   sm_apply_bf16_delta_multi does on other ranks            */
+
 typedef struct {
     const SmMatrixSpec* matrices;
     int32_t n_matrices;
@@ -149,6 +155,7 @@ typedef struct {
     int32_t n_stats;
     float statistic_beta;    /* 0.97 (sandmuon/optimizer.py:123)            */
     float momentum;          /* 0.8  (sandmuon/optimizer.py:139)            */
+    int32_t export_mode;     /* SM_EXPORT_WEIGHTS or SM_EXPORT_BF16_DELTA    */
 } SmPlanSpec;
 
 typedef struct SmPlan SmPlan;
@@ -220,6 +227,19 @@ typedef struct {
  * scatter of all-gathered weights back into the parameters of a sharded
  * step; no counterpart in the single-device reference). */
 int sm_copy_multi(const SmCopySpec* copies, int32_t count, void* stream);
+
+/* One weight and the BF16 update delta to subtract from it. */
+typedef struct {
+    float* weight;
+    const void* delta;    /* bf16, same element count as the weight */
+    int64_t numel;
+} SmDeltaSpec;
+
+/* weight[i] -= float(delta[i]) for every (weight, delta) of the list, in one
+ * kernel launch per 64 entries: how a rank applies the BF16 update deltas of
+ * the matrices other ranks own (the sharded step's BF16 exchange; no
+ * counterpart in the single-device reference). */
+int sm_apply_bf16_delta_multi(const SmDeltaSpec* items, int32_t count, void* stream);
 
 /* --------------------------------------------------------- S8 (batch) */
 

@@ -32,6 +32,8 @@ SM_GEMM_B_KMAJOR = 1
 SM_GEMM_A_MNMAJOR = 2
 SM_GEMM_PAIR = 4
 SM_GEMM_BN128 = 8
+SM_EXPORT_WEIGHTS = 0
+SM_EXPORT_BF16_DELTA = 1
 SM_TCLASS_GEMM = 0
 SM_TCLASS_ELEMWISE = 1
 SM_TCLASS_STATS = 2
@@ -64,7 +66,11 @@ class SmStatSpec(ctypes.Structure):
 class SmPlanSpec(ctypes.Structure):
     _fields_ = [("matrices", ctypes.POINTER(SmMatrixSpec)), ("n_matrices", _c_i32),
                 ("stats", ctypes.POINTER(SmStatSpec)), ("n_stats", _c_i32),
-                ("statistic_beta", _c_float), ("momentum", _c_float)]
+                ("statistic_beta", _c_float), ("momentum", _c_float), ("export_mode", _c_i32)]
+
+
+class SmDeltaSpec(ctypes.Structure):
+    _fields_ = [("weight", _c_void_p), ("delta", _c_void_p), ("numel", _c_i64)]
 
 
 class SmStepArgs(ctypes.Structure):
@@ -101,6 +107,7 @@ SIGNATURES = {
     "sm_copy_multi": (_c_int, [ctypes.POINTER(SmCopySpec), _c_i32, _c_void_p]),
     "sm_s8_workspace_bytes": (_c_size, [_c_i32, _c_i32, _c_i32]),
     "sm_s8_polar": (_c_int, [_c_void_p, _c_void_p, _c_i32, _c_i32, _c_i32, _c_void_p, _c_size, _c_void_p]),
+    "sm_apply_bf16_delta_multi": (_c_int, [ctypes.POINTER(SmDeltaSpec), _c_i32, _c_void_p]),
     "sm_s8_executed_flops": (_c_int, [_c_i32, _c_i32, _c_i32, ctypes.POINTER(ctypes.c_double)]),
     "sm_adamw_multi": (_c_int, [ctypes.POINTER(SmAdamTensor), _c_i32, _c_float, _c_float, _c_float, _c_float,
                                 _c_float, _c_void_p]),

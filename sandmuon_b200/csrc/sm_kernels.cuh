@@ -17,6 +17,25 @@
 
 namespace smb {
 
+// The last of `count` CTAs to arrive on `ticket` returns true (after a fence
+// that makes every other CTA's prior global writes visible to it) and resets
+// the ticket to zero.  Call from all threads after the CTA's writes.
+__device__ __forceinline__ bool last_cta_of(unsigned* ticket, unsigned count) {
+  __shared__ unsigned s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(ticket, 1u);
+    s_last = (t + 1u == count) ? 1u : 0u;
+    if (s_last) {
+      __threadfence();
+      *ticket = 0u;
+    }
+  }
+  __syncthreads();
+  return s_last != 0u;
+}
+
 // ============================================================ N1: statistics
 // sum_sq[c] += sum_r x[r,c]^2 ; sum[c] += sum_r x[r,c]
 // (sandmuon/optimizer.py:156-168 forward hook, :170-178 cotangent hook).
@@ -423,7 +442,8 @@ struct MatDev {
   const float* grad;    // [d_out, d_in]
   float* mom;           // [d_out, d_in]
   float* weight;        // [d_out, d_in]
-  float* export_to;     // [d_out, d_in] copy of the updated weight, or null
+  float* export_to;     // [d_out, d_in] copy of the updated weight (FP32), or of the
+                        // BF16 update delta when export_bf16; or null
   const float* inv_a;   // [d_in]
   const float* z_a;     // [d_in] or null (diagonal A)
   const float* zeta_a;  // [d_in] inv_a * z_a or null
@@ -434,7 +454,8 @@ struct MatDev {
   int32_t slot;
   float lr;
   float sqrt_rows;      // sqrt(d_out): the graft norm
-  int32_t pad0, pad1;
+  int32_t export_bf16;  // 1: export_to holds bf16 D = bf16(lr * direction), W -= float(D)
+  int32_t pad1;
 };
 
 // ========================================== N3 pass 1: whitening row stats
@@ -452,25 +473,6 @@ struct MatDev {
 // s = 1.35 |G^2|_F^(1/4)), so any norm that keeps X in range reproduces
 // x / |x|_F (sandmuon/optimizer.py:77-78); |Y|_F bounds |V|_F within the
 // factor rho = sqrt(1 + |z|^2) of the rank-one whitener and never cancels.
-
-// The last of `count` CTAs to arrive on `ticket` returns true (after a fence
-// that makes every other CTA's prior global writes visible to it) and resets
-// the ticket to zero.  Call from all threads after the CTA's writes.
-__device__ __forceinline__ bool last_cta_of(unsigned* ticket, unsigned count) {
-  __shared__ unsigned s_last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned t = atomicAdd(ticket, 1u);
-    s_last = (t + 1u == count) ? 1u : 0u;
-    if (s_last) {
-      __threadfence();
-      *ticket = 0u;
-    }
-  }
-  __syncthreads();
-  return s_last != 0u;
-}
 
 // Sum over rows 0..n of rs[row].y in a fixed order (FP64), whole CTA.
 __device__ __forceinline__ double rows_sum_y(const float2* rs, int n, double* sh) {
@@ -910,12 +912,22 @@ __global__ void __launch_bounds__(256)
       if (RANK1) z = *reinterpret_cast<const float4*>(md.z_a + i);
       float4* wp = reinterpret_cast<float4*>(md.weight + static_cast<int64_t>(o) * md.d_in + i);
       float4 w = *wp;
-      w.x = w.x - step * (((v.x + ct * z.x) * ib) * a.x);
-      w.y = w.y - step * (((v.y + ct * z.y) * ib) * a.y);
-      w.z = w.z - step * (((v.z + ct * z.z) * ib) * a.z);
-      w.w = w.w - step * (((v.w + ct * z.w) * ib) * a.w);
+      float4 d = make_float4(step * (((v.x + ct * z.x) * ib) * a.x), step * (((v.y + ct * z.y) * ib) * a.y),
+                             step * (((v.z + ct * z.z) * ib) * a.z), step * (((v.w + ct * z.w) * ib) * a.w));
+      if (md.export_bf16) {
+        // every rank applies the same rounded delta (k_apply_bf16_delta)
+        const uint2 packed = make_uint2(pack_bf16x2(d.x, d.y), pack_bf16x2(d.z, d.w));
+        d = make_float4(bf16_lo_to_f(packed.x), bf16_hi_to_f(packed.x), bf16_lo_to_f(packed.y),
+                        bf16_hi_to_f(packed.y));
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(md.export_to) +
+                                  static_cast<int64_t>(o) * md.d_in + i) = packed;
+      }
+      w.x = w.x - d.x;
+      w.y = w.y - d.y;
+      w.z = w.z - d.z;
+      w.w = w.w - d.w;
       *wp = w;
-      if (md.export_to != nullptr)
+      if (md.export_to != nullptr && !md.export_bf16)
         *reinterpret_cast<float4*>(md.export_to + static_cast<int64_t>(o) * md.d_in + i) = w;
     } else {
       const int i = col;
@@ -923,9 +935,15 @@ __global__ void __launch_bounds__(256)
       if (RANK1) v += ct * md.z_a[i];
       const float u = (v * ib) * md.inv_a[i];
       const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
-      const float w = md.weight[wi] - step * u;
+      float d = step * u;
+      if (md.export_bf16) {
+        const __nv_bfloat16 db = __float2bfloat16_rn(d);
+        reinterpret_cast<__nv_bfloat16*>(md.export_to)[wi] = db;
+        d = __bfloat162float(db);
+      }
+      const float w = md.weight[wi] - d;
       md.weight[wi] = w;
-      if (md.export_to != nullptr) md.export_to[wi] = w;
+      if (md.export_to != nullptr && !md.export_bf16) md.export_to[wi] = w;
     }
   }
 }
@@ -958,6 +976,46 @@ __global__ void __launch_bounds__(256) k_copy_multi(const CopyBatch batch) {
         *reinterpret_cast<uint4*>(d + o) = *reinterpret_cast<const uint4*>(s + o);
     } else {
       for (int64_t o = base + threadIdx.x; o < end; o += blockDim.x) d[o] = s[o];
+    }
+  }
+}
+
+// ============================================= multi-tensor BF16 delta apply
+struct DeltaBatch {
+  float* weight[kCopyMax];
+  const __nv_bfloat16* delta[kCopyMax];
+  int64_t numel[kCopyMax];
+  int64_t chunk_start[kCopyMax + 1];  // prefix sums of kDeltaChunk-element chunks
+  int32_t count;
+};
+
+constexpr int64_t kDeltaChunk = 8192;
+
+// weight[i] -= float(delta[i]): the update a sharded step's owner applied to
+// its own copy (k_mapback_apply with export_bf16), replayed on another rank.
+__global__ void __launch_bounds__(256) k_apply_bf16_delta(const DeltaBatch batch) {
+  const int64_t total = batch.chunk_start[batch.count];
+  for (int64_t ch = blockIdx.x; ch < total; ch += gridDim.x) {
+    int t = 0;
+    while (batch.chunk_start[t + 1] <= ch) ++t;
+    const int64_t base = (ch - batch.chunk_start[t]) * kDeltaChunk;
+    const int64_t end = min(base + kDeltaChunk, batch.numel[t]);
+    float* w = batch.weight[t];
+    const __nv_bfloat16* d = batch.delta[t];
+    const bool vec = ((reinterpret_cast<uintptr_t>(w) & 15) | (reinterpret_cast<uintptr_t>(d) & 7) |
+                      (batch.numel[t] & 3)) == 0;
+    if (vec) {
+      for (int64_t i = base + threadIdx.x * 4; i < end; i += blockDim.x * 4) {
+        const uint2 p = *reinterpret_cast<const uint2*>(d + i);
+        float4 v = *reinterpret_cast<float4*>(w + i);
+        v.x -= bf16_lo_to_f(p.x);
+        v.y -= bf16_hi_to_f(p.x);
+        v.z -= bf16_lo_to_f(p.y);
+        v.w -= bf16_hi_to_f(p.y);
+        *reinterpret_cast<float4*>(w + i) = v;
+      }
+    } else {
+      for (int64_t i = base + threadIdx.x; i < end; i += blockDim.x) w[i] -= __bfloat162float(d[i]);
     }
   }
 }

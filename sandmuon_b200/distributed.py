@@ -10,7 +10,12 @@ its own microbatches; at step():
      the matrices it owns (partition "lpt": longest-processing-time greedy
      over S8 FLOPs; "layer": contiguous transformer layers per rank);
   3. exchange: the owners' updated FP32 weights are all-gathered with one
-     padded all_gather_into_tensor and copied back into every rank's params.
+     padded all_gather_into_tensor and copied back into every rank's params
+     (exchange="weights", the default).  exchange="bf16_delta" gathers the
+     update deltas lr * direction rounded to BF16 instead (half the NVLink
+     bytes); every rank, the owner included, subtracts the same rounded delta,
+     so the ranks stay bitwise identical.  The rounding (2^-9 relative per
+     element) perturbs the update direction far inside its 1e-2 tolerance.
 There is no other data-path collective; gradients are averaged by the
 caller's data-parallel wrapper as usual.
 """
@@ -51,10 +56,16 @@ def partition_matrices(named_shapes: dict[str, tuple[int, int]], world: int, how
     return owner
 
 
+EXCHANGES = ("weights", "bf16_delta")
+
+
 class MatrixSharding:
-    def __init__(self, opt, group, *, partition: str = "lpt"):
+    def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights"):
+        if exchange not in EXCHANGES:
+            raise ValueError(f"unknown exchange {exchange!r} (expected one of {EXCHANGES})")
         self.opt = opt
         self.group = group
+        self.exchange_mode = exchange
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         shapes = {n: tuple(p.shape) for n, p in opt.named_matrices.items()}
@@ -98,10 +109,12 @@ class MatrixSharding:
             per_rank = [[] for _ in range(self.world)]
             for p in params:
                 per_rank[self.owner(p)].append(p)
-            shard = max(sum(p.numel() for p in ps) for ps in per_rank)
+            # 4-element alignment keeps every slot 16-byte (FP32) / 8-byte (BF16) aligned
+            shard = max(sum((p.numel() + 3) // 4 * 4 for p in ps) for ps in per_rank)
             device = params[0].device
-            send = torch.zeros(shard, dtype=torch.float32, device=device)
-            recv = torch.empty(shard * self.world, dtype=torch.float32, device=device)
+            dtype = torch.bfloat16 if self.exchange_mode == "bf16_delta" else torch.float32
+            send = torch.zeros(shard, dtype=dtype, device=device)
+            recv = torch.empty(shard * self.world, dtype=dtype, device=device)
             slots, unpack = {}, []
             for r, ps in enumerate(per_rank):
                 offset = 0
@@ -110,13 +123,19 @@ class MatrixSharding:
                         slots[id(p)] = send[offset:offset + p.numel()].view_as(p)
                     else:
                         unpack.append((p, recv[r * shard + offset:r * shard + offset + p.numel()]))
-                    offset += p.numel()
+                    offset += (p.numel() + 3) // 4 * 4
             self._gather = (send, recv, slots, unpack)
         return self._gather
 
+    @property
+    def export_mode(self) -> int:
+        """The plan's export mode for this exchange (see StepPlan)."""
+        from . import _lib
+        return _lib.SM_EXPORT_BF16_DELTA if self.exchange_mode == "bf16_delta" else _lib.SM_EXPORT_WEIGHTS
+
     def send_slot(self, parameter) -> torch.Tensor | None:
-        """Where the step also writes an owned matrix's updated weight (its
-        all-gather send slot); None for a single rank."""
+        """Where the step also writes an owned matrix's updated weight, or its
+        BF16 update delta (its all-gather send slot); None for a single rank."""
         if self.world == 1:
             return None
         return self._layout()[2][id(parameter)]
@@ -124,10 +143,17 @@ class MatrixSharding:
     def exchange(self, matrix_items) -> None:
         """All-gathers every matrix from its owner into all ranks.  The owners'
         send slots were filled by the update kernel itself; the received
-        weights are scattered back with one multi-tensor copy launch."""
+        weights are scattered back with one multi-tensor copy launch, or the
+        received BF16 deltas of the matrices stepped now are subtracted with
+        one multi-tensor launch."""
         if self.world == 1:
             return
-        from .engine import copy_multi
+        from .engine import apply_bf16_delta_multi, copy_multi
         send, recv, slots, unpack = self._layout()
         dist.all_gather_into_tensor(recv, send, group=self.group)
-        copy_multi([(p.detach(), src) for p, src in unpack], recv.device)
+        if self.exchange_mode == "bf16_delta":
+            # only the matrices stepped now: a skipped matrix's slot holds an old delta
+            stepped = {id(item[0]) for item in matrix_items}
+            apply_bf16_delta_multi([(p.detach(), src) for p, src in unpack if id(p) in stepped], recv.device)
+        else:
+            copy_multi([(p.detach(), src) for p, src in unpack], recv.device)

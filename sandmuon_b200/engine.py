@@ -192,9 +192,11 @@ class StepPlan:
     is replaced (the optimizer keys plans by those pointers)."""
 
     def __init__(self, device: torch.device, matrices: list[tuple], stats: list[tuple], *,
-                 statistic_beta: float, momentum: float):
+                 statistic_beta: float, momentum: float, export_mode: int = _lib.SM_EXPORT_WEIGHTS):
         """matrices: (weight, momentum_buffer, a_stat_index, b_stat_index, export | None)
-        stats: (kind, sum, first_sum | None, ema, mean_ema | None)."""
+        stats: (kind, sum, first_sum | None, ema, mean_ema | None).
+        export_mode: what the step writes to each export tensor, FP32 updated
+        weights (SM_EXPORT_WEIGHTS) or BF16 update deltas (SM_EXPORT_BF16_DELTA)."""
         _lib.ensure_device(device)
         self.device = device
         self._keep = []
@@ -214,7 +216,8 @@ class StepPlan:
             slot.mean_ema = mema.data_ptr() if mema is not None else 0
             slot.n, slot.kind = s.numel(), kind
             self._keep += [s, ema] + [t for t in (fs, mema) if t is not None]
-        self._spec = _lib.SmPlanSpec(mat_arr, len(matrices), stat_arr, len(stats), statistic_beta, momentum)
+        self._spec = _lib.SmPlanSpec(mat_arr, len(matrices), stat_arr, len(stats), statistic_beta, momentum,
+                                     export_mode)
         self._arrays = (mat_arr, stat_arr)
         lib = _lib.load()
         nbytes = ctypes.c_size_t(0)
@@ -298,6 +301,22 @@ def copy_multi(pairs: list[tuple[torch.Tensor, torch.Tensor]], device: torch.dev
     with torch.cuda.device(device):
         rc = _lib.load().sm_copy_multi(arr, len(pairs), _stream(device))
     _lib.check(rc, "sm_copy_multi")
+
+
+def apply_bf16_delta_multi(pairs: list[tuple[torch.Tensor, torch.Tensor]], device: torch.device) -> None:
+    """weight -= delta.float() for every (FP32 weight, BF16 delta) pair of
+    contiguous CUDA tensors with equal element counts, in one kernel launch per
+    64 pairs."""
+    if not pairs:
+        return
+    arr = (_lib.SmDeltaSpec * len(pairs))()
+    for slot, (w, d) in zip(arr, pairs):
+        if w.dtype != torch.float32 or d.dtype != torch.bfloat16 or w.numel() != d.numel():
+            raise ValueError("apply_bf16_delta_multi: needs float32 weights and bfloat16 deltas of equal size")
+        slot.weight, slot.delta, slot.numel = w.data_ptr(), d.data_ptr(), w.numel()
+    with torch.cuda.device(device):
+        rc = _lib.load().sm_apply_bf16_delta_multi(arr, len(pairs), _stream(device))
+    _lib.check(rc, "sm_apply_bf16_delta_multi")
 
 
 def s8_flops_per_matrix(rows: int, cols: int) -> float:

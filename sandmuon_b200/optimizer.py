@@ -30,13 +30,15 @@ class DiagonalWeightedPE(Optimizer):
     optimizer steps. Defaults match the 103M run: beta=.97, Muon momentum=.8,
     S8 margin=1.35, auxiliary AdamW LR ratio=.1 and decay=.01.
 
-    Extra keyword `process_group` (torch.distributed group or None) shards the
-    S8 work over the group's ranks; see sandmuon_b200.distributed.
+    Extra keywords: `process_group` (torch.distributed group or None) shards
+    the S8 work over the group's ranks, `partition` ("lpt" or "layer") picks
+    the owners and `exchange` ("weights" or "bf16_delta") what the owners
+    all-gather; see sandmuon_b200.distributed.
     """
 
     def __init__(self, model: nn.Module, lr: float, *, rank_one_a: bool = False,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
-                 process_group=None, partition: str = "lpt"):
+                 process_group=None, partition: str = "lpt", exchange: str = "weights"):
         choose = module_filter or (lambda name, module: isinstance(module, nn.Linear))
         matrices: dict[str, nn.Parameter] = {}
         modules: dict[str, nn.Module] = {}
@@ -81,7 +83,7 @@ class DiagonalWeightedPE(Optimizer):
         self._sharding = None
         if process_group is not None:
             from .distributed import MatrixSharding
-            self._sharding = MatrixSharding(self, process_group, partition=partition)
+            self._sharding = MatrixSharding(self, process_group, partition=partition, exchange=exchange)
 
         self.handles = []
         for name, module in modules.items():
@@ -303,7 +305,9 @@ class DiagonalWeightedPE(Optimizer):
                 for old in self._plans.values():
                     old.close()
                 self._plans.clear()
-            plan = engine.StepPlan(device, mats, stat_specs, statistic_beta=self.statistic_beta, momentum=momentum)
+            export_mode = self._sharding.export_mode if self._sharding is not None else _lib.SM_EXPORT_WEIGHTS
+            plan = engine.StepPlan(device, mats, stat_specs, statistic_beta=self.statistic_beta, momentum=momentum,
+                                   export_mode=export_mode)
             self._plans[key] = plan
         device_counts = None
         if self._sharding is not None:
@@ -345,6 +349,6 @@ class RankOneAWeightedPE(DiagonalWeightedPE):
 
     def __init__(self, model: nn.Module, lr: float, *,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
-                 process_group=None, partition: str = "lpt"):
+                 process_group=None, partition: str = "lpt", exchange: str = "weights"):
         super().__init__(model, lr, rank_one_a=True, module_filter=module_filter,
-                         process_group=process_group, partition=partition)
+                         process_group=process_group, partition=partition, exchange=exchange)

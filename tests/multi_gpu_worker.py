@@ -1,9 +1,11 @@
 """Worker for tests/test_gpu_multi.py: one rank of a sharded optimizer step.
 
-Launched by torch.distributed.run (one process per GPU).  Every rank builds the
-same mini GPT-named model, injects the same statistics and gradients, runs two
-sharded steps (statistic all-reduce, owned-matrix S8, weight all-gather) and
-saves its weights to <out_dir>/rank<r>.pt.
+Launched by torch.distributed.run (one process per GPU) with the output
+directory, the partition ("lpt" / "layer") and the exchange ("weights" /
+"bf16_delta").  Every rank builds the same mini GPT-named model, injects the
+same statistics and gradients, runs two sharded steps (statistic all-reduce,
+owned-matrix S8, exchange) and saves its weights to <out_dir>/rank<r>.pt
+(rank 0 also the initial weights to init.pt).
 """
 import datetime
 import os
@@ -18,7 +20,7 @@ ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
 
 
-def main(out_dir: str, partition: str):
+def main(out_dir: str, partition: str, exchange: str):
     from sandmuon_b200 import RankOneAWeightedPE
     from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
     rank = int(os.environ["RANK"])
@@ -29,7 +31,10 @@ def main(out_dir: str, partition: str):
     try:
         torch.manual_seed(5)
         model = gpt_matrix_model(3, 256, 1024).to(device)
-        opt = RankOneAWeightedPE(model, lr=1e-2, process_group=dist.group.WORLD, partition=partition)
+        if rank == 0:
+            torch.save({n: p.detach().cpu() for n, p in model.named_parameters()}, Path(out_dir) / "init.pt")
+        opt = RankOneAWeightedPE(model, lr=1e-2, process_group=dist.group.WORLD, partition=partition,
+                                 exchange=exchange)
         rng = np.random.default_rng(5)
         for step in range(2):
             synth_gpt_statistics(opt, rng, count=4096)
@@ -45,4 +50,4 @@ def main(out_dir: str, partition: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "lpt")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "lpt", sys.argv[3] if len(sys.argv) > 3 else "weights")

@@ -16,6 +16,11 @@ from sandmuon_b200.distributed import MatrixSharding, partition_matrices
 from sandmuon_b200.workloads import gpt_matrix_model, s8_executed_flops
 
 
+def test_unknown_exchange_is_rejected():
+    with pytest.raises(ValueError):
+        MatrixSharding(None, None, exchange="fp8")
+
+
 def test_lpt_partition_balances_s8_flops():
     shapes = {f"transformer.h.{l}.attn.{p}.weight": (768, 768) for l in range(9)
               for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
@@ -59,14 +64,14 @@ class _StubOptimizer:
                 self.a_sources[id(p)] = self.named_matrices[match.group(1) + "q_proj.weight"]
 
 
-def _worker(rank, world, port, partition, results):
+def _worker(rank, world, port, partition, results, exchange="weights"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         torch.manual_seed(0)
         model = gpt_matrix_model(3, 16, 64)
         opt = _StubOptimizer(model)
-        sharding = MatrixSharding(opt, dist.group.WORLD, partition=partition)
+        sharding = MatrixSharding(opt, dist.group.WORLD, partition=partition, exchange=exchange)
         items = []
         for name, p in opt.named_matrices.items():
             src = opt.a_sources[id(p)]
@@ -88,24 +93,40 @@ def _worker(rank, world, port, partition, results):
         total = sharding.reduce_statistics(tensors, [st[k] for st, k in counters])
         for (st, k), v in zip(counters, total.tolist()):
             st[k] = v
-        # test-only compute stub: each owner writes a value unique to (matrix, owner)
-        with torch.no_grad():
-            for i, (p, _, _) in enumerate(items):
-                if sharding.owns(p):
-                    p.fill_(100.0 * i + sharding.rank)
-                else:
-                    p.fill_(-1.0)
-        # the update kernel writes owned weights into their send slots; here the
-        # test packs them, gathers over gloo and scatters like exchange() does
         send, recv, slots, unpack = sharding._layout()
-        for p, _, _ in items:
-            if sharding.owns(p):
-                assert sharding.send_slot(p).data_ptr() == slots[id(p)].data_ptr()
-                slots[id(p)].copy_(p.detach())
-        dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
-        with torch.no_grad():
-            for p, src in unpack:
-                p.copy_(src.view_as(p))
+        if exchange == "weights":
+            # test-only compute stub: each owner writes a value unique to (matrix, owner)
+            with torch.no_grad():
+                for i, (p, _, _) in enumerate(items):
+                    p.fill_(100.0 * i + sharding.rank if sharding.owns(p) else -1.0)
+            # the update kernel writes owned weights into their send slots; here the
+            # test packs them, gathers over gloo and scatters like exchange() does
+            for p, _, _ in items:
+                if sharding.owns(p):
+                    assert sharding.send_slot(p).data_ptr() == slots[id(p)].data_ptr()
+                    slots[id(p)].copy_(p.detach())
+            dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
+            with torch.no_grad():
+                for p, src in unpack:
+                    p.copy_(src.view_as(p))
+        else:
+            # every rank starts from the same weights; each owner subtracts its
+            # BF16 delta (a value unique to matrix and owner) and exports it;
+            # the others subtract the gathered delta, as exchange() does
+            assert send.dtype == torch.bfloat16
+            with torch.no_grad():
+                for i, (p, _, _) in enumerate(items):
+                    p.fill_(1000.0)
+                    if sharding.owns(p):
+                        delta = torch.full_like(p, 2.0 * i + sharding.rank).to(torch.bfloat16)  # exact in BF16
+                        slots[id(p)].copy_(delta)
+                        p.sub_(delta.float())
+            dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
+            with torch.no_grad():
+                for p, src in unpack:
+                    p.sub_(src.view_as(p).float())
+                for i, (p, _, _) in enumerate(items):
+                    p.copy_(1000.0 - p)  # back to the delta value for the shared assertions
         out = {}
         for i, (p, src, _) in enumerate(items):
             out[i] = (float(p.min()), float(p.max()), sharding.owner(p),
@@ -116,14 +137,14 @@ def _worker(rank, world, port, partition, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("partition", ["lpt", "layer"])
-def test_two_rank_statistics_reduction_and_weight_exchange(partition):
+@pytest.mark.parametrize("partition,exchange", [("lpt", "weights"), ("layer", "weights"), ("lpt", "bf16_delta")])
+def test_two_rank_statistics_reduction_and_weight_exchange(partition, exchange):
     world = 2
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, partition, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, partition, results, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -134,6 +155,7 @@ def test_two_rank_statistics_reduction_and_weight_exchange(partition):
     owners = {v[2] for v in r0.values()}
     assert owners == {0, 1}
     for i, (lo, hi, owner, a_sum, a_first, a_count, b_sum, b_count) in r0.items():
-        assert lo == hi == 100.0 * i + owner  # the owner's update reached every rank
+        expected = 100.0 * i + owner if exchange == "weights" else 2.0 * i + owner
+        assert lo == hi == expected  # the owner's update reached every rank
         assert a_sum == 1.0 + 2.0 and a_first == 0.0 + 1.0 and a_count == 30
         assert b_sum == 2.0 + 4.0 and b_count == 30
