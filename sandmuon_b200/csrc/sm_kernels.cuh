@@ -524,6 +524,7 @@ __global__ void __launch_bounds__(256)
       dot[r] = 0.0f;
       sq[r] = 0.0f;
     }
+#pragma unroll 2
     for (int i = lane * VEC; i < md.d_in; i += 32 * VEC) {
       float av[VEC], zv[VEC];
       if constexpr (VEC == 4) {

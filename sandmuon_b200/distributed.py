@@ -16,8 +16,12 @@ its own microbatches; at step():
      bytes); every rank, the owner included, subtracts the same rounded delta,
      so the ranks stay bitwise identical.  The rounding (2^-9 relative per
      element) perturbs the update direction far inside its 1e-2 tolerance.
-There is no other data-path collective; gradients are averaged by the
-caller's data-parallel wrapper as usual.
+Gradients are averaged by the caller's data-parallel wrapper as usual, or,
+with reduce_gradients=True on the optimizer, by reduce_gradients below:
+every matrix gradient is reduce-scattered to its owner (half the bytes of an
+all-reduce; only the owner steps that matrix) and the auxiliary gradients are
+all-reduced.  Momentum buffers exist only on a matrix's owner (ZeRO-1 style);
+consolidated_momentum gathers them for a checkpoint in the reference layout.
 """
 from __future__ import annotations
 
@@ -59,13 +63,26 @@ def partition_matrices(named_shapes: dict[str, tuple[int, int]], world: int, how
 EXCHANGES = ("weights", "bf16_delta")
 
 
+def _copy_pairs(pairs, device) -> None:
+    """dst.copy_(src) for same-size CUDA tensors, one library launch per 64."""
+    from .engine import copy_multi
+    copy_multi(pairs, device)
+
+
 class MatrixSharding:
-    def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights"):
+    """copy_fn(pairs, device) performs the packing copies (dst, src) of the
+    gradient reduction and the momentum gather; the default is the library's
+    multi-tensor copy kernel."""
+
+    def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights", copy_fn=None):
         if exchange not in EXCHANGES:
             raise ValueError(f"unknown exchange {exchange!r} (expected one of {EXCHANGES})")
         self.opt = opt
         self.group = group
         self.exchange_mode = exchange
+        self._copy = copy_fn or _copy_pairs
+        self._grad_bufs = None
+        self._aux_bufs = {}
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         shapes = {n: tuple(p.shape) for n, p in opt.named_matrices.items()}
@@ -100,30 +117,120 @@ class MatrixSharding:
         dist.all_reduce(total, group=self.group)
         return total
 
+    # ------------------------------------------------------- gradients
+    def _slots(self):
+        """(shard, {id(p): (owner, offset)}): every matrix at a 4-element
+        aligned offset inside its owner's segment of `shard` elements."""
+        if not hasattr(self, "_slot_map"):
+            offsets, fill = {}, [0] * self.world
+            for p in self.opt.named_matrices.values():
+                r = self.owner(p)
+                offsets[id(p)] = (r, fill[r])
+                fill[r] += (p.numel() + 3) // 4 * 4
+            self._slot_map = (max(fill), offsets)
+        return self._slot_map
+
+    def _average_op(self):
+        """(averages?, op) for an averaging collective: NCCL averages inside
+        the collective; other backends sum, and the caller divides."""
+        avg = dist.get_backend(self.group) == "nccl"
+        return avg, (dist.ReduceOp.AVG if avg else dist.ReduceOp.SUM)
+
+    def reduce_gradients(self, matrix_items, aux_params) -> dict:
+        """Averages gradients over the group.  Matrix gradients are packed by
+        owner and reduce-scattered, so each rank receives the average of the
+        matrices it owns (returned as {id(p): averaged gradient view}; the
+        other ranks' .grad of those matrices stay local).  Auxiliary
+        gradients are all-reduced in place."""
+        if self.world == 1:
+            return {}
+        shard, offsets = self._slots()
+        params = [item[0] for item in matrix_items]
+        device = params[0].device if params else (aux_params[0].device if aux_params else None)
+        out = {}
+        if params:
+            if self._grad_bufs is None or self._grad_bufs[0].device != device:
+                self._grad_bufs = (torch.empty(shard * self.world, dtype=torch.float32, device=device),
+                                   torch.empty(shard, dtype=torch.float32, device=device))
+            send, recv = self._grad_bufs
+            pairs = []
+            for p in params:
+                r, off = offsets[id(p)]
+                pairs.append((send[r * shard + off:r * shard + off + p.numel()], p.grad.reshape(-1)))
+                if r == self.rank:
+                    out[id(p)] = recv[off:off + p.numel()].view_as(p)
+            self._copy(pairs, device)
+            avg, op = self._average_op()
+            dist.reduce_scatter_tensor(recv, send, op=op, group=self.group)
+            if not avg:
+                recv.div_(self.world)
+        if aux_params:
+            total = sum(p.numel() for p in aux_params)
+            buf = self._aux_bufs.get(device)
+            if buf is None or buf.numel() < total:
+                buf = torch.empty(total, dtype=torch.float32, device=device)
+                self._aux_bufs[device] = buf
+            views, off = [], 0
+            for p in aux_params:
+                views.append((buf[off:off + p.numel()], p.grad.reshape(-1)))
+                off += p.numel()
+            self._copy(views, device)
+            flat = buf[:total]
+            avg, op = self._average_op()
+            dist.all_reduce(flat, op=op, group=self.group)
+            if not avg:
+                flat.div_(self.world)
+            self._copy([(g, v) for v, g in views], device)
+        return out
+
+    def consolidated_momentum(self) -> dict:
+        """{id(p): momentum_buffer} of every selected matrix that has one on
+        its owner, all-gathered so every rank holds all of them (the
+        reference's state layout, for a checkpoint)."""
+        shard, offsets = self._slots()
+        params = list(self.opt.named_matrices.values())
+        have = torch.tensor([1 if (self.owns(p) and "momentum_buffer" in self.opt.state.get(p, {})) else 0
+                             for p in params], dtype=torch.int32)
+        device = params[0].device
+        if dist.get_backend(self.group) == "nccl":
+            have = have.to(device)
+        dist.all_reduce(have, group=self.group)
+        have = have.cpu().tolist()
+        send = torch.zeros(shard, dtype=torch.float32, device=device)
+        recv = torch.empty(shard * self.world, dtype=torch.float32, device=device)
+        pairs = []
+        for p, h in zip(params, have):
+            r, off = offsets[id(p)]
+            if h and r == self.rank:
+                pairs.append((send[off:off + p.numel()], self.opt.state[p]["momentum_buffer"].reshape(-1)))
+        if pairs:
+            self._copy(pairs, device)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        out = {}
+        for p, h in zip(params, have):
+            if h:
+                r, off = offsets[id(p)]
+                out[id(p)] = recv[r * shard + off:r * shard + off + p.numel()].view_as(p).clone()
+        return out
+
     # --------------------------------------------------------- weights
     def _layout(self):
         """Static all-gather layout: each rank's owned matrices back to back in
-        its send slot of `shard` floats (every selected matrix, every step)."""
+        its send slot of `shard` elements (every selected matrix, every step)."""
         if self._gather is None:
+            shard, offsets = self._slots()
             params = list(self.opt.named_matrices.values())
-            per_rank = [[] for _ in range(self.world)]
-            for p in params:
-                per_rank[self.owner(p)].append(p)
-            # 4-element alignment keeps every slot 16-byte (FP32) / 8-byte (BF16) aligned
-            shard = max(sum((p.numel() + 3) // 4 * 4 for p in ps) for ps in per_rank)
             device = params[0].device
             dtype = torch.bfloat16 if self.exchange_mode == "bf16_delta" else torch.float32
             send = torch.zeros(shard, dtype=dtype, device=device)
             recv = torch.empty(shard * self.world, dtype=dtype, device=device)
             slots, unpack = {}, []
-            for r, ps in enumerate(per_rank):
-                offset = 0
-                for p in ps:
-                    if r == self.rank:
-                        slots[id(p)] = send[offset:offset + p.numel()].view_as(p)
-                    else:
-                        unpack.append((p, recv[r * shard + offset:r * shard + offset + p.numel()]))
-                    offset += (p.numel() + 3) // 4 * 4
+            for p in params:
+                r, off = offsets[id(p)]
+                if r == self.rank:
+                    slots[id(p)] = send[off:off + p.numel()].view_as(p)
+                else:
+                    unpack.append((p, recv[r * shard + off:r * shard + off + p.numel()]))
             self._gather = (send, recv, slots, unpack)
         return self._gather
 

@@ -32,13 +32,17 @@ class DiagonalWeightedPE(Optimizer):
 
     Extra keywords: `process_group` (torch.distributed group or None) shards
     the S8 work over the group's ranks, `partition` ("lpt" or "layer") picks
-    the owners and `exchange` ("weights" or "bf16_delta") what the owners
-    all-gather; see sandmuon_b200.distributed.
+    the owners, `exchange` ("weights" or "bf16_delta") what the owners
+    all-gather, and `reduce_gradients=True` makes step() average the
+    gradients over the group itself (reduce-scatter of the matrix gradients
+    to their owners, all-reduce of the rest) in place of a data-parallel
+    wrapper's all-reduce; see sandmuon_b200.distributed.
     """
 
     def __init__(self, model: nn.Module, lr: float, *, rank_one_a: bool = False,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
-                 process_group=None, partition: str = "lpt", exchange: str = "weights"):
+                 process_group=None, partition: str = "lpt", exchange: str = "weights",
+                 reduce_gradients: bool = False):
         choose = module_filter or (lambda name, module: isinstance(module, nn.Linear))
         matrices: dict[str, nn.Parameter] = {}
         modules: dict[str, nn.Module] = {}
@@ -81,6 +85,9 @@ class DiagonalWeightedPE(Optimizer):
         self._plans: dict[tuple, engine.StepPlan] = {}
         self._stat_flat: dict = {}
         self._sharding = None
+        if reduce_gradients and process_group is None:
+            raise ValueError("reduce_gradients=True needs a process_group")
+        self._reduce_gradients = bool(reduce_gradients)
         if process_group is not None:
             from .distributed import MatrixSharding
             self._sharding = MatrixSharding(self, process_group, partition=partition, exchange=exchange)
@@ -211,9 +218,12 @@ class DiagonalWeightedPE(Optimizer):
             with torch.enable_grad():
                 loss = closure()
         matrix_items, auxiliary_items = self._collect()
+        averaged = {}
+        if self._reduce_gradients:
+            averaged = self._sharding.reduce_gradients(matrix_items, [p for p, _ in auxiliary_items])
         self._step_auxiliary(auxiliary_items)
         if matrix_items:
-            self._step_matrices(matrix_items)
+            self._step_matrices(matrix_items, averaged)
         if self._sharding is not None:
             self._sharding.exchange(matrix_items)
         return loss
@@ -248,7 +258,10 @@ class DiagonalWeightedPE(Optimizer):
             return matrix_items
         return [item for item in matrix_items if self._sharding.owns(item[0])]
 
-    def _step_matrices(self, matrix_items):
+    def _step_matrices(self, matrix_items, averaged=None):
+        """averaged: {id(p): gradient} replacing p.grad (the group-averaged
+        gradients of the matrices this rank owns)."""
+        averaged = averaged or {}
         device = matrix_items[0][0].device
         _lib.ensure_device(device)
         # statistics of every active source / target (finished on every rank)
@@ -284,15 +297,16 @@ class DiagonalWeightedPE(Optimizer):
         for parameter, source, group in owned:
             if parameter.device != device:
                 raise RuntimeError("sandmuon_b200 expects every selected matrix on one CUDA device")
+            grad = averaged.get(id(parameter), parameter.grad)
             self._require(parameter, "matrix parameters")
-            self._require(parameter.grad, "matrix gradients")
+            self._require(grad, "matrix gradients")
             st = self.state[parameter]
             if "momentum_buffer" not in st:
                 st["momentum_buffer"] = torch.zeros_like(parameter, dtype=torch.float32)
             export = self._sharding.send_slot(parameter) if self._sharding is not None else None
             mats.append((parameter, st["momentum_buffer"], stat_index[("a", id(source))],
                          stat_index[("b", id(parameter))], export))
-            grads.append(parameter.grad)
+            grads.append(grad)
             lrs.append(group["lr"])
         momentum = float(owned[0][2]["momentum"]) if owned else .8
         key = (tuple((m[0].data_ptr(), m[1].data_ptr(), m[2], m[3], 0 if m[4] is None else m[4].data_ptr())
@@ -331,9 +345,28 @@ class DiagonalWeightedPE(Optimizer):
 
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)
+        if self._sharding is not None:
+            # momentum lives only with a matrix's owner (a consolidated
+            # checkpoint carries every matrix's)
+            for parameter in self.named_matrices.values():
+                if not self._sharding.owns(parameter):
+                    self.state.get(parameter, {}).pop("momentum_buffer", None)
         for plan in self._plans.values():
             plan.close()
         self._plans.clear()
+
+    def consolidated_state_dict(self) -> dict:
+        """state_dict() in the reference's layout on every rank of a sharded
+        optimizer: the momentum buffer of each matrix, held only by its owner,
+        is gathered from the owners (a collective: call on every rank).  A
+        single-device optimizer returns state_dict()."""
+        sd = self.state_dict()
+        if self._sharding is None:
+            return sd
+        index = {id(p): i for i, p in enumerate(p for g in self.param_groups for p in g["params"])}
+        for pid, momentum in self._sharding.consolidated_momentum().items():
+            sd["state"].setdefault(index[pid], {})["momentum_buffer"] = momentum
+        return sd
 
     def close(self):
         for handle in self.handles:
@@ -349,6 +382,8 @@ class RankOneAWeightedPE(DiagonalWeightedPE):
 
     def __init__(self, model: nn.Module, lr: float, *,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
-                 process_group=None, partition: str = "lpt", exchange: str = "weights"):
+                 process_group=None, partition: str = "lpt", exchange: str = "weights",
+                 reduce_gradients: bool = False):
         super().__init__(model, lr, rank_one_a=True, module_filter=module_filter,
-                         process_group=process_group, partition=partition, exchange=exchange)
+                         process_group=process_group, partition=partition, exchange=exchange,
+                         reduce_gradients=reduce_gradients)

@@ -159,3 +159,68 @@ def test_two_rank_statistics_reduction_and_weight_exchange(partition, exchange):
         assert lo == hi == expected  # the owner's update reached every rank
         assert a_sum == 1.0 + 2.0 and a_first == 0.0 + 1.0 and a_count == 30
         assert b_sum == 2.0 + 4.0 and b_count == 30
+
+
+def _torch_copy(pairs, device):
+    """Test-only stand-in for the library's multi-tensor copy kernel."""
+    for dst, src in pairs:
+        dst.copy_(src.reshape(dst.shape))
+
+
+def _grad_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        model = gpt_matrix_model(3, 16, 64)
+        opt = _StubOptimizer(model)
+        sharding = MatrixSharding(opt, dist.group.WORLD, partition="lpt", copy_fn=_torch_copy)
+        params = list(opt.named_matrices.values())
+        aux = [torch.nn.Parameter(torch.zeros(5, 3)), torch.nn.Parameter(torch.zeros(7))]
+        for i, p in enumerate(params):
+            p.grad = torch.full_like(p, float(i + 1) * (rank + 1))     # rank-dependent gradients
+        for i, p in enumerate(aux):
+            p.grad = torch.full_like(p, 10.0 * (i + 1) * (rank + 1))
+        index = {id(p): i for i, p in enumerate(params)}
+        averaged = sharding.reduce_gradients([(p, p, {}) for p in params], aux)
+        out = {"owned": sorted(index[k] for k in averaged),
+               "avg": {index[k]: (float(v.min()), float(v.max())) for k, v in averaged.items()},
+               "aux": [(float(p.grad.min()), float(p.grad.max())) for p in aux]}
+        # momentum only on owners; the consolidated gather gives every rank all of them
+        for i, p in enumerate(params):
+            if sharding.owns(p):
+                opt.state.setdefault(p, {})["momentum_buffer"] = torch.full_like(p, 0.5 * i)
+        moms = sharding.consolidated_momentum()
+        out["moms"] = {index[k]: (float(v.min()), float(v.max())) for k, v in moms.items()}
+        out["owners"] = [sharding.owner(p) for p in params]
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gradient_reduce_scatter_and_momentum_gather():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_grad_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0, r1 = results[0], results[1]
+    owners = r0["owners"]
+    assert owners == r1["owners"] and set(owners) == {0, 1}
+    for rank, res in ((0, r0), (1, r1)):
+        # each rank receives the average (1 and 2 times (i + 1) -> 1.5 (i + 1)) of exactly its matrices
+        assert res["owned"] == [i for i, o in enumerate(owners) if o == rank]
+        for i, (lo, hi) in res["avg"].items():
+            assert lo == hi == 1.5 * (i + 1)
+        # auxiliary gradients are averaged in place on every rank
+        assert res["aux"] == [(15.0, 15.0), (30.0, 30.0)]
+        # every matrix's momentum (0.5 i, set by its owner) reaches every rank
+        assert sorted(res["moms"]) == list(range(len(owners)))
+        for i, (lo, hi) in res["moms"].items():
+            assert lo == hi == 0.5 * i
