@@ -247,8 +247,9 @@ int sm_apply_bf16_delta_multi(const SmDeltaSpec* items, int32_t count, void* str
 size_t sm_s8_workspace_bytes(int32_t batch, int32_t rows, int32_t cols);
 
 /* out[b] = S8(x[b]) for a contiguous FP32 batch [batch, rows, cols]; the same
- * oriented pipeline the plan runs (transposes when rows > cols). All-zero
- * matrices give exact zeros.  Replaces _s8_fp32 (sandmuon/optimizer.py:69-93). */
+ * oriented pipeline the plan runs (transposes when rows > cols), whose last
+ * stage rounds its output to BF16. All-zero matrices give exact zeros.
+ * Replaces _s8_fp32 (sandmuon/optimizer.py:69-93). */
 int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t cols,
                 void* workspace, size_t workspace_bytes, void* stream);
 

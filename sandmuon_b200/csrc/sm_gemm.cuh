@@ -68,14 +68,16 @@ struct GemmProblem {
   void* out0;           // [batch, m, n] FP32 or BF16 (hi plane for hi/lo outputs)
   void* out1;           // lo plane for hi/lo outputs
   const float* alpha;   // [batch] scale of the accumulator, or null (= 1)
+  // aux / aux_lo / pa / pb / pc: the polynomial epilogues, reachable through
+  // sm_gemm_bf16 (the optimizer's S8 uses scale / diag with a shifted gram)
   const __nv_bfloat16* aux;     // [batch, m, n] BF16 gram (hi plane) for the poly epilogues
   const __nv_bfloat16* aux_lo;  // lo plane of the gram for the hi/lo poly epilogue
   float pa, pb, pc;     // poly coefficients: out = pa*I + pb*gram + pc*acc
   float scale;          // F32 / BF16 / hi-lo epilogues: out = scale*alpha*acc + diag*I
   float diag;
   float* partials;      // [batch, tiles_m*tiles_n*kNormSlots] sum of squares (F32Norm)
-  const int* tmask;     // [batch] or null: 1 = store this matrix's FP32 result
-                        // transposed ([n, m], row stride m) -- F32 epilogue only
+  const int* tmask;     // [batch] or null: 1 = store this matrix's result transposed
+                        // ([n, m], row stride m) -- F32 and BF16 epilogues only
 };
 
 struct GemmLaunch {
@@ -497,7 +499,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
         // off-diagonal tile of a symmetric product or a matrix whose FP32
         // result is stored transposed, of its transpose (rows col0.., cols
         // row0..), read from the staging tile by columns.
-        const bool tout = (EPI == kEpiF32) && P.tmask != nullptr && P.tmask[tc.b] != 0;
+        const bool tout = (EPI == kEpiF32 || EPI == kEpiBF16) && P.tmask != nullptr && P.tmask[tc.b] != 0;
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
           if (pass == 0 && tout) continue;
@@ -532,7 +534,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_bf16(const __grid_cons
               float x[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) x[e] = pass == 0 ? stg[rr * 33 + c8 + e] : stg[(c8 + e) * 33 + rr];
-              const size_t off = static_cast<size_t>(orow0 + rr) * P.n + ocol0 + c8;
+              const size_t ld = tout ? P.m : P.n;
+              const size_t off = static_cast<size_t>(orow0 + rr) * ld + ocol0 + c8;
               if (kTwo) {
                 float h[8], l[8];
 #pragma unroll

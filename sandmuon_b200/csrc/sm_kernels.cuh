@@ -796,7 +796,7 @@ __device__ __forceinline__ int64_t q_ld(const MatDev& md, int64_t rp, int64_t cp
 
 template <bool RANK1>
 __global__ void __launch_bounds__(256)
-    k_mapback_rowstats(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+    k_mapback_rowstats(const MatDev* __restrict__ mats, const __nv_bfloat16* __restrict__ q, int64_t rp, int64_t cp,
                        float2* __restrict__ out, int ld_out, float* __restrict__ gamma,
                        unsigned* __restrict__ tickets) {
   grid_dep_wait();
@@ -810,7 +810,7 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   float2* outb = out + static_cast<int64_t>(b) * ld_out;
   if (obase < md.d_out) {
-    const float* qr[kMapbackRows];
+    const __nv_bfloat16* qr[kMapbackRows];
     float t[kMapbackRows], s1[kMapbackRows], s2[kMapbackRows];
 #pragma unroll
     for (int r = 0; r < kMapbackRows; ++r) {
@@ -831,8 +831,8 @@ __global__ void __launch_bounds__(256)
       }
 #pragma unroll
       for (int r = 0; r < kMapbackRows; ++r) {
-        const float4 v = *reinterpret_cast<const float4*>(qr[r] + i);
-        const float vv[4] = {v.x, v.y, v.z, v.w};
+        const uint2 v = *reinterpret_cast<const uint2*>(qr[r] + i);
+        const float vv[4] = {bf16_lo_to_f(v.x), bf16_hi_to_f(v.x), bf16_lo_to_f(v.y), bf16_hi_to_f(v.y)};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           s1[r] += aa[e] * vv[e] * vv[e];
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(256)
       const float z = RANK1 ? md.z_a[i] : 0.f;
 #pragma unroll
       for (int r = 0; r < kMapbackRows; ++r) {
-        const float v = qr[r][i];
+        const float v = __bfloat162float(qr[r][i]);
         s1[r] += a2 * v * v;
         if (RANK1) {
           t[r] += z * v;
@@ -887,13 +887,13 @@ __global__ void __launch_bounds__(256)
 // in 16-byte groups when d_in % 4 == 0, else element by element.
 template <bool RANK1, bool VEC4>
 __global__ void __launch_bounds__(256)
-    k_mapback_apply(const MatDev* __restrict__ mats, const float* __restrict__ q, int64_t rp, int64_t cp,
+    k_mapback_apply(const MatDev* __restrict__ mats, const __nv_bfloat16* __restrict__ q, int64_t rp, int64_t cp,
                     const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma) {
   grid_dep_wait();
   grid_dep_launch();
   const int b = blockIdx.y;
   const MatDev md = mats[b];
-  const float* qb = q + static_cast<int64_t>(b) * rp * cp;
+  const __nv_bfloat16* qb = q + static_cast<int64_t>(b) * rp * cp;
   const int64_t ldq = q_ld(md, rp, cp);
   const float step = md.lr * gamma[b];
   const float coef = RANK1 ? md.scal_a[0] : 0.0f;
@@ -907,7 +907,9 @@ __global__ void __launch_bounds__(256)
     const float ct = RANK1 ? coef * rs[static_cast<int64_t>(b) * ld_rs + o].x : 0.0f;
     if (VEC4) {
       const int i = col * 4;
-      const float4 v = *reinterpret_cast<const float4*>(qb + static_cast<int64_t>(o) * ldq + i);
+      const uint2 raw = *reinterpret_cast<const uint2*>(qb + static_cast<int64_t>(o) * ldq + i);
+      const float4 v = make_float4(bf16_lo_to_f(raw.x), bf16_hi_to_f(raw.x), bf16_lo_to_f(raw.y),
+                                   bf16_hi_to_f(raw.y));
       const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
       float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
       if (RANK1) z = *reinterpret_cast<const float4*>(md.z_a + i);
@@ -932,7 +934,7 @@ __global__ void __launch_bounds__(256)
         *reinterpret_cast<float4*>(md.export_to + static_cast<int64_t>(o) * md.d_in + i) = w;
     } else {
       const int i = col;
-      float v = qb[static_cast<int64_t>(o) * ldq + i];
+      float v = __bfloat162float(qb[static_cast<int64_t>(o) * ldq + i]);
       if (RANK1) v += ct * md.z_a[i];
       const float u = (v * ib) * md.inv_a[i];
       const int64_t wi = static_cast<int64_t>(o) * md.d_in + i;
