@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of one SandMuon optimizer step on B200 (config 1 of the baseline).
 
-Workload (the default): the 9-layer x 768 GPT matrix
+Workload (benchmark configuration 1, the default): the 9-layer x 768 GPT matrix
 set -- per layer q/k/v/o 768x768, mlp.c_fc 3072x768, mlp.c_proj 768x3072, 54
 matrices, 63,700,992 FP32 parameters -- under RankOneAWeightedPE.  Gradients
 ~ N(0, 1e-4^2), weights ~ N(0, 0.02^2), and the hook statistics of 8
@@ -21,10 +21,10 @@ of neighbouring steps overlapped on separate streams (e2e.serial_value: the
 same with every copy and step on one stream).
 
 Other workloads (not the contract line): cfg4 = the same step on the 24-layer
-x 2048 matrix set (144 matrices); cfg3 = the S8 sweep of BASELINE configs[3]
+x 2048 matrix set (144 matrices); cfg3 = the S8 sweep of configuration 3
 (one line per shape: S8 TFLOP/s and error against an FP32 torch restatement,
 plus one optimizer step of each class); cfg2 = the GPT-2 training step of
-BASELINE configs[2] (tokens/s, hooks on real activations, fused AdamW beside
+configuration 2 (tokens/s, hooks on real activations, fused AdamW beside
 it); stats = the hook statistic
 reductions of one config-1 microbatch (HBM GB/s, FP32 and BF16 inputs).
 """
@@ -481,7 +481,7 @@ def run_cfg3(args, device):
 # ------------------------------------------- config 2: GPT-2 training step
 
 def run_cfg2(args, device):
-    """a GPT-2-style decoder (9 layers, width 768, 12 heads,
+    """Benchmark configuration 2: a GPT-2-style decoder (9 layers, width 768, 12 heads,
     vocab 50257, context 1024) trained on uniform random tokens, batch 128 as
     8 microbatches of 16, BF16 autocast forward/backward, FP32 weights.
     RankOneAWeightedPE takes the 54 block Linear weights (its hooks reduce the

@@ -134,7 +134,7 @@ class GPT2Block(nn.Module):
 
 
 class GPT2(nn.Module):
-    """GPT-2-style decoder of BASELINE config 2 (historical parameter names, so
+    """GPT-2-style decoder of benchmark configuration 2 (historical parameter names, so
     q/k/v statistic sharing applies): token and position embeddings, pre-LN
     blocks of bias-free Linear layers, final LayerNorm, and an output head
     tied to the token embedding.  Random initialisation (N(0, 0.02^2)); the

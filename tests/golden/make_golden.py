@@ -1,14 +1,14 @@
 """Generates the golden fixtures in tests/golden/ by running the REFERENCE.
 
-Run in a container where the reference checkout exists (default
-/root/reference, override with SANDMUON_REFERENCE):
+Run where a checkout of the SandMuon project exists, naming its root:
 
-    python tests/golden/make_golden.py
+    SANDMUON_REFERENCE=<checkout> python tests/golden/make_golden.py [fixture ...]
 
 It imports the reference package under the module name `sandmuon_ref` (to
 avoid clashing with any other `sandmuon`), evaluates its public helpers and
 optimizers on seeded inputs, and writes compressed .npz files next to this
-script.  The GPU box never runs this script; tests only read the fixtures.
+script.  The GPU test machines never run this script; tests only read the
+fixtures.
 """
 from __future__ import annotations
 
@@ -26,7 +26,10 @@ from mini_models import MiniGPT  # noqa: E402
 
 
 def load_reference():
-    root = Path(os.environ.get("SANDMUON_REFERENCE", "/root/reference")) / "sandmuon"
+    checkout = os.environ.get("SANDMUON_REFERENCE")
+    if not checkout:
+        raise SystemExit("set SANDMUON_REFERENCE to the root of a SandMuon checkout")
+    root = Path(checkout) / "sandmuon"
     spec = importlib.util.spec_from_file_location("sandmuon_ref", root / "__init__.py",
                                                   submodule_search_locations=[str(root)])
     module = importlib.util.module_from_spec(spec)

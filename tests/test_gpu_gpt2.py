@@ -1,5 +1,5 @@
-"""The drop-in optimizer inside a real training loop (BASELINE config 2 at a
-small size): a GPT-2-style decoder with fused causal attention, BF16 autocast
+"""The drop-in optimizer inside a real training loop (benchmark configuration
+2 at a small size): a GPT-2-style decoder with fused causal attention, BF16 autocast
 forward/backward over several microbatches, tied embeddings and LayerNorms on
 the AdamW auxiliaries.  Checks that the hooks' statistics equal torch
 reductions of the tensors they saw (1e-5 relative), that q/k/v share one

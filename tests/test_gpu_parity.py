@@ -1,6 +1,6 @@
 """End-to-end parity of the CUDA optimizer with the reference.
 
-Bars: hook statistics within 1e-5 relative; per-matrix
+Bars (the path's stated tolerances): hook statistics within 1e-5 relative; per-matrix
 update direction (W_before - W_after) / lr within 1e-2 relative Frobenius
 error and cosine >= 0.999 of the reference FP32 path.
   * mini-GPT replays of the reference's own recorded runs (golden fixtures)
