@@ -40,12 +40,38 @@ def test_binding_signatures_cover_the_header(built_library):
     assert lib.sm_version() == 2
 
 
-def test_ctypes_structs_match_c_layout():
+STRUCTS = ("SmMatrixSpec", "SmStatSpec", "SmPlanSpec", "SmStepArgs", "SmCopySpec", "SmDeltaSpec", "SmAdamTensor")
+
+
+def test_ctypes_structs_match_c_layout(tmp_path):
+    """Every POD struct of the header: the ctypes binding has the size and the
+    field offsets gcc computes for the C declaration."""
+    import json
+    import shutil
+    import subprocess
     from sandmuon_b200 import _lib
-    assert ctypes.sizeof(_lib.SmMatrixSpec) == 40
-    assert ctypes.sizeof(_lib.SmStatSpec) == 40
-    assert ctypes.sizeof(_lib.SmAdamTensor) == 48
-    assert ctypes.sizeof(_lib.SmStepArgs) == 40
+    gcc = shutil.which("gcc") or shutil.which("cc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "sandmuon_b200.h"', "int main(void) {",
+             '  printf("{");']
+    for i, name in enumerate(STRUCTS):
+        fields = [f for f, _ in getattr(_lib, name)._fields_]
+        offs = ", ".join(f'\\"{f}\\": %zu' for f in fields)
+        args = ", ".join(f"offsetof({name}, {f})" for f in fields)
+        sep = "," if i else ""
+        lines.append(f'  printf("{sep}\\"{name}\\": {{\\"size\\": %zu, {offs}}}", sizeof({name}), {args});')
+    lines += ['  printf("}\\n");', "  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    c_layout = json.loads(subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout)
+    for name in STRUCTS:
+        cls = getattr(_lib, name)
+        assert c_layout[name]["size"] == ctypes.sizeof(cls), name
+        for field, _ in cls._fields_:
+            assert c_layout[name][field] == getattr(cls, field).offset, (name, field)
 
 
 def test_engine_constants_match_package_constants():
