@@ -5,7 +5,7 @@
 //   N3  k_whiten_rowstats / k_whiten_write     : Nesterov momentum, two-sided
 //                                                whitening, stage-1 hi/lo split
 //   N5  k_poly_stage1                          : first S8 polynomial (hi/lo)
-//   N7  k_mapback_rowstats_* / k_mapback_apply : mapback, graft, weight update
+//   N7  k_mapback_rowstats / k_mapback_apply   : mapback, graft, weight update
 //   N8  k_adamw_multi                          : auxiliary AdamW
 //   --  k_reduce_*                             : per-matrix scalar reductions
 //
