@@ -148,3 +148,77 @@ def test_mini_gpt_three_steps_match_reference(variant):
         with torch.no_grad():
             for n, p in model.named_parameters():
                 p.copy_(torch.from_numpy(weights[n]))
+
+
+def test_oracle_follows_reference_gpt2_training_run():
+    """The oracle as the optimizer of the small config-2 GPT-2 model (FP32 torch
+    forward/backward on CPU, hooks feeding add_a / add_b): every step's loss
+    and the recorded matrices after the last step match the reference
+    optimizer's own run (tests/golden/gpt2_small.npz)."""
+    import re
+
+    import torch
+
+    from sandmuon_b200.workloads import GPT2, gpt2_matrix_filter
+    g = load("gpt2_small.npz")
+    steps, lr = int(g["steps"]), float(g["lr"])
+    torch.manual_seed(0)
+    model = GPT2(layers=2, width=128, heads=4, vocab=512, context=64)
+    params = dict(model.named_parameters())
+    with torch.no_grad():
+        for n, p in params.items():
+            p.copy_(torch.from_numpy(g[f"init/{n}"]))
+    modules = {n + ".weight": m for n, m in model.named_modules() if gpt2_matrix_filter(n, m)}
+    sharing = re.compile(r"^(transformer\.h\.\d+\.attn\.)[kv]_proj\.weight$")
+    source = {}
+    for n in modules:
+        m = sharing.match(n)
+        source[n] = m.group(1) + "q_proj.weight" if m else n
+    aux = [n for n in params if n not in modules]
+    oracle = orc.OracleSandMuon({n: tuple(params[n].shape) for n in modules}, source, aux, rank_one_a=True, lr=lr)
+    captured_a, captured_b = {}, {}
+
+    def hook(name):
+        def fwd(module, inputs, output):
+            if source[name] == name:
+                captured_a.setdefault(name, []).append(inputs[0].detach().reshape(-1, inputs[0].shape[-1]).numpy())
+            output.register_hook(lambda grad: captured_b.setdefault(name, []).append(
+                grad.detach().reshape(-1, grad.shape[-1]).numpy()))
+        return fwd
+
+    handles = [m.register_forward_hook(hook(n)) for n, m in modules.items()]
+    batches = [torch.from_numpy(g[f"tokens/{i}"]) for i in range(2)]
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)  # the fixture was recorded single-threaded
+    try:
+        for s in range(steps):
+            captured_a.clear()
+            captured_b.clear()
+            model.zero_grad(set_to_none=True)
+            total = 0.0
+            for b in batches:
+                logits = model(b[:, :-1])
+                loss = torch.nn.functional.cross_entropy(logits.reshape(-1, 512), b[:, 1:].reshape(-1)) / 2
+                loss.backward()
+                total += float(loss.detach())
+            assert abs(total - float(g[f"loss/{s}"])) / float(g[f"loss/{s}"]) < 1e-4, (s, total)
+            for n, rows in captured_a.items():
+                for r in rows:
+                    oracle.add_a(n, r)
+            for n, rows in captured_b.items():
+                for r in rows:
+                    oracle.add_b(n, r)
+            weights = {n: p.detach().numpy().copy() for n, p in params.items()}
+            grads = {n: p.grad.detach().numpy() for n, p in params.items() if p.grad is not None}
+            oracle.step(weights, grads)
+            with torch.no_grad():
+                for n, p in params.items():
+                    p.copy_(torch.from_numpy(weights[n]))
+    finally:
+        torch.set_num_threads(threads)
+        for h in handles:
+            h.remove()
+    for key in g:
+        if key.startswith("final/"):
+            n = key[len("final/"):]
+            assert rel(params[n].detach().numpy() - g[f"init/{n}"], g[key] - g[f"init/{n}"]) < 1e-3, n
