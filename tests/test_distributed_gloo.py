@@ -224,3 +224,60 @@ def test_two_rank_gradient_reduce_scatter_and_momentum_gather():
         assert sorted(res["moms"]) == list(range(len(owners)))
         for i, (lo, hi) in res["moms"].items():
             assert lo == hi == 0.5 * i
+
+
+def _sparse_worker(rank, world, port, results):
+    """More ranks than matrices: some ranks own nothing."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        model = gpt_matrix_model(1, 8, 16)            # 6 matrices over 8 ranks
+        opt = _StubOptimizer(model)
+        sharding = MatrixSharding(opt, dist.group.WORLD, partition="lpt", copy_fn=_torch_copy)
+        params = list(opt.named_matrices.values())
+        for i, p in enumerate(params):
+            p.grad = torch.full_like(p, float(i + 1) * (rank + 1))
+        averaged = sharding.reduce_gradients([(p, p, {}) for p in params], [])
+        send, recv, slots, unpack = sharding._layout()
+        with torch.no_grad():
+            for i, p in enumerate(params):
+                if sharding.owns(p):
+                    p.fill_(10.0 * i)
+                    slots[id(p)].copy_(p)
+            dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
+            for p, src in unpack:
+                p.copy_(src.view_as(p))
+        for i, p in enumerate(params):
+            if sharding.owns(p):
+                opt.state.setdefault(p, {})["momentum_buffer"] = torch.full_like(p, float(i))
+        moms = sharding.consolidated_momentum()
+        results[rank] = {"owned": sum(sharding.owns(p) for p in params),
+                         "avg": sorted(float(v.mean()) for v in averaged.values()),
+                         "weights": [float(p.mean()) for p in params],
+                         "moms": sorted(float(v.mean()) for v in moms.values())}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_more_ranks_than_matrices():
+    world = 8
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_sparse_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    owned = [results[r]["owned"] for r in range(world)]
+    assert sum(owned) == 6 and owned.count(0) == 2
+    mean_factor = sum(r + 1 for r in range(world)) / world        # 4.5
+    for r in range(world):
+        res = results[r]
+        assert len(res["avg"]) == owned[r]
+        assert all(any(abs(v - mean_factor * (i + 1)) < 1e-5 for i in range(6)) for v in res["avg"])
+        assert res["weights"] == [10.0 * i for i in range(6)]      # every rank received every owner's matrix
+        assert res["moms"] == [float(i) for i in range(6)]
