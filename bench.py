@@ -223,6 +223,30 @@ def make_refill(opt, stats, rows, device):
     return refill, flat.numel() * 4
 
 
+def agreed_max(value, device, world):
+    """The maximum of a per-rank float over all ranks (the value itself for
+    one rank); a collective, called by every rank at the same point."""
+    if world <= 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def check_device_status(device, world, where):
+    """Reads (and clears) every rank's device status word and raises on all
+    ranks together when any bounded wait of a library kernel ran out, so a
+    stuck rank ends the run with a diagnosis instead of leaving its peers in
+    a collective until the process-group timeout.  A collective."""
+    from sandmuon_b200 import _lib
+    status = _lib.device_status(device)
+    worst = int(agreed_max(float(status), device, world))
+    if worst != 0:
+        raise RuntimeError(f"a library kernel reported a device-side timeout {where} (status 0x{worst:x} on "
+                           f"at least one of {world} rank(s); this rank 0x{status:x}): no bench line")
+
+
 def time_steps(opt, refill, steps, device, host=None):
     """Device ms per step (CUDA events); `host`, a list, receives the host
     ms per step spent issuing the steps (before the final synchronise)."""
@@ -671,7 +695,7 @@ def main():
     torch.cuda.set_device(device)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         group = dist.group.WORLD
     model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition, args.workload,
                                                        args.exchange)
@@ -692,14 +716,12 @@ def main():
         refill()
         opt.step()
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
+    check_device_status(device, world, "after warm-up")
     t0 = time.monotonic()
     host_ms = []
     ms = time_steps(opt, refill, args.steps, device, host_ms)
     sampler.mark(t0, time.monotonic())
-    if world > 1:
-        dist.barrier()
+    check_device_status(device, world, "after the timed steps")
     plan = opt._last_plan
     launches = plan.launches_per_step()
 
@@ -725,18 +747,20 @@ def main():
     e2e_ms = e2e_pipelined(opt, params, host_g, refill, args.steps, device)
     sampler.mark(t0, time.monotonic())
 
-    # keep the GPU under the same load for ~1 s more so clocks are sampled
+    # Keep the GPU under the same load for ~1 s more so clocks are sampled.
+    # Every step holds collectives, so all ranks must run the same number of
+    # steps: the count comes from the slowest rank's step time, never from a
+    # rank's own wall clock (ranks that leave such a loop at different
+    # iterations pair one rank's step collectives with another's final
+    # all-reduce and hang until the process-group timeout).
+    ms_max = agreed_max(ms, device, world)
     t0 = time.monotonic()
-    while time.monotonic() - t0 < 1.0:
-        time_steps(opt, refill, 5, device)
+    time_steps(opt, refill, max(5, int(1000.0 / max(ms_max, 1e-3))), device)
     sampler.mark(t0, time.monotonic())
     clocks = sampler.summary()
 
     # a bounded device-side wait that ran out makes every number above meaningless
-    from sandmuon_b200 import _lib
-    status = _lib.device_status(device)
-    if status != 0:
-        raise RuntimeError(f"a kernel reported a device-side timeout (status {status}): no bench line")
+    check_device_status(device, world, "after the timed loops")
 
     # [max: ms, e2e, gemm ms] [sum: gemm flops, gemm ms]: each rank executes only the S8
     # work of the matrices it owns, so the per-GPU tensor rate is sum(flops) / sum(GEMM ms)

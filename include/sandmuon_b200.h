@@ -104,9 +104,12 @@ int sm_stats_accumulate(const void* rows, int dtype, int64_t n_rows, int64_t n_c
  * work.  The first call on a device looks the array's device address up
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * Each device has its own copy of the array, shared by every call on that
- * device; a call overwrites the partial sums the previous call left there
- * before reading them, so nothing needs clearing, but calls that overlap on
- * the GPU (for example on two streams) race: keep them in one stream order. */
+ * device and keeping what the last call left there.  A call overwrites the
+ * partial sums before reading them and clears the completion counters it
+ * uses (cudaMemsetAsync on its stream, which allocates nothing), so nothing
+ * from an earlier call leaks into a later one; but calls that overlap on the
+ * GPU (for example on two streams) race on the array and may return wrong
+ * sums: keep them in one stream order. */
 #define SM_STATS_NOALLOC_SCRATCH_FLOATS (1 << 19)
 #define SM_STATS_NOALLOC_MAX_COLS (SM_STATS_NOALLOC_SCRATCH_FLOATS / 2)
 int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int64_t n_cols,

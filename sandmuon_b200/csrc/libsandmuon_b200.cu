@@ -1222,8 +1222,7 @@ static int stats_tma_launch(const CUtensorMap& map, const StatsTmaArgs& args, in
 
 // Runs the TMA path when the input qualifies and the partial capacity
 // suffices; *done says whether it ran.
-// zero_tickets: clear the call's tickets first (a caller workspace); the
-// library-owned no-allocation tickets are zero already.
+// zero_tickets: clear the call's tickets first, in stream order.
 template <typename T>
 static int stats_tma_run(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
                          float* sum, unsigned* tickets, bool zero_tickets, float* partials, int64_t partial_floats,
@@ -1288,7 +1287,9 @@ static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, 
 // a pointer: its device address comes from cudaGetSymbolAddress, looked up
 // once per device with that device current.
 static __device__ __align__(256) float g_noalloc_scratch[SM_STATS_NOALLOC_SCRATCH_FLOATS];
-// tickets of the TMA path: zero at module load, left zero by every call
+// last-CTA tickets of the TMA path; each call clears the ones it uses
+// (cudaMemsetAsync, in stream order) before its kernel, so a ticket left
+// non-zero by two overlapping calls cannot affect later ones
 static __device__ __align__(256) unsigned g_noalloc_tickets[kStatsTicketWords];
 static std::mutex g_noalloc_mutex;
 static float* g_noalloc_addr[64] = {};
@@ -1316,12 +1317,13 @@ static int noalloc_scratch_address(float** out, unsigned** tickets) {
 
 // Same kernels as stats_launch; the number of row splits is capped so the
 // partials fit the fixed scratch array.  Every partial is written before it
-// is read, so stale contents never leak.
+// is read, so stale contents never leak; the TMA path's tickets are cleared
+// by each call (a memset allocates nothing).
 template <typename T>
 static int stats_launch_noalloc(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int64_t cs, float* sum_sq,
                                 float* sum, float* scratch, unsigned* tickets, cudaStream_t st, int sms) {
   bool done = false;
-  SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, false, scratch,
+  SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, true, scratch,
                        static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS), st, sms, &done));
   if (done) return SM_OK;
   const int64_t per_split = n_cols * (sum ? 2 : 1);

@@ -71,8 +71,9 @@ def _copy_pairs(pairs, device) -> None:
 
 class MatrixSharding:
     """copy_fn(pairs, device) performs the packing copies (dst, src) of the
-    gradient reduction and the momentum gather; the default is the library's
-    multi-tensor copy kernel."""
+    gradient reduction and the momentum gather, and the scatter of gathered
+    weights in the exchange; the default is the library's multi-tensor copy
+    kernel."""
 
     def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights", copy_fn=None):
         if exchange not in EXCHANGES:
@@ -248,19 +249,27 @@ class MatrixSharding:
         return self._layout()[2][id(parameter)]
 
     def exchange(self, matrix_items) -> None:
-        """All-gathers every matrix from its owner into all ranks.  The owners'
-        send slots were filled by the update kernel itself; the received
-        weights are scattered back with one multi-tensor copy launch, or the
-        received BF16 deltas of the matrices stepped now are subtracted with
-        one multi-tensor launch."""
+        """All-gathers the owners' send slots into all ranks and applies the
+        matrices stepped now.  The owners' send slots were filled by the update
+        kernel itself; the received weights are scattered back with one
+        multi-tensor copy launch, or the received BF16 deltas are subtracted
+        with one multi-tensor launch.
+
+        Only matrices in `matrix_items` (those with a gradient this step) are
+        unpacked: the slot of a matrix its owner did not step holds nothing
+        (zeros before its first step, an older value after), so copying it
+        would overwrite the other ranks' current weights.  The all-gather runs
+        on every rank whenever step() runs, whatever was stepped, so the ranks'
+        collectives stay paired; with data-parallel gradients every rank has
+        the same set of matrices with a gradient."""
         if self.world == 1:
             return
-        from .engine import apply_bf16_delta_multi, copy_multi
+        from .engine import apply_bf16_delta_multi
         send, recv, slots, unpack = self._layout()
         dist.all_gather_into_tensor(recv, send, group=self.group)
+        stepped = {id(item[0]) for item in matrix_items}
+        pairs = [(p.detach(), src) for p, src in unpack if id(p) in stepped]
         if self.exchange_mode == "bf16_delta":
-            # only the matrices stepped now: a skipped matrix's slot holds an old delta
-            stepped = {id(item[0]) for item in matrix_items}
-            apply_bf16_delta_multi([(p.detach(), src) for p, src in unpack if id(p) in stepped], recv.device)
+            apply_bf16_delta_multi(pairs, recv.device)
         else:
-            copy_multi([(p.detach(), src) for p, src in unpack], recv.device)
+            self._copy(pairs, recv.device)

@@ -281,3 +281,62 @@ def test_more_ranks_than_matrices():
         assert all(any(abs(v - mean_factor * (i + 1)) < 1e-5 for i in range(6)) for v in res["avg"])
         assert res["weights"] == [10.0 * i for i in range(6)]      # every rank received every owner's matrix
         assert res["moms"] == [float(i) for i in range(6)]
+
+
+def _skip_worker(rank, world, port, results):
+    """exchange() with a matrix that has no gradient this step: its owner does
+    not step it, and no rank may overwrite its weights from the stale slot."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        model = gpt_matrix_model(2, 16, 64)
+        opt = _StubOptimizer(model)
+        sharding = MatrixSharding(opt, dist.group.WORLD, partition="lpt", copy_fn=_torch_copy)
+        params = list(opt.named_matrices.values())
+        skipped = {0, 5}                      # e.g. an unused layer: grad None on every rank
+        slots = sharding._layout()[2]
+        history = []
+        for step in range(2):
+            stepped = [i for i in range(len(params)) if i not in skipped or step == 1]
+            with torch.no_grad():
+                if step == 0:
+                    for i, p in enumerate(params):
+                        p.fill_(-1.0 - i)     # the weights every rank starts from
+                for i in stepped:
+                    p = params[i]
+                    if sharding.owns(p):      # test-only compute stub: the owner's update
+                        p.fill_(100.0 * i + 10.0 * step + sharding.rank)
+                        slots[id(p)].copy_(p)
+            sharding.exchange([(params[i], params[i], {}) for i in stepped])
+            history.append([float(p.min()) for p in params] + [float(p.max()) for p in params])
+        results[rank] = {"history": history, "owners": [sharding.owner(p) for p in params]}
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_keeps_weights_of_matrices_without_gradient():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_skip_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r0, r1 = results[0], results[1]
+    assert r0 == r1
+    owners = r0["owners"]
+    n = len(owners)
+    assert {owners[0], owners[5]} <= {0, 1}
+    for step, row in enumerate(r0["history"]):
+        lo, hi = row[:n], row[n:]
+        for i in range(n):
+            if i in (0, 5) and step == 0:
+                expected = -1.0 - i            # not stepped: every rank keeps its weights
+            else:
+                expected = 100.0 * i + 10.0 * step + owners[i]
+            assert lo[i] == hi[i] == expected, (step, i, lo[i], hi[i], expected)

@@ -197,3 +197,92 @@ def test_config1_gpt9_step_matches_oracle():
                 assert rel(npy(opt.state[opt.named_matrices[n]][key]), oracle.state[n][key]) < STAT_REL
         assert rel(npy(opt.state[opt.named_matrices[n]]["b_ema"]), oracle.state[n]["b_ema"]) < STAT_REL
     opt.close()
+
+
+def test_config1_three_steps_follow_oracle():
+    """Config 1 over three steps, each with fresh gradients and statistics:
+    momentum and the statistic EMAs carry across steps.  Every step's
+    direction of every matrix, and the final momenta and EMAs, against the
+    oracle run on the same inputs.  The direction depends on the momentum and
+    statistics only, so the GPU weights need no teacher forcing."""
+    from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    torch.manual_seed(1337)
+    model = gpt_matrix_model(9, 768, 3072).to(DEV)
+    opt = RankOneAWeightedPE(model, lr=1e-2)
+    names = list(opt.named_matrices)
+    sources = {n: opt.parameter_names[id(opt.a_sources[id(p)])] for n, p in opt.named_matrices.items()}
+    oracle = orc.OracleSandMuon({n: tuple(p.shape) for n, p in opt.named_matrices.items()}, sources,
+                                rank_one_a=True, lr=1e-2)
+    rng = np.random.default_rng(4242)
+    weights = {}
+    for n, p in opt.named_matrices.items():
+        with torch.no_grad():
+            p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
+        weights[n] = npy(p)
+    for step in range(3):
+        stats = synth_gpt_statistics(opt, rng, count=8 * 16384)
+        grads = {}
+        for n, p in opt.named_matrices.items():
+            grads[n] = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
+            p.grad = torch.from_numpy(grads[n]).to(DEV)
+            oracle.inject(n, **stats[n])
+        before_gpu = {n: npy(p) for n, p in opt.named_matrices.items()}
+        before_ref = dict(weights)
+        oracle.step(weights, grads)
+        opt.step()
+        worst_rel, worst_cos = 0.0, 1.0
+        for n in names:
+            d_gpu = (before_gpu[n] - npy(opt.named_matrices[n])) / 1e-2
+            d_ref = (before_ref[n] - weights[n]) / 1e-2
+            worst_rel = max(worst_rel, rel(d_gpu, d_ref))
+            worst_cos = min(worst_cos, cos(d_gpu, d_ref))
+        assert worst_rel < DIR_REL and worst_cos > DIR_COS, (step, worst_rel, worst_cos)
+    for n in names:
+        st = opt.state[opt.named_matrices[n]]
+        assert rel(npy(st["momentum_buffer"]), oracle.state[n]["momentum_buffer"]) < STAT_REL, n
+        assert rel(npy(st["b_ema"]), oracle.state[n]["b_ema"]) < STAT_REL, n
+        if sources[n] == n:
+            for key in ("a_ema", "a_mean_ema"):
+                assert rel(npy(st[key]), oracle.state[n][key]) < STAT_REL, (n, key)
+    assert _lib.device_status(DEV) == 0
+    opt.close()
+
+
+# --------------------------------------------------------------- config 4
+
+@pytest.mark.parametrize("variant", ["rank1", "diag"])
+def test_config4_layer_shapes_match_oracle(variant):
+    """One layer of the config-4 matrix set (q/k/v/o 2048^2, mlp.c_fc 8192 x
+    2048, mlp.c_proj 2048 x 8192): the tile shapes, schedules and workspace
+    sizes of config 4 on one GPU, statistics of 8 x (8 x 2048) rows injected,
+    every direction against the oracle."""
+    from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
+    torch.manual_seed(24)
+    model = gpt_matrix_model(1, 2048, 8192).to(DEV)
+    rank1 = variant == "rank1"
+    opt = (RankOneAWeightedPE if rank1 else DiagonalWeightedPE)(model, lr=1e-2)
+    names = list(opt.named_matrices)
+    sources = {n: opt.parameter_names[id(opt.a_sources[id(p)])] for n, p in opt.named_matrices.items()}
+    oracle = orc.OracleSandMuon({n: tuple(p.shape) for n, p in opt.named_matrices.items()}, sources,
+                                rank_one_a=rank1, lr=1e-2)
+    rng = np.random.default_rng(24)
+    stats = synth_gpt_statistics(opt, rng, count=8 * 8 * 2048)
+    weights, grads = {}, {}
+    for n, p in opt.named_matrices.items():
+        with torch.no_grad():
+            p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
+        grads[n] = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
+        p.grad = torch.from_numpy(grads[n]).to(DEV)
+        weights[n] = npy(p)
+        oracle.inject(n, **stats[n])
+    before = dict(weights)
+    oracle.step(weights, grads)
+    opt.step()
+    for n in names:
+        d_gpu = (before[n] - npy(opt.named_matrices[n])) / 1e-2
+        d_ref = (before[n] - weights[n]) / 1e-2
+        assert rel(d_gpu, d_ref) < DIR_REL and cos(d_gpu, d_ref) > DIR_COS, (n, rel(d_gpu, d_ref))
+        assert abs(np.linalg.norm(d_gpu) - np.sqrt(opt.named_matrices[n].shape[0])) < 1e-3 * np.sqrt(
+            opt.named_matrices[n].shape[0])
+    assert _lib.device_status(DEV) == 0
+    opt.close()
