@@ -264,8 +264,9 @@ def time_steps(opt, refill, steps, device, host=None):
 
 
 def e2e_serial(opt, params, host_g, refill, steps, device):
-    """Per step on one stream: pinned-host gradients and statistic sums in,
-    opt.step(), updated weights out to pinned host memory."""
+    """Per step on one stream: pinned-host gradients (of `params`, the
+    matrices this rank steps) and statistic sums in, opt.step(), updated
+    weights of `params` out to pinned host memory."""
     host_w = [torch.empty(tuple(p.shape), dtype=torch.float32).pin_memory() for p in params]
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -351,41 +352,128 @@ def e2e_pipelined(opt, params, host_g, refill, steps, device):
     return start.elapsed_time(end) / steps
 
 
-def cpu_baseline_sample(seconds=10.0, workload="cfg1"):
-    """The numpy oracle on one layer of the matrix set (6 matrices), repeated
-    for ~`seconds`; the median is scaled by the layer count to a full step."""
-    from oracle import sandmuon_oracle as orc
-    layers, width, hidden, rows = SETS[workload]
-    rng = np.random.default_rng(SEED)
-    shapes = {f"transformer.h.0.attn.{p}.weight": (width, width) for p in ("q_proj", "k_proj", "v_proj", "o_proj")}
-    shapes["transformer.h.0.mlp.c_fc.weight"] = (hidden, width)
-    shapes["transformer.h.0.mlp.c_proj.weight"] = (width, hidden)
-    source = {n: n.replace("k_proj", "q_proj").replace("v_proj", "q_proj") for n in shapes}
-    weights = {n: (rng.standard_normal(s) * 0.02).astype(np.float32) for n, s in shapes.items()}
-    grads = {n: (rng.standard_normal(s) * 1e-4).astype(np.float32) for n, s in shapes.items()}
-    stats = {}
-    for n, (d_out, d_in) in shapes.items():
-        e = {"b_sum": (rows * (1e-3 * np.exp(rng.normal(0, .5, d_out))) ** 2).astype(np.float32), "b_count": rows}
-        if source[n] == n:
-            mean, std = rng.normal(.1, .05, d_in), np.exp(rng.normal(0, .5, d_in))
-            e.update(a_sum=(rows * (mean ** 2 + std ** 2)).astype(np.float32),
-                     a_first_sum=(rows * mean).astype(np.float32), a_count=rows)
-        stats[n] = e
-    opt = orc.OracleSandMuon(shapes, source, rank_one_a=True, lr=LR)
-    times = []
-    t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end or len(times) < 2:
-        for n, e in stats.items():
-            opt.inject(n, **e)
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def load_reference_package():
+    """The unmodified reference package (pxike/SandMuon's `sandmuon`, pip-installed
+    into baseline/_ref), imported as `sandmuon_ref`; None when absent."""
+    init = REF_DIR / "sandmuon" / "__init__.py"
+    if not init.exists():
+        return None
+    import importlib.util
+    if "sandmuon_ref" in sys.modules:
+        return sys.modules["sandmuon_ref"]
+    spec = importlib.util.spec_from_file_location("sandmuon_ref", init,
+                                                  submodule_search_locations=[str(init.parent)])
+    module = importlib.util.module_from_spec(spec)
+    sys.modules["sandmuon_ref"] = module
+    spec.loader.exec_module(module)
+    return module
+
+
+class CpuStep:
+    """The reference's CPU step on the whole matrix set of a workload (all
+    layers x 6 matrices), with the accumulated statistics injected before
+    every step as the hooks would leave them.
+
+    kind "reference": the reference's own RankOneAWeightedPE.step() (its eager
+    FP32 torch path, sandmuon/optimizer.py:224-316) from baseline/_ref, torch
+    intra-op threads on every host core.  kind "port" (when the reference is
+    not installed): the numpy restatement of that step
+    (oracle/sandmuon_oracle.py, pinned to the reference's outputs by the
+    golden tests), BLAS on every host core."""
+
+    def __init__(self, workload="cfg1", prefer_reference=True):
+        layers, width, hidden, rows = SETS[workload]
+        self.layers = layers
+        rng = np.random.default_rng(SEED)
+        shapes, source = {}, {}
+        for layer in range(layers):
+            pre = f"transformer.h.{layer}."
+            for p in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                shapes[f"{pre}attn.{p}.weight"] = (width, width)
+                source[f"{pre}attn.{p}.weight"] = f"{pre}attn.{'q_proj' if p in ('k_proj', 'v_proj') else p}.weight"
+            shapes[f"{pre}mlp.c_fc.weight"] = (hidden, width)
+            shapes[f"{pre}mlp.c_proj.weight"] = (width, hidden)
+            source[f"{pre}mlp.c_fc.weight"] = f"{pre}mlp.c_fc.weight"
+            source[f"{pre}mlp.c_proj.weight"] = f"{pre}mlp.c_proj.weight"
+        self.matrices = len(shapes)
+        self.weights = {n: (rng.standard_normal(s) * 0.02).astype(np.float32) for n, s in shapes.items()}
+        self.grads = {n: (rng.standard_normal(s) * 1e-4).astype(np.float32) for n, s in shapes.items()}
+        self.stats = {}
+        for n, (d_out, d_in) in shapes.items():
+            e = {"b_sum": (rows * (1e-3 * np.exp(rng.normal(0, .5, d_out))) ** 2).astype(np.float32),
+                 "b_count": rows}
+            if source[n] == n:
+                mean, std = rng.normal(.1, .05, d_in), np.exp(rng.normal(0, .5, d_in))
+                e.update(a_sum=(rows * (mean ** 2 + std ** 2)).astype(np.float32),
+                         a_first_sum=(rows * mean).astype(np.float32), a_count=rows)
+            self.stats[n] = e
+        ref = load_reference_package() if prefer_reference else None
+        if ref is not None:
+            from sandmuon_b200.workloads import gpt_matrix_model
+            torch.set_num_threads(os.cpu_count())
+            self.cores = torch.get_num_threads()
+            self.kind = "reference"
+            self.model = gpt_matrix_model(layers, width, hidden)
+            self.params = dict(self.model.named_parameters())
+            with torch.no_grad():
+                for n, p in self.params.items():
+                    p.copy_(torch.from_numpy(self.weights[n]))
+                    p.grad = torch.from_numpy(self.grads[n])
+            self.opt = ref.RankOneAWeightedPE(self.model, lr=LR)
+        else:
+            from oracle import sandmuon_oracle as orc
+            try:
+                from threadpoolctl import threadpool_info, threadpool_limits
+                # torch.distributed.run sets OMP_NUM_THREADS=1; the baseline uses every core
+                threadpool_limits(limits=os.cpu_count())
+                self.cores = max((int(i.get("num_threads", 1)) for i in threadpool_info()), default=os.cpu_count())
+            except Exception:
+                self.cores = os.cpu_count()
+            self.kind = "port"
+            self.opt = orc.OracleSandMuon(shapes, source, rank_one_a=True, lr=LR)
+
+    def describe(self):
+        if self.kind == "reference":
+            return (f"the reference's own RankOneAWeightedPE.step() (pip-installed unmodified into baseline/_ref), "
+                    f"the full {self.matrices}-matrix step, torch CPU on {self.cores} threads")
+        return (f"numpy port of the reference step (oracle/sandmuon_oracle.py), the full {self.matrices}-matrix "
+                f"step, BLAS on {self.cores} threads")
+
+    def step_ms(self):
+        """One full step (statistics finish, momentum, whitening, S8, mapback,
+        update of every matrix), wall-clock ms; the injection is not timed."""
+        if self.kind == "reference":
+            for n, p in self.params.items():
+                st, e = self.opt.state[p], self.stats[n]
+                if "a_sum" in e:
+                    st["a_sum"] = torch.from_numpy(e["a_sum"].copy())
+                    st["a_first_sum"] = torch.from_numpy(e["a_first_sum"].copy())
+                    st["a_count"] = e["a_count"]
+                st["b_sum"] = torch.from_numpy(e["b_sum"].copy())
+                st["b_count"] = e["b_count"]
+            t0 = time.perf_counter()
+            self.opt.step()
+            return (time.perf_counter() - t0) * 1e3
+        for n, e in self.stats.items():
+            self.opt.inject(n, **e)
         t0 = time.perf_counter()
-        opt.step(weights, grads)
-        times.append(time.perf_counter() - t0)
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) if threadpool_info() else os.cpu_count()
-    except Exception:
-        cores = os.cpu_count()
-    return statistics.median(times[1:] if len(times) > 2 else times) * layers * 1e3, cores, len(times)
+        self.opt.step(self.weights, self.grads)
+        return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_baseline_sample(seconds=15.0, workload="cfg1"):
+    """Full CPU steps of the workload for about `seconds` (at least two: the
+    first warms the thread pool and is dropped): (median ms per step, the
+    CpuStep, timed steps)."""
+    cpu = CpuStep(workload)
+    times = [cpu.step_ms()]
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        times.append(cpu.step_ms())
+    return statistics.median(times[1:]), cpu, len(times) - 1
 
 
 # ------------------------------------------------------- config 3: S8 sweep
@@ -646,31 +734,26 @@ def run_stats(args, device):
 # ------------------------------------------------------------------- main
 
 def run_reference(args, rank):
+    """The reference arm: the reference's CPU step on the full matrix set of
+    the workload, on every host core, rank 0 only (the other ranks exit
+    without work); each of the K timed steps (after W warm-up steps) is one
+    full step.  The reference's own step from baseline/_ref when it is
+    installed, else the numpy restatement of it (CpuStep)."""
     if rank != 0:
         return
-    # torch.distributed.run sets OMP_NUM_THREADS=1; the CPU baseline uses every core
-    try:
-        from threadpoolctl import threadpool_limits
-        threadpool_limits(limits=os.cpu_count())
-    except Exception:
-        pass
-    value, cores, reps = None, None, 0
-    samples = []
     workload = args.workload if args.workload in SETS else "cfg1"
-    layers = SETS[workload][0]
+    cpu = CpuStep(workload)
     for _ in range(args.warmup):
-        cpu_baseline_sample(seconds=0.0, workload=workload)
-    for _ in range(args.steps):
-        v, cores, _ = cpu_baseline_sample(seconds=0.0, workload=workload)
-        samples.append(v)
+        cpu.step_ms()
+    samples = [cpu.step_ms() for _ in range(args.steps)]
     value = statistics.median(samples)
-    sample = (f"numpy port of the reference's eager FP32 step (oracle/sandmuon_oracle.py) on 1 of the {layers} "
-              f"layers (6 of {6 * layers} matrices) per step, scaled x{layers}")
+    sample = (f"{cpu.describe()} of {workload}: every step is a full step (no scaling), median of {args.steps} "
+              f"steps after {args.warmup} warm-up steps")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": workload_config(args.gpus, args.partition, workload),
-            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cpu.cores, "kind": cpu.kind,
                              "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -733,9 +816,15 @@ def main():
     timing = plan.read_timing()
     plan.set_timing(False)
 
-    # end to end through the public API with host buffers
-    params = list(opt.named_matrices.values())
-    host_g = [grads_host[n] for n in opt.named_matrices]
+    # End to end through the public API with host buffers.  A sharded rank
+    # steps only the matrices it owns, so it copies in only their gradients
+    # and, after the exchange, copies out only their updated weights: over the
+    # job every gradient and weight crosses a host link once, spread over the
+    # N ranks' links.  (Every rank copies in its own statistic sums.)
+    sharding = opt.sharding
+    owned = [n for n, p in opt.named_matrices.items() if sharding is None or sharding.owns(p)]
+    params = [opt.named_matrices[n] for n in owned]
+    host_g = [grads_host[n] for n in owned]
     if world > 1:
         dist.barrier()
     t0 = time.monotonic()
@@ -775,13 +864,16 @@ def main():
     gemm_ms_sum /= args.steps
     peak, peak_sustained, hbm, peak_kind = peaks()
     achieved = gemm_flops / (gemm_ms_sum * 1e-3) / 1e12 if gemm_ms_sum > 0 else 0.0
-    h2d = sum(g.numel() * 4 for g in host_g) + stat_bytes
-    d2h = sum(p.numel() * 4 for p in params)
+    # whole-job bytes per step (every rank's copies)
+    copied = torch.tensor([sum(g.numel() * 4 for g in host_g) + stat_bytes, sum(p.numel() * 4 for p in params)],
+                          dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(copied, op=dist.ReduceOp.SUM)
+    h2d, d2h = (int(v) for v in copied.tolist())
 
     if rank == 0:
-        cpu_ms, cores, reps = (cpu_baseline_sample(10.0, args.workload) if world == 1 and not args.no_cpu_baseline
-                               else (None, None, 0))
-        layers = SETS[args.workload][0]
+        cpu_ms, cpu, reps = (cpu_baseline_sample(15.0, args.workload)
+                             if world == 1 and not args.no_cpu_baseline else (None, None, 0))
         line = {
             "metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
@@ -802,7 +894,9 @@ def main():
                                    + (", per GPU: sum of rank FLOPs / sum of rank GEMM time" if world > 1 else "")},
             "e2e": {"value": round(e2e_ms, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "mode": "pipelined: step k+1 host-to-device copy and step k-1 device-to-host copy overlap "
-                            "step k (copy-in / compute / copy-out streams)",
+                            "step k (copy-in / compute / copy-out streams)"
+                            + ("; each rank copies the gradients in and the updated weights out of the matrices it "
+                               "owns, bytes are whole-job totals" if world > 1 else ""),
                     "serial_value": round(e2e_serial_ms, 4)},
             "host_issue_ms_per_step": round(host_ms[0], 4),
             "gpu_launches": int(launches * args.steps),
@@ -810,9 +904,9 @@ def main():
             "clocks": clocks,
         }
         if cpu_ms is not None:
-            line["cpu_baseline"] = {"value": round(cpu_ms, 2), "unit": UNIT, "cores": cores, "kind": "port",
-                                    "sample": f"numpy oracle, 1 of {layers} layers (6 of {6 * layers} matrices), "
-                                              f"median of {reps} runs over ~10 s, scaled x{layers}"}
+            line["cpu_baseline"] = {"value": round(cpu_ms, 2), "unit": UNIT, "cores": cpu.cores, "kind": cpu.kind,
+                                    "sample": f"{cpu.describe()} (no scaling), median of {reps} steps over ~15 s "
+                                              f"after one warm-up step"}
         print(json.dumps(line), flush=True)
     opt.close()
     if world > 1:

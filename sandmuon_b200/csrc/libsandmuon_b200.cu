@@ -25,6 +25,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <queue>
 #include <string>
 #include <vector>
 
@@ -499,8 +500,9 @@ struct Timer {
 struct Group {
   int r = 0, c = 0;      // oriented shape, r <= c
   int rp = 0, cp = 0;    // padded to multiples of 128
-  int cg = 1;            // 2: X X^T and P X run on CTA pairs (256-row tiles)
-  int bn_c = 0;          // N tile of P X
+  bool pair_ok = false;  // rp % 256 == 0 and CTA pairs fit: 256-row pair tiles possible
+  int tile_cg[3] = {1, 1, 1};        // per GEMM kind: 1 = one CTA, 128-row tiles; 2 = CTA pair, 256-row
+  int tile_bn[3] = {128, 128, 128};  // per GEMM kind: N extent of a tile
   int batch = 0;
   int mat_off = 0;       // first descriptor of this group in the MatDev table
   bool rank1 = false;
@@ -541,41 +543,26 @@ struct Carver {
 
 enum GemmKind : int { kGram = 0, kGramSq = 1, kPX = 2 };
 
-// Tilings of the symmetric products X X^T and G G: 0 = one CTA, 128 x 128
-// tiles; 1 = CTA pair, 256 x 256; 2 = CTA pair, 256 x 128 block rows (each
-// CTA stages 64 B rows: the *_K64 tensor maps); -1 = by size (pairs from 1024
-// rows, one CTA below).  Measured on B200 (config-1 768-row groups, ncu launch
-// lists): X X^T is fastest on 256 x 256 pair tiles; so is G G now that its
-// epilogue only scales and shifts the diagonal (compensated 79 vs 89 us per
-// launch on single-CTA tiles, plain 43 vs 48 us); with the old polynomial
-// epilogue, which re-read the gram, single-CTA tiles had been faster.
-#ifndef SMB_GRAM_TILE
-#define SMB_GRAM_TILE 1
-#endif
-#ifndef SMB_GG_TILE
-#define SMB_GG_TILE 1
-#endif
-static_assert(SMB_GRAM_TILE >= -1 && SMB_GRAM_TILE <= 2 && SMB_GG_TILE >= -1 && SMB_GG_TILE <= 2,
-              "plan tilings: -1 (by size), 0, 1 or 2");
-static int kind_tiling(const Group& g, int kind) {
-  const int t = kind == kGram ? SMB_GRAM_TILE : SMB_GG_TILE;
-  if (t >= 0) return t;
-  return g.rp >= 1024 ? 1 : 0;
-}
-static int kind_cg(const Group& g, int kind) {
-  if (g.cg == 1) return 1;
-  return (kind == kPX || kind_tiling(g, kind) != 0) ? 2 : 1;
-}
-static int kind_bn(const Group& g, int kind) {
-  if (kind == kPX) return g.bn_c;
-  return (kind_cg(g, kind) == 2 && kind_tiling(g, kind) == 1) ? 2 * kGemmBM : kGemmBM;
-}
+// Tile shapes of the three GEMM kinds, chosen per plan (choose_tilings):
+//   X X^T, G G (symmetric, upper block triangle): one CTA with 128 x 128
+//     tiles; a CTA pair with 256 x 256 tiles; or a CTA pair with 256 x 128
+//     block-row tiles (each CTA stages 64 B rows: the *_K64 tensor maps);
+//   P X: one CTA or a CTA pair (128 / 256 rows) with BN = 128 or 256.
+static int kind_cg(const Group& g, int kind) { return g.tile_cg[kind]; }
+static int kind_bn(const Group& g, int kind) { return g.tile_bn[kind]; }
 
 // F32Norm partial sums of one matrix's G*G (its tiles_m x tiles_n grid).
 static int norm_slots_per_matrix(const Group& g) {
   const int tm = g.rp / (kGemmBM * kind_cg(g, kGramSq));
   const int tn = g.rp / kind_bn(g, kGramSq);
   return tm * tn * kNormSlots;
+}
+
+// Room for the partials of the finest tiling (128 x 128 tiles), so a plan's
+// layout does not depend on the tiling it picks.
+static int norm_slots_capacity(const Group& g) {
+  const int t = g.rp / kGemmBM;
+  return t * t * kNormSlots;
 }
 
 static void carve_group(Carver& cv, Group& g) {
@@ -591,7 +578,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.g2 = cv.take<float>(gs);
   g.ph = reinterpret_cast<__nv_bfloat16*>(g.g2);  // P hi | P lo in the g2 bytes
   g.pl = g.ph ? g.ph + gs : nullptr;
-  g.partials = cv.take<float>(static_cast<size_t>(g.batch) * norm_slots_per_matrix(g));
+  g.partials = cv.take<float>(static_cast<size_t>(g.batch) * norm_slots_capacity(g));
   g.inv_norm = cv.take<float>(g.batch);
   g.s = cv.take<float>(g.batch);
   g.s_inv = cv.take<float>(g.batch);
@@ -625,13 +612,21 @@ static int encode_group_maps(Group& g) {
   return SM_OK;
 }
 
+// Shape fields and the default tiling (pair tiles where possible: 256 x 256
+// for the symmetric products, BN = 256 for P X when the columns allow it);
+// choose_tilings may replace the tiling for a plan's batch sizes.
 static void init_group_shape(Group& g, int r, int c, int batch, bool pair_ok) {
   g.r = r;
   g.c = c;
   g.rp = static_cast<int>(round_up(r, 128));
   g.cp = static_cast<int>(round_up(c, 128));
-  g.cg = (SMB_PAIR && g.rp % 256 == 0 && pair_ok) ? 2 : 1;
-  g.bn_c = pick_bn(g.cp);
+  g.pair_ok = SMB_PAIR && g.rp % 256 == 0 && pair_ok;
+  for (int kind = 0; kind < 2; ++kind) {
+    g.tile_cg[kind] = g.pair_ok ? 2 : 1;
+    g.tile_bn[kind] = g.pair_ok ? 2 * kGemmBM : kGemmBM;
+  }
+  g.tile_cg[2] = g.pair_ok ? 2 : 1;
+  g.tile_bn[2] = pick_bn(g.cp);
   g.batch = batch;
   g.dmax = c;
 }
@@ -666,6 +661,116 @@ static double s8_shift(int stage) { return kS8Coeff[stage][1] / (2.0 * kS8Coeff[
 
 static int kind_k(const Group& g, int kind) { return kind == kGram ? g.cp : g.rp; }
 static int kind_n(const Group& g, int kind) { return kind == kPX ? g.cp : g.rp; }
+
+// ------------------------------------------------- tiling by cost model
+// A plan's GEMM launches are persistent: each worker (a CTA, or a CTA pair)
+// takes its share of the launch's tiles from an LPT schedule, so a launch
+// lasts as long as its most loaded worker.  Pair tiles are the most
+// efficient per SM, but with few matrices per launch (a rank's share of a
+// sharded step) a handful of long tiles leaves most workers idle.  Per GEMM
+// kind, choose_tilings estimates that makespan for every tiling the plan's
+// groups support and keeps the shortest.
+//
+// Relative cost of one 64-deep k-block of one tile, in units of a CTA-pair
+// 256 x 256 tile's k-block: tile area / (per-SM efficiency x SMs).  The
+// per-SM efficiencies relative to the 256 x 256 pair tile come from
+// config-1 ncu launch lists on B200 (compensated G G: 79 us per launch on
+// pair tiles, 89 us on single-CTA 128 x 128 tiles at 4.4 and 7.7 tile waves,
+// i.e. 0.71); the 256 x 128 and 128 x 256 figures are interpolated.
+static double kblock_cost(int cg, int bn) {
+  const double area = static_cast<double>(kGemmBM * cg) * bn / (256.0 * 256.0);
+  double eff;
+  if (cg == 2) eff = bn == 256 ? 1.0 : 0.80;
+  else eff = bn == 256 ? 0.85 : 0.71;
+  return area / (eff * cg / 2.0);
+}
+
+// LPT makespan of `costs` over `workers` (the schedule lpt_schedule builds).
+static double lpt_makespan(std::vector<double> costs, int workers) {
+  if (costs.empty() || workers <= 0) return 0.0;
+  std::sort(costs.begin(), costs.end(), [](double a, double b) { return a > b; });
+  std::priority_queue<double, std::vector<double>, std::greater<double>> load;
+  for (int w = 0; w < workers; ++w) load.push(0.0);
+  double worst = 0.0;
+  for (double c : costs) {
+    double l = load.top() + c;
+    load.pop();
+    load.push(l);
+    worst = std::max(worst, l);
+  }
+  return worst;
+}
+
+// Estimated duration of one stage's launches of `kind` with the groups'
+// current tile choices: groups sharing a (cg, bn) share a launch (as in
+// build_s8_launches); launches run one after another, each paying a fixed
+// ramp of about two k-blocks.
+static double kind_cost(const std::vector<Group>& groups, int kind, int sms, int pairs) {
+  std::vector<std::pair<int, int>> keys;
+  for (const Group& g : groups) {
+    const std::pair<int, int> key{kind_cg(g, kind), kind_bn(g, kind)};
+    if (std::find(keys.begin(), keys.end(), key) == keys.end()) keys.push_back(key);
+  }
+  double total = 0.0;
+  for (const auto& key : keys) {
+    std::vector<double> costs;
+    const double unit = kblock_cost(key.first, key.second);
+    for (const Group& g : groups) {
+      if (kind_cg(g, kind) != key.first || kind_bn(g, kind) != key.second) continue;
+      const int64_t tm = g.rp / (kGemmBM * key.first);
+      const int64_t tn = kind_n(g, kind) / key.second;
+      const int64_t tiles = (kind == kPX ? tm * tn : sym_tiles(tm, tn)) * g.batch;
+      const double c = unit * (kind_k(g, kind) / kBkK);
+      for (int64_t t = 0; t < tiles; ++t) costs.push_back(c);
+    }
+    total += lpt_makespan(costs, key.first == 2 ? pairs : sms) + 2.0;
+  }
+  return total;
+}
+
+// Picks, per GEMM kind, the tiling with the shortest estimated launches for
+// these groups (the same candidate for every group that supports it; the
+// others keep one-CTA tiles).  The default (first candidate: pair tiles)
+// stays unless another is estimated at least 10% faster, since the
+// efficiencies above are estimates.  SMB_TILE_MODEL=0 keeps the defaults
+// (for measuring the model against them).
+#ifndef SMB_TILE_MODEL
+#define SMB_TILE_MODEL 1
+#endif
+static void choose_tilings(std::vector<Group>& groups, int sms, int pairs) {
+  if (!SMB_TILE_MODEL) return;
+  for (int kind = 0; kind < 3; ++kind) {
+    const std::pair<int, int> sym_options[] = {{2, 256}, {2, 128}, {1, 128}};
+    const std::pair<int, int> px_options[] = {{2, 256}, {2, 128}, {1, 256}, {1, 128}};
+    const std::pair<int, int>* options = kind == kPX ? px_options : sym_options;
+    const int n_options = kind == kPX ? 4 : 3;
+    double best = -1.0;
+    std::vector<std::pair<int, int>> best_pick;
+    for (int o = 0; o < n_options; ++o) {
+      std::vector<std::pair<int, int>> pick;
+      for (Group& g : groups) {
+        int cg = options[o].first, bn = options[o].second;
+        const bool ok = (cg == 1 || (g.pair_ok && pairs > 0)) && kind_n(g, kind) % bn == 0;
+        if (!ok) {
+          cg = 1;
+          bn = kind == kPX ? pick_bn(g.cp) : kGemmBM;
+        }
+        g.tile_cg[kind] = cg;
+        g.tile_bn[kind] = bn;
+        pick.push_back({cg, bn});
+      }
+      const double cost = kind_cost(groups, kind, sms, pairs) * (o == 0 ? 0.9 : 1.0);
+      if (best < 0.0 || cost < best) {
+        best = cost;
+        best_pick = pick;
+      }
+    }
+    for (size_t i = 0; i < groups.size(); ++i) {
+      groups[i].tile_cg[kind] = best_pick[i].first;
+      groups[i].tile_bn[kind] = best_pick[i].second;
+    }
+  }
+}
 
 // Builds the launch sets of every GEMM kind.  With `cv` the tile schedules
 // are carved from the workspace (measured when cv.base is null).  `pairs` is
@@ -1003,6 +1108,7 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     if (any_r1 && any_diag) return fail(SM_ERR_ARG, "a shape group mixes rank-one and diagonal A statistics");
     groups[g].rank1 = any_r1;
   }
+  choose_tilings(groups, di->sms, pairs);
   MatDev* d_mats = cv.take<MatDev>(nm);
   StatDev* d_stats = cv.take<StatDev>(ns);
   std::vector<float*> s_inv(ns), s_z(ns), s_zeta(ns), s_scal(ns);
@@ -1744,6 +1850,11 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   s8_layout(batch, rows, cols, pairs > 0, nullptr, &g, &d_mats, &ones, &need);
   if (workspace_bytes < need) return fail(SM_ERR_WORKSPACE, "S8 workspace too small");
   s8_layout(batch, rows, cols, pairs > 0, workspace, &g, &d_mats, &ones, &need);
+  {
+    std::vector<Group> one(1, g);
+    choose_tilings(one, di->sms, pairs);
+    g = one[0];
+  }
   SM_TRY(encode_group_maps(g));
   SM_CUDA(cudaMemsetAsync(workspace, 0, need, st));
   const int64_t nmax = std::max(rows, cols);
@@ -1798,8 +1909,10 @@ int sm_s8_executed_flops(int32_t batch, int32_t rows, int32_t cols, double* flop
   SM_TRY(current_device_info(&di));
   int pairs = 0;
   SM_TRY(pair_workers(di, &pairs));
-  Group g;
-  init_group_shape(g, std::min(rows, cols), std::max(rows, cols), batch, pairs > 0);
+  std::vector<Group> one(1);
+  init_group_shape(one[0], std::min(rows, cols), std::max(rows, cols), batch, pairs > 0);
+  choose_tilings(one, di->sms, pairs);
+  const Group& g = one[0];
   double total = 0.0;
   for (int stage = 0; stage < 5; ++stage) {
     for (int kind = 0; kind < 3; ++kind) {

@@ -24,11 +24,16 @@ _QKV_SHARING = re.compile(r"^(transformer\.h\.\d+\.attn\.)[kv]_proj\.weight$")
 
 
 class DiagonalWeightedPE(Optimizer):
-    """S8 directions weighted by activation and output-cotangent diagonals.
+    """SandMuon with diagonal whitening on both sides of each weight matrix.
 
-    Statistics are accumulated from every forward/backward microbatch between
-    optimizer steps. Defaults match the 103M run: beta=.97, Muon momentum=.8,
-    S8 margin=1.35, auxiliary AdamW LR ratio=.1 and decay=.01.
+    Each selected Linear weight is updated along the Schatten-8 polar
+    direction of its Nesterov momentum, whitened on the input side by the
+    running second moment of the layer's activations and on the output side
+    by that of its output cotangents.  Those moments are summed by forward
+    and cotangent hooks over all microbatches of a step, then folded into
+    exponential averages (factor 0.97) at step().  Other trainable parameters
+    take AdamW at a tenth of the learning rate with weight decay 0.01;
+    momentum is 0.8.
 
     Extra keywords: `process_group` (torch.distributed group or None) shards
     the S8 work over the group's ranks, `partition` ("lpt" or "layer") picks
@@ -84,6 +89,7 @@ class DiagonalWeightedPE(Optimizer):
 
         self._plans: dict[tuple, engine.StepPlan] = {}
         self._stat_flat: dict = {}
+        self._work: dict[int, tuple] = {}
         self._sharding = None
         if reduce_gradients and process_group is None:
             raise ValueError("reduce_gradients=True needs a process_group")
@@ -204,11 +210,50 @@ class DiagonalWeightedPE(Optimizer):
                     auxiliary_items.append((parameter, group))
         return matrix_items, auxiliary_items
 
+    # ------------------------------------------- parameter dtypes / layouts
+    # The kernels read and write contiguous FP32.  Like the reference, which
+    # steps in FP32 on `gradient.float()` and adds `direction.to(param.dtype)`
+    # (sandmuon/optimizer.py:245-248, 281, 315), other dtypes and strided
+    # tensors are accepted: a gradient is converted to a contiguous FP32 copy
+    # for the step, and a parameter is stepped through a persistent FP32 work
+    # copy whose update is then added to it in its own dtype.
+
     @staticmethod
-    def _require(t: torch.Tensor, what: str):
-        if t.dtype != torch.float32 or not t.is_contiguous():
-            raise TypeError(f"sandmuon_b200 needs contiguous float32 {what}; got {t.dtype} "
-                            f"{'contiguous' if t.is_contiguous() else 'strided'}")
+    def _native(t: torch.Tensor) -> bool:
+        return t.dtype == torch.float32 and t.is_contiguous()
+
+    @staticmethod
+    def _fp32_grad(g: torch.Tensor) -> torch.Tensor:
+        return g if DiagonalWeightedPE._native(g) else g.detach().float().contiguous()
+
+    def _work_copy(self, parameter) -> torch.Tensor:
+        """The FP32 tensor the kernels update in place of `parameter`: the
+        parameter itself when it is contiguous FP32, else a persistent work
+        copy refreshed from it (apply with _apply_work_copy after the step)."""
+        if self._native(parameter):
+            return parameter
+        if self._sharding is not None:
+            raise TypeError("a sharded sandmuon_b200 optimizer needs contiguous float32 parameters; got "
+                            f"{parameter.dtype} {'contiguous' if parameter.is_contiguous() else 'strided'}")
+        pair = self._work.get(id(parameter))
+        if pair is None or pair[0].shape != parameter.shape or pair[0].device != parameter.device:
+            pair = (torch.empty(parameter.shape, dtype=torch.float32, device=parameter.device),
+                    torch.empty(parameter.shape, dtype=torch.float32, device=parameter.device))
+            self._work[id(parameter)] = pair
+        work, before = pair
+        work.copy_(parameter.detach())
+        if parameter.dtype != torch.float32:
+            before.copy_(work)
+        return work
+
+    def _apply_work_copy(self, parameter) -> None:
+        if self._native(parameter):
+            return
+        work, before = self._work[id(parameter)]
+        if parameter.dtype == torch.float32:
+            parameter.detach().copy_(work)
+        else:
+            parameter.detach().add_((work - before).to(parameter.dtype))
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -230,23 +275,30 @@ class DiagonalWeightedPE(Optimizer):
 
     def _step_auxiliary(self, auxiliary_items):
         by_hyper: dict[tuple, list] = {}
+        converted = []
         for parameter, group in auxiliary_items:
             _lib.ensure_device(parameter.device)
-            self._require(parameter, "auxiliary parameters")
-            self._require(parameter.grad, "auxiliary gradients")
             state = self.state[parameter]
             if "exp_avg" not in state:
-                state["exp_avg"] = torch.zeros_like(parameter, dtype=torch.float32)
-                state["exp_avg_sq"] = torch.zeros_like(parameter, dtype=torch.float32)
+                state["exp_avg"] = torch.zeros(parameter.shape, dtype=torch.float32, device=parameter.device)
+                state["exp_avg_sq"] = torch.zeros(parameter.shape, dtype=torch.float32, device=parameter.device)
                 state["step"] = 0
+            for key in ("exp_avg", "exp_avg_sq"):
+                if not self._native(state[key]):
+                    state[key] = state[key].float().contiguous()
             state["step"] += 1
             b1, b2 = group["adamw_betas"]
             key = (group["lr"] * group["adamw_lr_ratio"], float(b1), float(b2), group["adamw_eps"],
                    group["weight_decay"], parameter.device)
-            by_hyper.setdefault(key, []).append(engine.AdamItem(parameter, parameter.grad, state["exp_avg"],
-                                                                state["exp_avg_sq"], state["step"]))
+            work = self._work_copy(parameter)
+            if work is not parameter:
+                converted.append(parameter)
+            by_hyper.setdefault(key, []).append(engine.AdamItem(work, self._fp32_grad(parameter.grad),
+                                                                state["exp_avg"], state["exp_avg_sq"], state["step"]))
         for (lr, b1, b2, eps, wd, _device), items in by_hyper.items():
             engine.adamw_multi(items, lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd)
+        for parameter in converted:
+            self._apply_work_copy(parameter)
 
     @property
     def sharding(self):
@@ -293,18 +345,21 @@ class DiagonalWeightedPE(Optimizer):
             stat_specs.append((_lib.SM_STAT_B, st["b_sum"], None, st["b_ema"], None))
             counts.append(self.state[source]["a_count"])
             ema_init.append(init)
-        mats, grads, lrs = [], [], []
+        mats, grads, lrs, converted = [], [], [], []
         for parameter, source, group in owned:
             if parameter.device != device:
                 raise RuntimeError("sandmuon_b200 expects every selected matrix on one CUDA device")
-            grad = averaged.get(id(parameter), parameter.grad)
-            self._require(parameter, "matrix parameters")
-            self._require(grad, "matrix gradients")
+            grad = self._fp32_grad(averaged.get(id(parameter), parameter.grad))
             st = self.state[parameter]
             if "momentum_buffer" not in st:
-                st["momentum_buffer"] = torch.zeros_like(parameter, dtype=torch.float32)
+                st["momentum_buffer"] = torch.zeros(parameter.shape, dtype=torch.float32, device=parameter.device)
+            elif not self._native(st["momentum_buffer"]):
+                st["momentum_buffer"] = st["momentum_buffer"].float().contiguous()
+            work = self._work_copy(parameter)
+            if work is not parameter:
+                converted.append(parameter)
             export = self._sharding.send_slot(parameter) if self._sharding is not None else None
-            mats.append((parameter, st["momentum_buffer"], stat_index[("a", id(source))],
+            mats.append((work, st["momentum_buffer"], stat_index[("a", id(source))],
                          stat_index[("b", id(parameter))], export))
             grads.append(grad)
             lrs.append(group["lr"])
@@ -336,6 +391,8 @@ class DiagonalWeightedPE(Optimizer):
                         sums.append(fs)
             device_counts = self._sharding.reduce_statistics(sums, counts)
         plan.step(grads, lrs, counts, ema_init, device_counts=device_counts)
+        for parameter in converted:
+            self._apply_work_copy(parameter)
         # host-side counters follow the reference (sums are zeroed on the device)
         for source in sources.values():
             self.state[source]["a_count"] = 0
@@ -378,7 +435,10 @@ class DiagonalWeightedPE(Optimizer):
 
 
 class RankOneAWeightedPE(DiagonalWeightedPE):
-    """Production SAND variant with exact rank-one activation mean correction."""
+    """SandMuon whose activation-side whitener also removes the activation
+    mean: the input covariance is modelled as diagonal plus the rank-one
+    outer product of the mean, inverted exactly (DiagonalWeightedPE with
+    rank_one_a=True)."""
 
     def __init__(self, model: nn.Module, lr: float, *,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,

@@ -323,3 +323,23 @@ def test_pair_rejects_unaligned_rows():
     a = torch.zeros(1, 384, 64, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="M%256"):
         engine.gemm_bf16(a, a, pair=True, out0=torch.empty(1, 384, 384, device=DEV))
+
+
+@pytest.mark.parametrize("comp", [False, True])
+def test_pair_narrow_mn_major_b(comp):
+    """P X on 256 x 128 pair tiles (each CTA stages one 64-column chunk of an
+    MN-major B), the tiling a plan may pick for P X at small batches."""
+    p = rnd(3, 512, 384, seed=31)
+    x = rnd(3, 384, 640, seed=32)
+    ph, pl = split(p)
+    xh, xl = split(x)
+    out = torch.full((3, 512, 640), float("nan"), device=DEV)
+    kw = dict(a_lo=pl, b_lo=xl) if comp else {}
+    engine.gemm_bf16(ph, xh, b_kmajor=False, pair=True, bn128=True, epilogue=_lib.SM_EPI_F32, out0=out, **kw)
+    if comp:
+        want = torch.bmm(p.double(), x.double())
+        assert rel(out, want) < 2e-5
+    else:
+        want = torch.bmm(ph.float(), xh.float())
+        assert rel(out, want) < 1e-5
+    assert _lib.device_status(DEV) == 0
