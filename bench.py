@@ -72,20 +72,14 @@ def parse_args():
     return ap.parse_args()
 
 
-def gemm_traffic_per_launch():
-    """DRAM bytes (read + write) per S8 GEMM launch from the committed ncu
-    launch list of a config-1 step (profiles/launches_cfg1_step.md, line
-    `traffic_per_launch_bytes: N`), or None when the summary has no figure."""
-    path = ROOT / "profiles" / "launches_cfg1_step.md"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        if line.startswith("traffic_per_launch_bytes:"):
-            try:
-                return int(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per S8 GEMM
+# launch of a config-1 step, the mean over the 15 GEMM launches of one step,
+# from one ncu capture of the launch list (a stated constant: DRAM counters
+# are not readable inside a timed run).  Capture command:
+#   python bench.py --steps 2 --warmup 1 --profile && ncu --metrics
+#   gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#   --clock-control none --csv --log-file <out> python bench.py --steps 2 --warmup 1 --profile
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 331_695_849
 
 
 def peaks():
@@ -886,9 +880,10 @@ def main():
             "phase_ms_per_step": {k: round(v / args.steps, 4) for k, v in timing["ms"].items()},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4),
-                         "traffic": gemm_traffic_per_launch() if args.workload == "cfg1" else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the "
-                                           "S8 GEMM launches of a config-1 step (profiles/launches_cfg1_step.md)",
+                         "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if args.workload == "cfg1" else None,
+                         "traffic_source": "stated constant from one ncu capture: dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum, mean over the 15 S8 GEMM launches of a "
+                                           "config-1 step",
                          "peak_kind": f"{peak_kind} burst bf16 (sustained {peak_sustained})",
                          "kernel": "k_gemm_bf16 (all S8 GEMM launches of a step)"
                                    + (", per GPU: sum of rank FLOPs / sum of rank GEMM time" if world > 1 else "")},

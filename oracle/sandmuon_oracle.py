@@ -93,6 +93,38 @@ def graft_direction(value, output_rows):
     return (v * F32(math.sqrt(float(output_rows)) / norm)).astype(F32)
 
 
+# ---------------------------------------------------- one-sided (split_sides)
+# The historical optimizer's split_sides option
+# (reproduction/odl/optim/diagonal_weighted_pe.py:408-410, 500-543): only the
+# activation side carries a rank-one factor (the cotangent side's z is zero),
+# so the whitening and the finish apply the rank-one action on that side
+# alone -- the left side for a transposed matrix, else the right.
+
+def one_side_whiten(sources, left_inverse, right_inverse, z, coefficient, rank_one_left):
+    """reproduction/odl/optim/diagonal_weighted_pe.py:141-148, batched."""
+    c = np.asarray(coefficient, F32).reshape(-1, 1, 1)
+    v = (_f(sources) * _f(left_inverse)[:, :, None] * _f(right_inverse)[:, None, :]).astype(F32)
+    if rank_one_left:
+        return (v + c * _f(z)[:, :, None] * np.matmul(_f(z)[:, None, :], v)).astype(F32)
+    return (v + c * np.matmul(v, _f(z)[:, :, None]) * _f(z)[:, None, :]).astype(F32)
+
+
+def one_side_finish(q, left_inverse, right_inverse, z, coefficient, rank_one_left, q_scale, graft_rows):
+    """reproduction/odl/optim/diagonal_weighted_pe.py:152-164, batched: the
+    one-sided mapback, then the graft to norm sqrt(rows) (which cancels the
+    historical aspect factor q_scale)."""
+    c = np.asarray(coefficient, F32).reshape(-1, 1, 1)
+    v = (_f(q) * np.asarray(q_scale, F32).reshape(-1, 1, 1)).astype(F32)
+    if rank_one_left:
+        v = v + c * _f(z)[:, :, None] * np.matmul(_f(z)[:, None, :], v)
+    else:
+        v = v + c * np.matmul(v, _f(z)[:, :, None]) * _f(z)[:, None, :]
+    v = (v * _f(left_inverse)[:, :, None] * _f(right_inverse)[:, None, :]).astype(F32)
+    norms = np.sqrt((v.astype(np.float64) ** 2).sum(axis=(-2, -1), keepdims=True)).astype(F32)
+    rows = np.sqrt(np.asarray(graft_rows, F32)).reshape(-1, 1, 1)
+    return (v * (rows / np.maximum(norms, TINY))).astype(F32)
+
+
 # ------------------------------------------------------------------------ S8
 
 def s8_fp32(x):
@@ -159,7 +191,8 @@ class OracleSandMuon:
     (q/k/v sharing already resolved); auxiliaries: ordered {name: shape}.
     Statistics are injected with add_a / add_b (the hook reductions)."""
 
-    def __init__(self, matrices, a_source, auxiliaries=(), *, rank_one_a, lr):
+    def __init__(self, matrices, a_source, auxiliaries=(), *, rank_one_a, lr, split_sides=False):
+        self.split_sides = bool(split_sides) and bool(rank_one_a)
         self.matrices = dict(matrices)
         self.a_source = dict(a_source)
         self.auxiliaries = list(auxiliaries)
@@ -272,6 +305,10 @@ class OracleSandMuon:
         groups: dict[tuple, list] = {}
         for item in items:
             groups.setdefault(item[1].shape, []).append(item)
+        if self.split_sides:
+            for entries in groups.values():
+                self._step_one_sided(entries, weights, directions_out)
+            return
         for entries in groups.values():
             sources = np.stack([e[1] for e in entries])
             if self.rank_one_a:
@@ -296,6 +333,38 @@ class OracleSandMuon:
                 if directions_out is not None:
                     directions_out[name] = np.ascontiguousarray(direction)
                 weights[name] = (weights[name] + F32(-self.lr) * direction).astype(F32)
+
+    def _step_one_sided(self, entries, weights, directions_out):
+        """One shape group with split_sides (diagonal_weighted_pe.py:500-543):
+        transposed matrices first (rank-one action on the left), then the
+        others (on the right)."""
+        entries = sorted(entries, key=lambda e: e[4], reverse=True)
+        boundary = sum(1 for e in entries if e[4])
+        # rank-one factors: (inverse, z, coefficient) of the A side; the B side's
+        # (inverse, zero, zero) contributes its inverse only
+        li = np.stack([e[2][0] for e in entries]); ri = np.stack([e[3][0] for e in entries])
+        sources = np.stack([e[1] for e in entries])
+        rows = np.array([self.matrices[e[0]][0] for e in entries], F32)
+        cols = np.array([self.matrices[e[0]][1] for e in entries], F32)
+        q_scale = np.sqrt(np.maximum(F32(1.0), rows / cols)).astype(F32)
+        # pieces (first, end, rank-one on the left, z, coefficient); the z of the
+        # two pieces differ in length (d_in on either side)
+        pieces = []
+        for lo, hi, left in ((0, boundary, True), (boundary, len(entries), False)):
+            if hi > lo:
+                side = 2 if left else 3
+                pieces.append((lo, hi, left, np.stack([e[side][1] for e in entries[lo:hi]]),
+                               np.array([e[side][2] for e in entries[lo:hi]], F32)))
+        q = s8_fp32(np.concatenate([one_side_whiten(sources[lo:hi], li[lo:hi], ri[lo:hi], z, c, left)
+                                    for lo, hi, left, z, c in pieces]))
+        finished = [one_side_finish(q[lo:hi], li[lo:hi], ri[lo:hi], z, c, left, q_scale[lo:hi], rows[lo:hi])
+                    for lo, hi, left, z, c in pieces]
+        directions = np.concatenate(finished)
+        for index, (name, _, _, _, transposed) in enumerate(entries):
+            direction = directions[index].T if transposed else directions[index]
+            if directions_out is not None:
+                directions_out[name] = np.ascontiguousarray(direction)
+            weights[name] = (weights[name] + F32(-self.lr) * direction).astype(F32)
 
     # sandmuon/optimizer.py:268-281
     def _adamw(self, name, weights, g):

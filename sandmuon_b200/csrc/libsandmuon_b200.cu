@@ -511,7 +511,12 @@ struct Group {
   __nv_bfloat16 *ph = nullptr, *pl = nullptr;
   __nv_bfloat16* q = nullptr;  // S8 output Q, BF16 [B, rp, cp] (param layout when transposed)
   float *g2 = nullptr, *partials = nullptr;
-  float *inv_norm = nullptr, *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
+  // plane scale 2^k of the stored stage-1 input, its stage-1 alphas (rho for
+  // X = rho * planes, rho^2 for X X^T, rho / s for P X), S8 scale s, 1/s, graft
+  float *pre = nullptr, *rho = nullptr, *rho2 = nullptr, *px_alpha = nullptr;
+  float *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
+  bool fused_ok = false;  // every matrix fits k_whiten_fused (rows in shared memory)
+  int fused_blocks = 0;   // grid x of k_whiten_fused: the most row blocks of a matrix
   float2 *rs_white = nullptr, *rs_map = nullptr;
   int* tmask = nullptr;  // [B] 1 = transposed matrix: its Q is stored in param layout
   unsigned *tk_white = nullptr, *tk_map = nullptr;  // [B] last-CTA tickets (zero between launches)
@@ -579,7 +584,10 @@ static void carve_group(Carver& cv, Group& g) {
   g.ph = reinterpret_cast<__nv_bfloat16*>(g.g2);  // P hi | P lo in the g2 bytes
   g.pl = g.ph ? g.ph + gs : nullptr;
   g.partials = cv.take<float>(static_cast<size_t>(g.batch) * norm_slots_capacity(g));
-  g.inv_norm = cv.take<float>(g.batch);
+  g.pre = cv.take<float>(g.batch);
+  g.rho = cv.take<float>(g.batch);
+  g.rho2 = cv.take<float>(g.batch);
+  g.px_alpha = cv.take<float>(g.batch);
   g.s = cv.take<float>(g.batch);
   g.s_inv = cv.take<float>(g.batch);
   g.gamma = cv.take<float>(g.batch);
@@ -838,8 +846,10 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
     p.out0 = g.gh;
     p.out1 = g.gl;
     *epi = comp ? kEpiHiLo : kEpiBF16;
-    // stages 2-5 store the shifted gram H = G + beta I (see the G H product)
+    // stages 2-5 store the shifted gram H = G + beta I (see the G H product);
+    // stage 1 scales the planes' product by rho^2 (normalised input)
     if (stage > 0) p.diag = static_cast<float>(s8_shift(stage));
+    else p.alpha = g.rho2;
   } else if (kind == kGramSq) {
     // G G with G symmetric: B = G read K-major as G^T
     const CUtensorMap& bG_h = b64 ? g.gh_K64 : g.gh_K;
@@ -887,7 +897,7 @@ static GemmProblem s8_problem(const Group& g, int kind, int stage, int bn, int* 
       p.out1 = in_a ? g.xl : g.xb;
       *epi = next_comp ? kEpiHiLo : kEpiBF16;
     }
-    if (stage == 0) p.alpha = g.s_inv;  // X2 = (P X) / s
+    if (stage == 0) p.alpha = g.px_alpha;  // X2 = (P rho planes) / s
   }
   return p;
 }
@@ -937,7 +947,7 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
         const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 4, 1024), 512));
         SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
                    SM_TRY(launch_kernel(k_reduce_s8scale, dim3(g.batch), dim3(256), 0, st, g.partials, per_mat,
-                                        kS8Margin, g.s, g.s_inv));
+                                        kS8Margin, g.s, g.s_inv, g.rho, g.px_alpha));
                    SM_TRY(launch_kernel(k_poly_stage1, dim3(blocks, g.batch), dim3(256), 0, st, g.gh, g.gl, g.g2,
                                         g.s, g.rp, (float)kS8Coeff[0][0], (float)kS8Coeff[0][1],
                                         (float)kS8Coeff[0][2]));
@@ -952,17 +962,54 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
 }
 
 // Whitening / normalisation front end for one group (N3 passes 1 and 2).
-static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float mom_omb, bool vec4,
+// Raises k_whiten_fused's dynamic shared-memory limit once per device and
+// instantiation (at plan creation, outside any capture).
+static int prepare_front_fused(bool rank1) {
+  static std::mutex mutex;
+  static bool done[2][64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mutex);
+  if (!done[rank1][dev]) {
+    auto kern = rank1 ? k_whiten_fused<true> : k_whiten_fused<false>;
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmemBytes));
+    done[rank1][dev] = true;
+  }
+  return SM_OK;
+}
+
+// One launch of the fused front end (k_whiten_fused) for group g.
+static int launch_front_fused(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, cudaStream_t st) {
+  auto kern = g.rank1 ? k_whiten_fused<true> : k_whiten_fused<false>;
+  dim3 grid(static_cast<unsigned>(g.fused_blocks), static_cast<unsigned>(g.batch));
+  return launch_kernel(kern, grid, dim3(256), static_cast<size_t>(kFusedSmemBytes), st, mats, mom_beta, mom_omb,
+                       g.rs_white, g.dmax, g.pre, g.rho, g.rho2, g.tk_white, g.xh, g.xl,
+                       static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp));
+}
+
+// Whitening / normalisation front end for one group (N3).  `fused`: one pass
+// (k_whiten_fused) when the group qualifies (16-byte aligned rows that fit
+// its shared memory) -- it scales the planes by the previous step's plane
+// scale, so a plan's first step always takes the two passes, which derive
+// the scale from this step's norm.  Both paths store the same planes up to
+// the power-of-two scale and set the same stage-1 alphas.
+static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float mom_omb, bool vec4, bool fused,
                      cudaStream_t st, Timer* tm, int64_t* launches) {
   const int B = g.batch;
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
+  if (fused && vec4 && g.fused_ok) {
+    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_fused(g, mats, mom_beta, mom_omb, st));
+    *launches += 1;
+    return SM_OK;
+  }
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
              dim3 grid(static_cast<unsigned>(cdiv(g.dmax, 8 * kWhitenRows)), B);
              auto kern = g.rank1 ? (vec4 ? k_whiten_rowstats<4, true> : k_whiten_rowstats<1, true>)
                                  : (vec4 ? k_whiten_rowstats<4, false> : k_whiten_rowstats<1, false>);
-             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
-                                  g.inv_norm, g.tk_white));
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld, g.pre,
+                                  g.rho, g.rho2, g.tk_white));
              return SM_OK;
            }()));
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
@@ -971,8 +1018,8 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
              dim3 grid(static_cast<unsigned>(tiles), B);
              auto kern = g.rank1 ? (vec4 ? k_whiten_write<true, true> : k_whiten_write<true, false>)
                                  : (vec4 ? k_whiten_write<false, true> : k_whiten_write<false, false>);
-             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld,
-                                  g.inv_norm, g.xh, g.xl, static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp)));
+             SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, mom_beta, mom_omb, g.rs_white, ld, g.pre,
+                                  g.xh, g.xl, static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp)));
              return SM_OK;
            }()));
   *launches += 2;
@@ -1107,6 +1154,23 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     }
     if (any_r1 && any_diag) return fail(SM_ERR_ARG, "a shape group mixes rank-one and diagonal A statistics");
     groups[g].rank1 = any_r1;
+    // The fused front end needs every matrix's rows in shared memory (at
+    // least 4 rows per CTA for a transposed matrix, whose rows become X
+    // columns); the rows' 16-byte alignment is checked per step (vec4).
+    bool fused_ok = true;
+    int fused_blocks = 0;
+    for (int i = 0; i < nm; ++i) {
+      if (mg[i] != static_cast<int>(g)) continue;
+      const SmMatrixSpec& m = spec->matrices[i];
+      const int rows = fused_rows(m.d_in);
+      if (m.d_in % 4 != 0 || rows < (m.d_out > m.d_in ? 4 : 1)) {
+        fused_ok = false;
+        break;
+      }
+      fused_blocks = std::max(fused_blocks, static_cast<int>(cdiv(m.d_out, rows)));
+    }
+    groups[g].fused_ok = fused_ok;
+    groups[g].fused_blocks = fused_blocks;
   }
   choose_tilings(groups, di->sms, pairs);
   MatDev* d_mats = cv.take<MatDev>(nm);
@@ -1231,6 +1295,88 @@ static int stats_run(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, int
                                                                           sum_sq, sum);
   SM_LAUNCHED();
   return SM_OK;
+}
+
+// ------------------------------------- statistics in one cluster launch
+#ifndef SMB_STATS_CLUSTER
+#define SMB_STATS_CLUSTER 1
+#endif
+// k_colstats_cluster for contiguous rows with 16-byte-aligned starts and
+// n_cols a multiple of the vector width: a cluster of `cl` CTAs per 128-byte
+// column slab, cl a power of two <= 16 chosen for about two CTAs per SM
+// (<= 8 where the device cannot co-schedule 16-CTA clusters of this kernel).
+static int stats_cluster_max(int* out) {
+  static int cached[64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  if (cached[dev] == 0) {
+    auto kern = k_colstats_cluster<float, true>;
+    int best = 8;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t cfg;
+      memset(&cfg, 0, sizeof(cfg));
+      cudaLaunchAttribute attr;
+      memset(&attr, 0, sizeof(attr));
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 16;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.gridDim = dim3(16);
+      cfg.blockDim = dim3(256);
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) best = 16;
+    }
+    cudaGetLastError();  // a refused query leaves no error behind
+    cached[dev] = best;
+  }
+  *out = cached[dev];
+  return SM_OK;
+}
+
+template <typename T, bool FIRST>
+static int stats_cluster_run(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, float* sum_sq, float* sum,
+                             cudaStream_t st, int sms) {
+  constexpr int kSlab = 8 * (16 / static_cast<int>(sizeof(T)));
+  const int64_t slabs = cdiv(n_cols, kSlab);
+  int cmax = 8;
+  SM_TRY(stats_cluster_max(&cmax));
+  int cl = 1;
+  while (cl < cmax && slabs * cl < 2 * static_cast<int64_t>(sms) && cl < n_rows) cl *= 2;
+  if (slabs * cl > (int64_t{1} << 31) - 1) return fail(SM_ERR_ARG, "too many columns for the statistics grid");
+  auto kern = k_colstats_cluster<T, FIRST>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchAttribute attr;
+  memset(&attr, 0, sizeof(attr));
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(cl);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(slabs * cl));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  SM_CUDA(cudaLaunchKernelEx(&cfg, kern, x, n_rows, n_cols, rs, cl, sum_sq, sum));
+  return SM_OK;
+}
+
+// Whether an input takes the one-launch cluster kernel.
+template <typename T>
+static bool stats_cluster_eligible(const T* x, int64_t n_cols, int64_t rs, int64_t cs) {
+  constexpr int kVec = 16 / sizeof(T);
+  return cs == 1 && rs >= n_cols && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+         ((rs * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (n_cols % kVec == 0);
 }
 
 // Largest number of row splits any input geometry of this shape may use.
@@ -1380,6 +1526,9 @@ static int stats_launch(const T* x, int64_t n_rows, int64_t n_cols, int64_t rs, 
   bool done = false;
   SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, true, partials, cap, st, sms, &done));
   if (done) return SM_OK;
+  if (SMB_STATS_CLUSTER && stats_cluster_eligible(x, n_cols, rs, cs))
+    return sum ? stats_cluster_run<T, true>(x, n_rows, n_cols, rs, sum_sq, sum, st, sms)
+               : stats_cluster_run<T, false>(x, n_rows, n_cols, rs, sum_sq, sum, st, sms);
   const int64_t per_split = n_cols * (sum ? 2 : 1);
   const int64_t max_splits = cap / per_split;
   if (max_splits < stats_max_splits(n_rows, n_cols, sms)) return fail(SM_ERR_WORKSPACE, "statistics workspace too small");
@@ -1432,6 +1581,9 @@ static int stats_launch_noalloc(const T* x, int64_t n_rows, int64_t n_cols, int6
   SM_TRY(stats_tma_run(x, n_rows, n_cols, rs, cs, sum_sq, sum, tickets, true, scratch,
                        static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS), st, sms, &done));
   if (done) return SM_OK;
+  if (SMB_STATS_CLUSTER && stats_cluster_eligible(x, n_cols, rs, cs))
+    return sum ? stats_cluster_run<T, true>(x, n_rows, n_cols, rs, sum_sq, sum, st, sms)
+               : stats_cluster_run<T, false>(x, n_rows, n_cols, rs, sum_sq, sum, st, sms);
   const int64_t per_split = n_cols * (sum ? 2 : 1);
   const int64_t cap = static_cast<int64_t>(SM_STATS_NOALLOC_SCRATCH_FLOATS) / per_split;
   if (cap < 1) return fail(SM_ERR_ARG, "too many columns for the no-allocation scratch");
@@ -1596,6 +1748,7 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
     for (auto& g : p->groups) {
       if (rc != SM_OK) break;
       rc = encode_group_maps(g);
+      if (rc == SM_OK && g.fused_ok) rc = prepare_front_fused(g.rank1);
     }
     for (size_t gi = 0; gi < p->groups.size() && rc == SM_OK; ++gi) {
       Group& g = p->groups[gi];
@@ -1632,7 +1785,8 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
   return SM_OK;
 }
 
-static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, cudaStream_t st, Timer* tm, int64_t* out);
+static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, bool first, cudaStream_t st, Timer* tm,
+                       int64_t* out);
 
 int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
   if (p == nullptr || args == nullptr || args->grads == nullptr || args->lrs == nullptr || args->counts == nullptr ||
@@ -1710,6 +1864,7 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
   SM_CUDA(cudaMemcpyAsync(p->d_mats, p->h_table.data(), p->table_bytes, cudaMemcpyHostToDevice, st));
 
   const bool use_graph = p->replay && tm == nullptr && p->steps_done > 0;
+  const bool first = p->steps_done == 0;
   ++p->steps_done;
   if (use_graph) {
     if (p->exec != nullptr && p->exec_vec4 != vec4) {
@@ -1719,7 +1874,7 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     if (p->exec == nullptr) {
       int64_t n = 0;
       SM_CUDA(cudaStreamBeginCapture(p->cap_stream, cudaStreamCaptureModeThreadLocal));
-      const int rc = launch_step(p, vec4, p->cap_stream, nullptr, &n);
+      const int rc = launch_step(p, vec4, false, p->cap_stream, nullptr, &n);
       cudaGraph_t graph = nullptr;
       const cudaError_t e = cudaStreamEndCapture(p->cap_stream, &graph);
       if (rc != SM_OK) {
@@ -1740,18 +1895,20 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     p->launches_last = p->exec_launches;
     return SM_OK;
   }
-  SM_TRY(launch_step(p, vec4, st, tm, &launches));
+  SM_TRY(launch_step(p, vec4, first, st, tm, &launches));
   p->launches_last = launches;
   return SM_OK;
 }
 
-// Every kernel of one step, in stream order on `st`.
-static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, cudaStream_t st, Timer* tm, int64_t* out) {
+// Every kernel of one step, in stream order on `st`.  `first`: the plan's
+// first step (the two-pass front end; see run_front).
+static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, bool first, cudaStream_t st, Timer* tm,
+                       int64_t* out) {
   const int ns = static_cast<int>(p->stats.size());
   int64_t launches = 0;
   // The first kernel follows the descriptor upload in plain stream order;
   // every later one may launch early (programmatic dependent launch).
-  PdlScope first(false);
+  PdlScope plain(false);
   SM_TIMED(tm, SM_TCLASS_STATS, 0.0, st, ([&]() -> int {
              if (ns > 0) SM_TRY(launch_kernel(k_stats_finish, dim3(ns), dim3(256), 0, st, p->d_stats,
                                               p->stat_beta, p->stat_omb));
@@ -1760,7 +1917,8 @@ static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, cudaStream_t
   ++launches;
   PdlScope rest(p->pdl);
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
-    SM_TRY(run_front(p->groups[gi], p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, st, tm, &launches));
+    SM_TRY(run_front(p->groups[gi], p->d_mats, p->mom_beta, p->mom_omb, vec4[gi] != 0, !first, st, tm,
+                     &launches));
   SM_TRY(run_s8(p->groups, p->s8, st, tm, &launches));
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
@@ -1884,7 +2042,7 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   g.host_tmask.assign(batch, rows > cols ? 1 : 0);
   SM_CUDA(cudaMemcpyAsync(g.tmask, g.host_tmask.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, st));
   int64_t launches = 0;
-  SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, st, nullptr, &launches));
+  SM_TRY(run_front(g, d_mats, 0.0f, 1.0f, vec4, false, st, nullptr, &launches));
   std::vector<Group> groups(1, g);
   S8Launches s8;
   build_s8_launches(groups, di->sms, pairs, nullptr, &s8);  // round-robin tiles: no schedule tables

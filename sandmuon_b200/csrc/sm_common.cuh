@@ -32,6 +32,8 @@ enum StatusCode : int {
   kStatusTimeoutEpilogue = 0x103,
   kStatusTimeoutStatsLoad = 0x111,
   kStatusTimeoutStatsReduce = 0x112,
+  kStatusTimeoutFrontLoad = 0x121,
+  kStatusFrontRange = 0x122,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -128,6 +130,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
       : "memory");
 }
 
+// Contiguous global -> shared copy of `bytes` bytes (both addresses 16-byte
+// aligned, `bytes` a multiple of 16) on the TMA engine, completing as
+// transaction bytes on `bar`.  Plain (non-multicast) form.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // ------------------------------------------------------- CTA pairs (2-SM)
 // A cluster of two CTAs on neighbouring SMs computes one 256-row tile with
 // tcgen05 cta_group::2: each CTA stages its own 128 A rows and half of the B
@@ -146,6 +157,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
+}
+
+// 64-bit load from the shared memory of a cluster CTA (a shared::cluster
+// address from mapa_shared).
+__device__ __forceinline__ double ld_shared_cluster_f64(uint32_t cluster_addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 // All threads of both CTAs; release/acquire orders shared-memory writes

@@ -172,6 +172,112 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ------------------------------------- N1, one launch reduced in a cluster
+// For contiguous rows with 16-byte-aligned starts and n_cols a multiple of
+// the vector width (16 bytes of T).  A cluster of CL CTAs owns one slab of
+// 128 bytes of every row (32 FP32 / 64 BF16 columns); its CTAs split the
+// rows in contiguous ranges.  In a CTA, 8 lanes cover a row's slab with one
+// 16-byte load each, so the 256 threads are 32 row lanes x 8 column lanes,
+// each keeping kStatsUnroll loads in flight.  Sums: FP32 per thread over its
+// rows, then FP64 over the 32 row lanes in order, then the cluster's leader
+// adds its CTAs' FP64 sums in rank order through distributed shared memory
+// and accumulates into sum_sq / sum.  One launch per call, no workspace,
+// reproducible results.
+constexpr int kStatsUnroll = 8;
+
+template <typename T, bool FIRST>
+__global__ void __launch_bounds__(256)
+    k_colstats_cluster(const T* __restrict__ x, int64_t n_rows, int64_t n_cols, int64_t rs, int cl,
+                       float* __restrict__ sum_sq, float* __restrict__ sum) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int kSlab = 8 * VEC;  // columns of one cluster
+  // row-lane sums; the leader reuses them for the cluster's FP64 sums
+  // (16 x kSlab doubles fit in 32 x (kSlab + 1) floats)
+  __shared__ __align__(8) float sh_sq[32][kSlab + 1];
+  __shared__ __align__(8) float sh_s[FIRST ? 32 : 1][FIRST ? kSlab + 1 : 1];
+  __shared__ double cta_sq[kSlab];
+  __shared__ double cta_s[FIRST ? kSlab : 1];
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int64_t slab = blockIdx.x / cl;
+  const int cl_lane = threadIdx.x & 7;   // 16-byte column lane
+  const int row_lane = threadIdx.x >> 3;  // 0..31
+  const int64_t col0 = slab * kSlab + cl_lane * VEC;
+  const int64_t per = (n_rows + cl - 1) / cl;
+  const int64_t r_begin = min(static_cast<int64_t>(rank) * per, n_rows);
+  const int64_t r_end = min(r_begin + per, n_rows);
+  float acc_sq[VEC], acc_s[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc_sq[i] = acc_s[i] = 0.0f;
+  if (col0 < n_cols) {
+    const T* base = x + col0;
+    int64_t r = r_begin + row_lane;
+    for (; r + (kStatsUnroll - 1) * 32 < r_end; r += kStatsUnroll * 32) {
+      float v[kStatsUnroll][VEC];
+#pragma unroll
+      for (int u = 0; u < kStatsUnroll; ++u) load_vec<T, VEC>(base + (r + u * 32) * rs, 1, v[u]);
+#pragma unroll
+      for (int u = 0; u < kStatsUnroll; ++u) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          acc_sq[i] += v[u][i] * v[u][i];
+          if (FIRST) acc_s[i] += v[u][i];
+        }
+      }
+    }
+    for (; r < r_end; r += 32) {
+      float v[VEC];
+      load_vec<T, VEC>(base + r * rs, 1, v);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        acc_sq[i] += v[i] * v[i];
+        if (FIRST) acc_s[i] += v[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    sh_sq[row_lane][cl_lane * VEC + i] = acc_sq[i];
+    if (FIRST) sh_s[row_lane][cl_lane * VEC + i] = acc_s[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < kSlab) {
+    double t2 = 0.0, t1 = 0.0;
+#pragma unroll 8
+    for (int l = 0; l < 32; ++l) {
+      t2 += static_cast<double>(sh_sq[l][threadIdx.x]);
+      if (FIRST) t1 += static_cast<double>(sh_s[l][threadIdx.x]);
+    }
+    cta_sq[threadIdx.x] = t2;
+    if (FIRST) cta_s[threadIdx.x] = t1;
+  }
+  // every CTA's sums are in its shared memory before the leader reads them
+  cluster_sync_all();
+  if (rank == 0) {
+    // all of the cluster's sums fetched at once (one round of remote loads),
+    // then added in rank order
+    double* all_sq = reinterpret_cast<double*>(&sh_sq[0][0]);  // [cl][kSlab], reusing the staging
+    double* all_s = FIRST ? reinterpret_cast<double*>(&sh_s[0][0]) : nullptr;
+    for (int e = threadIdx.x; e < cl * kSlab; e += blockDim.x) {
+      const int k = e / kSlab, c = e - k * kSlab;
+      all_sq[e] = ld_shared_cluster_f64(mapa_shared(smem_u32(&cta_sq[c]), static_cast<uint32_t>(k)));
+      if (FIRST) all_s[e] = ld_shared_cluster_f64(mapa_shared(smem_u32(&cta_s[c]), static_cast<uint32_t>(k)));
+    }
+    __syncthreads();
+    const int64_t col = slab * kSlab + threadIdx.x;
+    if (threadIdx.x < kSlab && col < n_cols) {
+      double t2 = 0.0, t1 = 0.0;
+      for (int k = 0; k < cl; ++k) {
+        t2 += all_sq[k * kSlab + threadIdx.x];
+        if (FIRST) t1 += all_s[k * kSlab + threadIdx.x];
+      }
+      sum_sq[col] += static_cast<float>(t2);
+      if (FIRST) sum[col] += static_cast<float>(t1);
+    }
+  }
+  // no CTA leaves while the leader may still read its shared memory
+  cluster_sync_all();
+}
+
 // ------------------------------------------------ N1, TMA-fed single launch
 // For contiguous 16-byte-aligned rows.  A persistent CTA (one per SM) takes
 // one column group (kStatsCols columns) and a contiguous range of its row
@@ -462,17 +568,59 @@ struct MatDev {
 // Per param row o (contiguous, d_in long):
 //   m' = .8 m + .2 g ; s = .8 m' + .2 g          (sandmuon/optimizer.py:246-248)
 //   y  = inv_b[o] * s * inv_a                    (whitening diagonals)
-//   rs[o] = { y . z_a , |y|^2 }
+//   rs[o] = { y . z_a , |y| }   (|y| from an FP64 sum of squares, so rows of
+//                                tiny or huge gradients neither underflow nor
+//                                overflow on the way to the matrix norm)
 // The rank-one whitening correction V = Y + c (Y z) z^T acts along d_in in
 // both orientations, so its dot products are row dots of the param layout.
 // The last CTA of a matrix to finish (an integer ticket per matrix, zero
 // between launches: that CTA resets it) also reduces the matrix's |y|^2 row
-// sums, in row order, into
-//   inv_norm[b] = 1 / max(|Y_b|_F, 1e-30).
-// The S8 map is invariant to the scale of its input (stage 1 divides by
-// s = 1.35 |G^2|_F^(1/4)), so any norm that keeps X in range reproduces
-// x / |x|_F (sandmuon/optimizer.py:77-78); |Y|_F bounds |V|_F within the
-// factor rho = sqrt(1 + |z|^2) of the rank-one whitener and never cancels.
+// sums, in row order, into the matrix's plane scale and stage-1 alphas
+// (plane_scale_for, set_stage1_alphas below).
+//
+// Normalisation.  The S8 input is x = v / max(|v|_F, 1e-30)
+// (sandmuon/optimizer.py:77-78).  The S8 map is invariant to the scale of
+// its input (stage 1 divides by s = 1.35 |G^2|_F^(1/4)), so any norm that
+// keeps X in range reproduces it; |Y|_F bounds |V|_F within the factor
+// sqrt(1 + |z|^2) of the rank-one whitener and never cancels.  The hi/lo
+// planes hold v * 2^k, a power-of-two scale near 1 / |Y|_F (exact: the split
+// commutes with it), and the stage-1 products take the remaining factor
+// rho = (1 / max(|Y|_F, 1e-30)) / 2^k as their alpha: rho^2 for X X^T, rho / s
+// for P X.  Every result is then bitwise independent of k.
+
+// 2^k with norm * 2^k in [1, 2), k clamped to [-126, 126]; 1 for a zero or
+// non-finite norm.
+__device__ __forceinline__ float plane_scale_for(double norm) {
+  if (!(norm > 0.0) || !isfinite(norm)) return 1.0f;
+  int e = 0;
+  frexp(norm, &e);  // norm in [2^(e-1), 2^e)
+  return ldexpf(1.0f, min(max(1 - e, -126), 126));
+}
+
+// Stage-1 alphas of planes written as v * `used`: rho = (1 / max(norm, 1e-30))
+// / used, exactly (used is a power of two), and rho^2; 0 for a zero matrix.
+__device__ __forceinline__ void set_stage1_alphas(double norm, float used, float* rho, float* rho2, int b) {
+  const float inv = 1.0f / fmaxf(static_cast<float>(norm), 1e-30f);
+  const float r = norm > 0.0 ? inv / used : 0.0f;
+  rho[b] = r;
+  rho2[b] = r * r;
+}
+
+// Sum over rows 0..n of rs[row].y^2 in a fixed order (FP64), whole CTA.
+__device__ __forceinline__ double rows_sum_sq_y(const float2* rs, int n, double* sh) {
+  double acc = 0.0;
+  for (int o = threadIdx.x; o < n; o += blockDim.x) {
+    const double v = static_cast<double>(__ldcg(&rs[o].y));
+    acc += v * v;
+  }
+  acc = warp_sum_d(acc);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += sh[w];
+  return t;
+}
 
 // Sum over rows 0..n of rs[row].y in a fixed order (FP64), whole CTA.
 __device__ __forceinline__ double rows_sum_y(const float2* rs, int n, double* sh) {
@@ -499,7 +647,8 @@ constexpr int kMapbackRows = 4;
 template <int VEC, bool RANK1>
 __global__ void __launch_bounds__(256)
     k_whiten_rowstats(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs,
-                      int ld_rs, float* __restrict__ inv_norm, unsigned* __restrict__ tickets) {
+                      int ld_rs, float* __restrict__ pre, float* __restrict__ rho, float* __restrict__ rho2,
+                      unsigned* __restrict__ tickets) {
   grid_dep_wait();
   grid_dep_launch();
   __shared__ double sh[8];
@@ -514,7 +663,8 @@ __global__ void __launch_bounds__(256)
     const bool has_mom = md.mom != nullptr;
     const float* g[kWhitenRows];
     const float* m[kWhitenRows];
-    float ib[kWhitenRows], dot[kWhitenRows], sq[kWhitenRows];
+    float ib[kWhitenRows], dot[kWhitenRows];
+    double sq[kWhitenRows];
 #pragma unroll
     for (int r = 0; r < kWhitenRows; ++r) {
       const int o = min(obase + r, md.d_out - 1);
@@ -561,34 +711,40 @@ __global__ void __launch_bounds__(256)
           const float mn = mom_beta * mv[e] + omb * gv[e];
           const float src = has_mom ? mom_beta * mn + omb * gv[e] : gv[e];
           const float y = (src * ib[r]) * av[e];
-          sq[r] += y * y;
+          sq[r] += static_cast<double>(y) * y;
           if (RANK1) dot[r] += y * zv[e];
         }
       }
     }
 #pragma unroll
     for (int r = 0; r < kWhitenRows; ++r) {
-      const float s_r = warp_sum(sq[r]);
+      const double s_r = warp_sum_d(sq[r]);
       const float d_r = RANK1 ? warp_sum(dot[r]) : 0.0f;
-      if (lane == 0 && obase + r < md.d_out) rsb[obase + r] = make_float2(d_r, s_r);
+      if (lane == 0 && obase + r < md.d_out) rsb[obase + r] = make_float2(d_r, static_cast<float>(sqrt(s_r)));
     }
   }
   if (last_cta_of(tickets + blockIdx.y, static_cast<unsigned>((md.d_out + 8 * kWhitenRows - 1) / (8 * kWhitenRows)))) {
-    const double t = rows_sum_y(rsb, md.d_out, sh);
-    if (threadIdx.x == 0) inv_norm[blockIdx.y] = 1.0f / fmaxf(static_cast<float>(sqrt(t)), 1e-30f);
+    const double t = rows_sum_sq_y(rsb, md.d_out, sh);
+    // k_whiten_write writes the planes with the scale set here
+    if (threadIdx.x == 0) {
+      const double norm = sqrt(t);
+      const float used = plane_scale_for(norm);
+      pre[blockIdx.y] = used;
+      set_stage1_alphas(norm, used, rho, rho2, blockIdx.y);
+    }
   }
 }
 
 // ========================================== N3 pass 2: whiten + split write
 // Tile of 32 param rows x 64 param columns per CTA (256 threads); grid
 // (tiles of the group's largest matrix, matrices).
-//   m' written back ; v = y + c * dot[o] * z[i] ; x = v * inv_norm
+//   m' written back ; v = y + c * dot[o] * z[i] ; x = v * pre[b]
 //   X_hi/X_lo at the oriented position: (o, i), or (i, o) when transposed
 //   (staged through shared memory so both reads and writes are coalesced).
 template <bool RANK1, bool VEC4>
 __global__ void __launch_bounds__(256)
     k_whiten_write(const MatDev* __restrict__ mats, float mom_beta, float omb, const float2* __restrict__ rs, int ld_rs,
-                   const float* __restrict__ inv_norm, __nv_bfloat16* __restrict__ xh,
+                   const float* __restrict__ pre, __nv_bfloat16* __restrict__ xh,
                    __nv_bfloat16* __restrict__ xl, int64_t rp, int64_t cp) {
   grid_dep_wait();
   grid_dep_launch();
@@ -602,7 +758,7 @@ __global__ void __launch_bounds__(256)
   const int o0 = static_cast<int>(blockIdx.x / tiles_x) * 32;
   const int i0 = static_cast<int>(blockIdx.x % tiles_x) * 64;
   if (o0 >= md.d_out) return;
-  const float scale = inv_norm[b];
+  const float scale = pre[b];
   const float coef = RANK1 ? md.scal_a[0] : 0.0f;
   const bool has_mom = md.mom != nullptr;
   const int tx = threadIdx.x & 15;   // 4 consecutive columns
@@ -721,12 +877,252 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ======================================== N3 in one pass: fused front end
+// From a plan's second step on, one kernel replaces the two above for groups
+// whose rows are 16-byte aligned.  A CTA owns R consecutive param rows of one
+// matrix (R = fused_rows(d_in): as many as fit kFusedSmemBytes, a power of
+// two <= 16):
+//   1. one thread copies the R gradient rows and R momentum rows into shared
+//      memory with bulk async copies (cp.async.bulk, no multicast)
+//      completing on one mbarrier (a bounded wait);
+//   2. row statistics from shared memory: y . z_a and |y| (FP64 sum of
+//      squares; rows split over 8 / R warps when R < 8, combined in order);
+//   3. m' is written back and the hi/lo planes of x = v * pre[b] at the
+//      oriented position; the param rows of a transposed matrix are columns
+//      of X, so there each thread writes the R consecutive bf16 of one X row.
+// DRAM traffic: g and m read once, m' and the planes written once (16 bytes
+// per param, against 24 for the two passes).  Measured on B200 (config 1,
+// ncu launch lists): 86 us for the 36 x 768^2 group (two passes 111 us) and
+// 188 us for the 18 x 768 x 3072 group (213 us).  pre[b] is the previous
+// step's plane scale; the last CTA of a matrix to finish (an integer ticket
+// per matrix, zero between launches) reduces the row norms into the stage-1
+// alphas for it and the next step's pre[b].  If |Y|_F * pre[b] falls outside
+// [2^-60, 2^60] (the norm moved that far since the previous step, so the
+// planes may have lost range) it sets kStatusFrontRange.
+constexpr int kFusedSmemBytes = 96 * 1024;
+
+__host__ __device__ constexpr int fused_rows(int d_in) {
+  int r = 16;
+  while (r > 0 && static_cast<int64_t>(r) * d_in * 8 > kFusedSmemBytes) r >>= 1;
+  return r;
+}
+
+// (y . z, |y|^2) of one row segment
+struct FrontSeg {
+  float dot;
+  double sq;
+};
+
+template <bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_whiten_fused(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs, int ld_rs,
+                   float* __restrict__ pre, float* __restrict__ rho, float* __restrict__ rho2,
+                   unsigned* __restrict__ tickets, __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl,
+                   int64_t rp, int64_t cp) {
+  extern __shared__ __align__(128) uint8_t fused_smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ FrontSeg s_seg[8];
+  __shared__ float s_dot[16], s_ib[16];
+  __shared__ double sh[8];
+  __shared__ int s_abort;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int b = blockIdx.y;
+  const MatDev md = mats[b];
+  const int R = fused_rows(md.d_in);
+  const int o0 = blockIdx.x * R;
+  if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
+  const int rows = min(R, md.d_out - o0);
+  const int n = md.d_in;
+  const int n4 = n / 4;
+  float* sg = reinterpret_cast<float*>(fused_smem);
+  float* sm = sg + static_cast<size_t>(R) * n;
+  const float scale = pre[b];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float2* rsb = rs + static_cast<int64_t>(b) * ld_rs;
+
+  // ---- 1. the rows into shared memory
+  const uint32_t bar_a = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(bar_a, 1);
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x < rows) s_ib[threadIdx.x] = md.inv_b[o0 + threadIdx.x];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t row_bytes = static_cast<uint32_t>(n) * 4u;
+    mbar_arrive_expect_tx(bar_a, 2u * static_cast<uint32_t>(rows) * row_bytes);
+    for (int r = 0; r < rows; ++r) {
+      const int64_t off = static_cast<int64_t>(o0 + r) * n;
+      bulk_load(smem_u32(sg + static_cast<size_t>(r) * n), md.grad + off, row_bytes, bar_a);
+      bulk_load(smem_u32(sm + static_cast<size_t>(r) * n), md.mom + off, row_bytes, bar_a);
+    }
+  }
+  bool ok = mbar_wait(bar_a, 0, &s_abort, kStatusTimeoutFrontLoad);
+  ok = __syncthreads_and(ok) != 0;
+  if (!ok) {
+    // let the copies in flight land (bounded) before this CTA's shared memory goes
+    mbar_wait(bar_a, 0, nullptr, kStatusTimeoutFrontLoad);
+  } else {
+    // ---- 2. row statistics: segment = (row, part), S parts per row
+    const int S = R >= 8 ? 1 : 8 / R;
+    for (int seg = warp; seg < rows * S; seg += 8) {
+      const int r = seg / S, part = seg - r * S;
+      const int lo4 = part * n4 / S, hi4 = (part + 1) * n4 / S;
+      const float4* g4 = reinterpret_cast<const float4*>(sg + static_cast<size_t>(r) * n);
+      const float4* m4 = reinterpret_cast<const float4*>(sm + static_cast<size_t>(r) * n);
+      const float ib = s_ib[r];
+      float dot = 0.0f;
+      double sq = 0.0;
+      for (int i4 = lo4 + lane; i4 < hi4; i4 += 32) {
+        const float4 gv = g4[i4], mv = m4[i4];
+        const float4 av = *reinterpret_cast<const float4*>(md.inv_a + 4 * i4);
+        float4 zv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (RANK1) zv = *reinterpret_cast<const float4*>(md.z_a + 4 * i4);
+        const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float ae[4] = {av.x, av.y, av.z, av.w}, ze[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mn = mom_beta * me[e] + omb * ge[e];
+          const float src = mom_beta * mn + omb * ge[e];
+          const float y = (src * ib) * ae[e];
+          sq += static_cast<double>(y) * y;
+          if (RANK1) dot += y * ze[e];
+        }
+      }
+      sq = warp_sum_d(sq);
+      dot = RANK1 ? warp_sum(dot) : 0.0f;
+      if (lane == 0) {
+        s_seg[seg & 7].dot = dot;
+        s_seg[seg & 7].sq = sq;
+        if (S == 1) {
+          s_dot[r] = dot;
+          rsb[o0 + r] = make_float2(dot, static_cast<float>(sqrt(sq)));
+        }
+      }
+    }
+    __syncthreads();
+    if (S > 1 && threadIdx.x < rows) {
+      const int r = threadIdx.x;
+      float dot = 0.0f;
+      double sq = 0.0;
+      for (int part = 0; part < S; ++part) {
+        dot += s_seg[r * S + part].dot;
+        sq += s_seg[r * S + part].sq;
+      }
+      s_dot[r] = dot;
+      rsb[o0 + r] = make_float2(dot, static_cast<float>(sqrt(sq)));
+    }
+    __syncthreads();
+
+    // ---- 3. momentum and planes
+    const float coef = RANK1 ? md.scal_a[0] : 0.0f;
+    const int64_t plane = static_cast<int64_t>(b) * rp * cp;
+    if (!md.transposed) {
+      for (int it = threadIdx.x; it < rows * n4; it += blockDim.x) {
+        const int r = it / n4, i4 = it - r * n4;
+        const int o = o0 + r;
+        const float4 gv = reinterpret_cast<const float4*>(sg + static_cast<size_t>(r) * n)[i4];
+        const float4 mv = reinterpret_cast<const float4*>(sm + static_cast<size_t>(r) * n)[i4];
+        const float4 av = *reinterpret_cast<const float4*>(md.inv_a + 4 * i4);
+        float4 zv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (RANK1) zv = *reinterpret_cast<const float4*>(md.z_a + 4 * i4);
+        const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float ae[4] = {av.x, av.y, av.z, av.w}, ze[4] = {zv.x, zv.y, zv.z, zv.w};
+        const float ib = s_ib[r], cw = coef * s_dot[r];
+        float mn[4], h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          mn[e] = mom_beta * me[e] + omb * ge[e];
+          const float src = mom_beta * mn[e] + omb * ge[e];
+          float v = (src * ib) * ae[e];
+          if (RANK1) v += cw * ze[e];
+          split_hilo(v * scale, h[e], l[e]);
+        }
+        *reinterpret_cast<float4*>(md.mom + static_cast<int64_t>(o) * n + 4 * i4) =
+            make_float4(mn[0], mn[1], mn[2], mn[3]);
+        const int64_t xo = plane + static_cast<int64_t>(o) * cp + 4 * i4;
+        *reinterpret_cast<uint2*>(xh + xo) = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+        *reinterpret_cast<uint2*>(xl + xo) = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+      }
+    } else {
+      // X row i = param column i; this CTA's rows are X columns o0 .. o0+rows
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float a = md.inv_a[i];
+        const float z = RANK1 ? md.z_a[i] : 0.0f;
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int r = 0; r < 16; r += 2) {
+          float h2[2] = {0.f, 0.f}, l2[2] = {0.f, 0.f};
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int rr = r + q;
+            if (rr < rows) {
+              const float gv = sg[static_cast<size_t>(rr) * n + i];
+              const float mv = sm[static_cast<size_t>(rr) * n + i];
+              const float mn = mom_beta * mv + omb * gv;
+              md.mom[static_cast<int64_t>(o0 + rr) * n + i] = mn;
+              const float src = mom_beta * mn + omb * gv;
+              float v = (src * s_ib[rr]) * a;
+              if (RANK1) v += coef * s_dot[rr] * z;
+              split_hilo(v * scale, h2[q], l2[q]);
+            }
+          }
+          hw[r / 2] = pack_bf16x2(h2[0], h2[1]);
+          lw[r / 2] = pack_bf16x2(l2[0], l2[1]);
+        }
+        __nv_bfloat16* dh = xh + plane + static_cast<int64_t>(i) * cp + o0;
+        __nv_bfloat16* dl = xl + plane + static_cast<int64_t>(i) * cp + o0;
+        if (rows == 16) {  // o0 % 16 == 0: 32-byte aligned
+          reinterpret_cast<uint4*>(dh)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          reinterpret_cast<uint4*>(dh)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+          reinterpret_cast<uint4*>(dl)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          reinterpret_cast<uint4*>(dl)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        } else if (rows == 8) {  // o0 % 8 == 0: 16-byte aligned
+          reinterpret_cast<uint4*>(dh)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          reinterpret_cast<uint4*>(dl)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        } else if (rows % 2 == 0) {  // o0 is even: 4-byte aligned pairs
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            if (2 * w < rows) {
+              reinterpret_cast<uint32_t*>(dh)[w] = hw[w];
+              reinterpret_cast<uint32_t*>(dl)[w] = lw[w];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            if (r < rows) {
+              const uint32_t wh = hw[r / 2], wl = lw[r / 2];
+              dh[r] = __ushort_as_bfloat16(static_cast<unsigned short>((r & 1) ? (wh >> 16) : (wh & 0xFFFFu)));
+              dl[r] = __ushort_as_bfloat16(static_cast<unsigned short>((r & 1) ? (wl >> 16) : (wl & 0xFFFFu)));
+            }
+          }
+        }
+      }
+    }
+  }
+  // ---- 4. the matrix's last CTA: stage-1 alphas for these planes, next scale
+  if (last_cta_of(tickets + b, static_cast<unsigned>((md.d_out + R - 1) / R))) {
+    const double t = rows_sum_sq_y(rsb, md.d_out, sh);
+    if (threadIdx.x == 0) {
+      const double norm = sqrt(t);
+      set_stage1_alphas(norm, scale, rho, rho2, b);
+      const double placed = norm * scale;
+      if (norm > 0.0 && !(placed > 0x1p-60 && placed < 0x1p60)) atomicExch(&g_status, kStatusFrontRange);
+      pre[b] = plane_scale_for(norm);
+    }
+  }
+}
+
 // ================================================ S8 stage-1 scale and poly
 // s[b] = max(1.35 * |G2_b|_F^(1/4), 1e-30) from the per-tile partial sums of
-// squares written by the G*G epilogue (sandmuon/optimizer.py:81).
+// squares written by the G*G epilogue (sandmuon/optimizer.py:81), and the
+// stage-1 P X alpha rho[b] / s[b].
 __global__ void __launch_bounds__(256)
     k_reduce_s8scale(const float* __restrict__ partials, int per_mat, float margin, float* __restrict__ s,
-                     float* __restrict__ s_inv) {
+                     float* __restrict__ s_inv, const float* __restrict__ rho, float* __restrict__ px_alpha) {
   grid_dep_wait();
   grid_dep_launch();
   __shared__ double sh[8];
@@ -739,6 +1135,8 @@ __global__ void __launch_bounds__(256)
     const float sv = fmaxf(margin * powf(nrm, 0.25f), 1e-30f);
     s[blockIdx.x] = sv;
     s_inv[blockIdx.x] = 1.0f / sv;
+    // stage-1 P X: (P x) / s with x = rho * (stored planes)
+    px_alpha[blockIdx.x] = rho[blockIdx.x] * (1.0f / sv);
   }
 }
 
@@ -820,30 +1218,37 @@ __global__ void __launch_bounds__(256)
       s1[r] = 0.f;
       s2[r] = 0.f;
     }
-    const int n4 = md.d_in & ~3;
-    for (int i = lane * 4; i < n4; i += 128) {
-      const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i);
-      const float aa[4] = {a.x * a.x, a.y * a.y, a.z * a.z, a.w * a.w};
-      float zz[4] = {0.f, 0.f, 0.f, 0.f};
-      if (RANK1) {
-        const float4 z = *reinterpret_cast<const float4*>(md.z_a + i);
-        zz[0] = z.x; zz[1] = z.y; zz[2] = z.z; zz[3] = z.w;
+    // 8 BF16 (16 bytes) per lane and row: Q rows are 16-byte aligned (row
+    // strides are multiples of 128 elements); the rows' tails go one by one
+    const int n8 = md.d_in & ~7;
+    for (int i = lane * 8; i < n8; i += 256) {
+      float aa[8], zz[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 a = *reinterpret_cast<const float4*>(md.inv_a + i + 4 * h);
+        aa[4 * h + 0] = a.x * a.x; aa[4 * h + 1] = a.y * a.y; aa[4 * h + 2] = a.z * a.z; aa[4 * h + 3] = a.w * a.w;
+        float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (RANK1) z = *reinterpret_cast<const float4*>(md.z_a + i + 4 * h);
+        zz[4 * h + 0] = z.x; zz[4 * h + 1] = z.y; zz[4 * h + 2] = z.z; zz[4 * h + 3] = z.w;
       }
+      uint4 raw[kMapbackRows];
+#pragma unroll
+      for (int r = 0; r < kMapbackRows; ++r) raw[r] = *reinterpret_cast<const uint4*>(qr[r] + i);
 #pragma unroll
       for (int r = 0; r < kMapbackRows; ++r) {
-        const uint2 v = *reinterpret_cast<const uint2*>(qr[r] + i);
-        const float vv[4] = {bf16_lo_to_f(v.x), bf16_hi_to_f(v.x), bf16_lo_to_f(v.y), bf16_hi_to_f(v.y)};
+        const uint32_t w[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          s1[r] += aa[e] * vv[e] * vv[e];
+        for (int e = 0; e < 8; ++e) {
+          const float v = (e & 1) ? bf16_hi_to_f(w[e >> 1]) : bf16_lo_to_f(w[e >> 1]);
+          s1[r] += aa[e] * v * v;
           if (RANK1) {
-            t[r] += zz[e] * vv[e];
-            s2[r] += aa[e] * zz[e] * vv[e];
+            t[r] += zz[e] * v;
+            s2[r] += aa[e] * zz[e] * v;
           }
         }
       }
     }
-    for (int i = n4 + lane; i < md.d_in; i += 32) {
+    for (int i = n8 + lane; i < md.d_in; i += 32) {
       const float a2 = md.inv_a[i] * md.inv_a[i];
       const float z = RANK1 ? md.z_a[i] : 0.f;
 #pragma unroll

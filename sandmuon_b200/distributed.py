@@ -30,7 +30,7 @@ import re
 import torch
 import torch.distributed as dist
 
-from .workloads import s8_executed_flops
+from .workloads import s8_dense_flops
 
 _LAYER = re.compile(r"\.h\.(\d+)\.")
 
@@ -50,7 +50,7 @@ def partition_matrices(named_shapes: dict[str, tuple[int, int]], world: int, how
         return {n: index[layers[n]] * world // len(distinct) for n in names}
     if how != "lpt":
         raise ValueError(f"unknown partition {how!r} (expected 'lpt' or 'layer')")
-    cost = {n: s8_executed_flops([named_shapes[n]]) for n in names}
+    cost = {n: s8_dense_flops([named_shapes[n]]) for n in names}
     load = [0.0] * world
     owner = {}
     for n in sorted(names, key=lambda k: (-cost[k], names.index(k))):

@@ -7,7 +7,6 @@ allocates memory here; all arithmetic happens in the library's kernels.
 from __future__ import annotations
 
 import ctypes
-import math
 from dataclasses import dataclass
 
 import torch
@@ -317,14 +316,3 @@ def apply_bf16_delta_multi(pairs: list[tuple[torch.Tensor, torch.Tensor]], devic
     with torch.cuda.device(device):
         rc = _lib.load().sm_apply_bf16_delta_multi(arr, len(pairs), _stream(device))
     _lib.check(rc, "sm_apply_bf16_delta_multi")
-
-
-def s8_flops_per_matrix(rows: int, cols: int) -> float:
-    """Executed BF16 tensor FLOPs of one S8 map: 7 * (4 r^2 c + 2 r^3), r <= c
-    (stage 1 counts its three compensated products)."""
-    r, c = min(rows, cols), max(rows, cols)
-    return 7.0 * (4.0 * r * r * c + 2.0 * r ** 3)
-
-
-def padded(n: int, m: int = 128) -> int:
-    return int(math.ceil(n / m) * m)

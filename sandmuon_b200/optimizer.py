@@ -443,7 +443,14 @@ class RankOneAWeightedPE(DiagonalWeightedPE):
     def __init__(self, model: nn.Module, lr: float, *,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
                  process_group=None, partition: str = "lpt", exchange: str = "weights",
-                 reduce_gradients: bool = False):
+                 reduce_gradients: bool = False, split_sides: bool = False):
         super().__init__(model, lr, rank_one_a=True, module_filter=module_filter,
                          process_group=process_group, partition=partition, exchange=exchange,
                          reduce_gradients=reduce_gradients)
+        # The historical option of that name (reproduction/odl/optim/
+        # diagonal_weighted_pe.py:408-410, 500-543) applies the rank-one
+        # whitening and mapback on the activation side only.  The engine's
+        # kernels always do: the cotangent side has no rank-one term, and the
+        # activation side's correction runs along d_in in either orientation.
+        # Both settings therefore run the same kernels, with identical results.
+        self.split_sides = bool(split_sides)

@@ -88,14 +88,17 @@ def inject_statistics(opt, stats: dict) -> None:
         st["b_count"] = int(entry["b_count"])
 
 
-def s8_executed_flops(shapes) -> float:
-    """Executed BF16 tensor FLOPs of one S8 map per matrix, summed:
-    7 * (4 r^2 c + 2 r^3) with r <= c (stage 1's three compensated products
-    plus four plain stages)."""
+def s8_dense_flops(shapes) -> float:
+    """Dense tensor-core FLOPs of the engine's S8 precision schedule per
+    matrix, summed: 13 x (4 r^2 c + 2 r^3) with r <= c -- stages 1-4 run
+    their three products (X X^T, G G, P X) compensated (three BF16 products
+    each), stage 5 plain.  Symmetric products are counted dense; the engine
+    computes only their upper block triangle (sm_s8_executed_flops gives the
+    executed count).  Used as the relative cost of a matrix when sharding."""
     total = 0.0
     for rows, cols in shapes:
         r, c = min(rows, cols), max(rows, cols)
-        total += 7.0 * (4.0 * r * r * c + 2.0 * r ** 3)
+        total += 13.0 * (4.0 * r * r * c + 2.0 * r ** 3)
     return total
 
 

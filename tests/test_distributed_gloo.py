@@ -13,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from sandmuon_b200.distributed import MatrixSharding, partition_matrices
-from sandmuon_b200.workloads import gpt_matrix_model, s8_executed_flops
+from sandmuon_b200.workloads import gpt_matrix_model, s8_dense_flops
 
 
 def test_unknown_exchange_is_rejected():
@@ -30,7 +30,7 @@ def test_lpt_partition_balances_s8_flops():
         owner = partition_matrices(shapes, world, "lpt")
         load = [0.0] * world
         for n, r in owner.items():
-            load[r] += s8_executed_flops([shapes[n]])
+            load[r] += s8_dense_flops([shapes[n]])
         assert set(owner) == set(shapes) and set(owner.values()) <= set(range(world))
         assert max(load) / (sum(load) / world) < 1.2
         by_layer = partition_matrices(shapes, world, "layer")

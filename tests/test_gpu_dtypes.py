@@ -102,7 +102,12 @@ def test_bf16_parameters_follow_reference_rounding():
         got = b1
         assert got.dtype == torch.bfloat16
         diff = (got.float() - want.float()).abs()
-        ulp = want.float().abs() * 2.0 ** -7 + 1e-30
-        assert bool((diff <= ulp).all())
-        assert float((diff == 0).float().mean()) > 0.95
+        # The update is rounded to BF16 in a different order (before or after
+        # the product with -lr, which is no power of two): the two updates
+        # differ by up to one BF16 step of the update, and the final roundings
+        # by one step of the result, so at most 2^-6 of the operands' scale.
+        step = (b0.abs() + LR * direction.abs()) * 2.0 ** -6 + 1e-30
+        worst = float((diff / step).max())
+        equal = float((diff == 0).float().mean())
+        assert worst <= 1.0 and equal > 0.95, (worst, equal)
     assert _lib.device_status(DEV) == 0

@@ -43,6 +43,26 @@ def test_column_stats_match_oracle(dtype, shape):
     assert rel(s1.cpu().numpy() + 0.25, want_s) < 1e-5
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,cols,stride", [(16384, 768, 768), (300, 512, 520), (200000, 32, 40),
+                                              (5, 100000, 100000), (16385, 776, 784), (2, 8, 8)])
+def test_column_stats_cluster_path(dtype, rows, cols, stride):
+    """Contiguous 16-byte-aligned rows below the TMA size take the one-launch
+    cluster reduction: padded row strides, a slab wider than the columns,
+    very tall and very wide inputs, odd row counts; twice in a row."""
+    g = torch.Generator().manual_seed(rows * 7 + cols)
+    base = (torch.randn(rows, stride, generator=g) * torch.exp(torch.randn(stride, generator=g) * .5) + .3).to(dtype)
+    x = base.to(DEV)[:, :cols]
+    sq = torch.zeros(cols, device=DEV)
+    s1 = torch.zeros(cols, device=DEV)
+    for _ in range(2):
+        engine.accumulate_column_stats(x, sq, s1)
+    want_sq, want_s = orc.column_stats(base[:, :cols].float().numpy(), True)
+    assert rel(sq.cpu().numpy(), 2 * want_sq) < 1e-5
+    assert rel(s1.cpu().numpy(), 2 * want_s) < 1e-5
+    assert _lib.device_status(DEV) == 0
+
+
 def test_column_stats_strided_and_transposed_views():
     base = torch.randn(300, 200, device=DEV)
     for view in (base[:, ::2], base.t(), base[10:250, 7:190]):

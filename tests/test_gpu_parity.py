@@ -286,3 +286,38 @@ def test_config4_layer_shapes_match_oracle(variant):
             opt.named_matrices[n].shape[0])
     assert _lib.device_status(DEV) == 0
     opt.close()
+
+
+@pytest.mark.parametrize("grad_scale", [1e-30, 1e-8, 1e6])
+def test_gradient_scale_range_follows_oracle(grad_scale):
+    """Three steps with gradients of magnitude 1e-4 * grad_scale.  The first
+    step's front end derives the stage-1 input scale from this step's norm,
+    later steps (one fused pass) reuse the previous step's; the S8 map is
+    scale invariant, so every step's direction must match the oracle's, which
+    normalises first (sandmuon/optimizer.py:77-78)."""
+    shapes = [(256, 384), (640, 256)]
+    model = nn.Sequential(*[nn.Linear(i, o, bias=False) for o, i in shapes]).to(DEV)
+    opt = RankOneAWeightedPE(model, lr=1e-2)
+    names = list(opt.named_matrices)
+    oracle = orc.OracleSandMuon({n: tuple(p.shape) for n, p in opt.named_matrices.items()}, {n: n for n in names},
+                                rank_one_a=True, lr=1e-2)
+    from sandmuon_b200.workloads import synth_gpt_statistics
+    rng = np.random.default_rng(77)
+    weights = {n: npy(p) for n, p in opt.named_matrices.items()}
+    for step in range(3):
+        stats = synth_gpt_statistics(opt, rng, count=4096)
+        grads = {}
+        for n, p in opt.named_matrices.items():
+            grads[n] = (rng.standard_normal(tuple(p.shape)) * 1e-4 * grad_scale).astype(np.float32)
+            p.grad = torch.from_numpy(grads[n]).to(DEV)
+            oracle.inject(n, **stats[n])
+        before = {n: npy(p) for n, p in opt.named_matrices.items()}
+        ref_before = dict(weights)
+        oracle.step(weights, grads)
+        opt.step()
+        for n in names:
+            d_gpu = (before[n] - npy(opt.named_matrices[n])) / 1e-2
+            d_ref = (ref_before[n] - weights[n]) / 1e-2
+            assert rel(d_gpu, d_ref) < DIR_REL and cos(d_gpu, d_ref) > DIR_COS, (grad_scale, step, n)
+    assert _lib.device_status(DEV) == 0
+    opt.close()
