@@ -79,7 +79,7 @@ def parse_args():
 #   python bench.py --steps 2 --warmup 1 --profile && ncu --metrics
 #   gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #   --clock-control none --csv --log-file <out> python bench.py --steps 2 --warmup 1 --profile
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 331_695_849
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 330_109_116
 
 
 def peaks():
