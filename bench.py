@@ -280,7 +280,8 @@ def e2e_serial(opt, params, host_g, refill, steps, device):
 def e2e_pipelined(opt, params, host_g, refill, steps, device):
     """The same per-step bytes and calls, overlapped across steps the way a
     host-offloaded training loop would run them: step k+1's host-to-device
-    copy (gradients and statistic sums, copy-in stream) runs during step k's
+    copy (gradients from one pinned staging buffer, and the statistic sums,
+    copy-in stream) runs during step k's
     optimizer step (compute stream) and step k-1's device-to-host copy of the
     updated weights (copy-out stream).  Gradients land in two alternating
     device buffer sets (p.grad is re-pointed each step); the updated weights
@@ -290,6 +291,12 @@ def e2e_pipelined(opt, params, host_g, refill, steps, device):
     region; steady-state ms per step = (last event - first event) / steps."""
     from sandmuon_b200 import engine
     total = sum(p.numel() for p in params)
+    # the caller's gradients in one pinned staging buffer: one copy per step
+    host_flat = torch.empty(total, dtype=torch.float32).pin_memory()
+    off = 0
+    for hg in host_g:
+        host_flat[off:off + hg.numel()].copy_(hg.reshape(-1))
+        off += hg.numel()
     compute = torch.cuda.current_stream(device)
     copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     grad_flat = [torch.empty(total, dtype=torch.float32, device=device) for _ in range(2)]
@@ -321,8 +328,7 @@ def e2e_pipelined(opt, params, host_g, refill, steps, device):
         s = k % 2
         with torch.cuda.stream(copy_in):
             copy_in.wait_event(grads_free[s])
-            for g, hg in zip(grad_sets[s], host_g):
-                g.copy_(hg, non_blocking=True)
+            grad_flat[s].copy_(host_flat, non_blocking=True)
             stat_dev[s].copy_(stat_host, non_blocking=True)
             in_ready[s].record(copy_in)
         compute.wait_event(in_ready[s])
