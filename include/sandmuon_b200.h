@@ -227,8 +227,9 @@ typedef struct {
 } SmCopySpec;
 
 /* Copies every (src -> dst, bytes) of the list in one kernel launch (the
- * scatter of all-gathered weights back into the parameters of a sharded
- * step; no counterpart in the single-device reference). */
+ * packing copies of a sharded step: gradients into the reduce-scatter's
+ * buffer, momenta into the consolidation gather; no counterpart in the
+ * single-device reference). */
 int sm_copy_multi(const SmCopySpec* copies, int32_t count, void* stream);
 
 /* One weight and the BF16 update delta to subtract from it. */

@@ -10,8 +10,10 @@ its own microbatches; at step():
      the matrices it owns (partition "lpt": longest-processing-time greedy
      over S8 FLOPs; "layer": contiguous transformer layers per rank);
   3. exchange: the owners' updated FP32 weights are all-gathered with one
-     padded all_gather_into_tensor and copied back into every rank's params
-     (exchange="weights", the default).  exchange="bf16_delta" gathers the
+     padded, in-place all_gather_into_tensor: the selected matrices live in
+     one flat buffer laid out as the gather's output, so nothing is copied
+     before or after it (exchange="weights", the default).
+     exchange="bf16_delta" gathers the
      update deltas lr * direction rounded to BF16 instead (half the NVLink
      bytes); every rank, the owner included, subtracts the same rounded delta,
      so the ranks stay bitwise identical.  The rounding (2^-9 relative per
@@ -71,9 +73,10 @@ def _copy_pairs(pairs, device) -> None:
 
 class MatrixSharding:
     """copy_fn(pairs, device) performs the packing copies (dst, src) of the
-    gradient reduction and the momentum gather, and the scatter of gathered
-    weights in the exchange; the default is the library's multi-tensor copy
-    kernel."""
+    gradient reduction and the momentum gather; the default is the library's
+    multi-tensor copy kernel.  With exchange="weights" (and more than one
+    rank) the constructor moves the selected matrices' storage into the flat
+    all-gather buffer (_rehome_weights)."""
 
     def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights", copy_fn=None):
         if exchange not in EXCHANGES:
@@ -90,6 +93,9 @@ class MatrixSharding:
         self.owner_by_name = partition_matrices(shapes, self.world, partition)
         self._owner = {id(opt.named_matrices[n]): r for n, r in self.owner_by_name.items()}
         self._gather = None
+        self._flat_weights = None
+        if exchange == "weights" and self.world > 1:
+            self._rehome_weights()
 
     def owns(self, parameter) -> bool:
         return self._owner[id(parameter)] == self.rank
@@ -215,24 +221,58 @@ class MatrixSharding:
         return out
 
     # --------------------------------------------------------- weights
+    def _rehome_weights(self):
+        """exchange="weights": every selected matrix becomes a view of one flat
+        FP32 buffer laid out as the all-gather's output (each owner's matrices
+        back to back in its shard, shards padded to the largest), so the
+        update kernel writes owned weights straight into the gathered layout
+        and the all-gather runs in place: no export copy of the owned weights
+        and no scatter of the received ones.  The parameters keep their
+        identity (only their storage moves); they must be contiguous float32.
+        A matrix not stepped this time travels as its current value."""
+        shard, offsets = self._slots()
+        params = list(self.opt.named_matrices.values())
+        for p in params:
+            if p.dtype != torch.float32 or not p.is_contiguous():
+                raise TypeError("a sharded sandmuon_b200 optimizer needs contiguous float32 matrix parameters; "
+                                f"got {p.dtype} {'contiguous' if p.is_contiguous() else 'strided'}")
+        flat = torch.zeros(shard * self.world, dtype=torch.float32, device=params[0].device)
+        with torch.no_grad():
+            for p in params:
+                r, off = offsets[id(p)]
+                view = flat[r * shard + off:r * shard + off + p.numel()].view_as(p)
+                view.copy_(p)
+                p.data = view
+        self._flat_weights = flat
+        self._homes = [(p, p.data_ptr()) for p in params]
+
     def _layout(self):
-        """Static all-gather layout: each rank's owned matrices back to back in
-        its send slot of `shard` elements (every selected matrix, every step)."""
+        """(send, recv, slots, unpack) of the all-gather.  Weights: send is this
+        rank's shard of the flat weight buffer and recv the whole buffer (an
+        in-place all-gather); slots are the owned parameters themselves and
+        nothing is unpacked.  BF16 deltas: each rank's owned matrices' deltas
+        back to back in its send slot of `shard` elements; unpack pairs every
+        other matrix with its gathered delta."""
         if self._gather is None:
             shard, offsets = self._slots()
             params = list(self.opt.named_matrices.values())
-            device = params[0].device
-            dtype = torch.bfloat16 if self.exchange_mode == "bf16_delta" else torch.float32
-            send = torch.zeros(shard, dtype=dtype, device=device)
-            recv = torch.empty(shard * self.world, dtype=dtype, device=device)
-            slots, unpack = {}, []
-            for p in params:
-                r, off = offsets[id(p)]
-                if r == self.rank:
-                    slots[id(p)] = send[off:off + p.numel()].view_as(p)
-                else:
-                    unpack.append((p, recv[r * shard + off:r * shard + off + p.numel()]))
-            self._gather = (send, recv, slots, unpack)
+            if self.exchange_mode == "weights":
+                flat = self._flat_weights
+                send = flat[self.rank * shard:(self.rank + 1) * shard]
+                slots = {id(p): p.detach() for p in params if self.owns(p)}
+                self._gather = (send, flat, slots, [])
+            else:
+                device = params[0].device
+                send = torch.zeros(shard, dtype=torch.bfloat16, device=device)
+                recv = torch.empty(shard * self.world, dtype=torch.bfloat16, device=device)
+                slots, unpack = {}, []
+                for p in params:
+                    r, off = offsets[id(p)]
+                    if r == self.rank:
+                        slots[id(p)] = send[off:off + p.numel()].view_as(p)
+                    else:
+                        unpack.append((p, recv[r * shard + off:r * shard + off + p.numel()]))
+                self._gather = (send, recv, slots, unpack)
         return self._gather
 
     @property
@@ -242,34 +282,33 @@ class MatrixSharding:
         return _lib.SM_EXPORT_BF16_DELTA if self.exchange_mode == "bf16_delta" else _lib.SM_EXPORT_WEIGHTS
 
     def send_slot(self, parameter) -> torch.Tensor | None:
-        """Where the step also writes an owned matrix's updated weight, or its
-        BF16 update delta (its all-gather send slot); None for a single rank."""
-        if self.world == 1:
+        """Where the step also writes an owned matrix's BF16 update delta (its
+        all-gather send slot); None for the weight exchange (the weights are
+        gathered in place) and for a single rank."""
+        if self.world == 1 or self.exchange_mode == "weights":
             return None
         return self._layout()[2][id(parameter)]
 
     def exchange(self, matrix_items) -> None:
-        """All-gathers the owners' send slots into all ranks and applies the
-        matrices stepped now.  The owners' send slots were filled by the update
-        kernel itself; the received weights are scattered back with one
-        multi-tensor copy launch, or the received BF16 deltas are subtracted
-        with one multi-tensor launch.
-
-        Only matrices in `matrix_items` (those with a gradient this step) are
-        unpacked: the slot of a matrix its owner did not step holds nothing
-        (zeros before its first step, an older value after), so copying it
-        would overwrite the other ranks' current weights.  The all-gather runs
-        on every rank whenever step() runs, whatever was stepped, so the ranks'
-        collectives stay paired; with data-parallel gradients every rank has
-        the same set of matrices with a gradient."""
+        """All-gathers the owners' updates into all ranks.  Weights: one
+        in-place all-gather of the flat weight buffer (the update kernel
+        already wrote the owned weights there).  BF16 deltas: the owners' send
+        slots were filled by the update kernel; the received deltas of the
+        matrices stepped now are subtracted with one multi-tensor launch (a
+        slot of a matrix its owner did not step holds an older delta).  The
+        all-gather runs on every rank whenever step() runs, whatever was
+        stepped, so the ranks' collectives stay paired."""
         if self.world == 1:
             return
         from .engine import apply_bf16_delta_multi
+        if self.exchange_mode == "weights":
+            for p, ptr in self._homes:
+                if p.data_ptr() != ptr:
+                    raise RuntimeError("a selected matrix's storage moved after the sharded optimizer was built "
+                                       "(for example model.to() or a reassigned .data); build the optimizer "
+                                       "after the model is in place")
         send, recv, slots, unpack = self._layout()
         dist.all_gather_into_tensor(recv, send, group=self.group)
-        stepped = {id(item[0]) for item in matrix_items}
-        pairs = [(p.detach(), src) for p, src in unpack if id(p) in stepped]
         if self.exchange_mode == "bf16_delta":
-            apply_bf16_delta_multi(pairs, recv.device)
-        else:
-            self._copy(pairs, recv.device)
+            stepped = {id(item[0]) for item in matrix_items}
+            apply_bf16_delta_multi([(p.detach(), src) for p, src in unpack if id(p) in stepped], recv.device)

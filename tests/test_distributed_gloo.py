@@ -99,16 +99,14 @@ def _worker(rank, world, port, partition, results, exchange="weights"):
             with torch.no_grad():
                 for i, (p, _, _) in enumerate(items):
                     p.fill_(100.0 * i + sharding.rank if sharding.owns(p) else -1.0)
-            # the update kernel writes owned weights into their send slots; here the
-            # test packs them, gathers over gloo and scatters like exchange() does
+            # the matrices live in the flat gather buffer: an owned slot is the
+            # parameter itself, and the in-place all-gather delivers the rest
+            assert not unpack and recv.data_ptr() <= send.data_ptr() < recv.data_ptr() + recv.numel() * 4
             for p, _, _ in items:
                 if sharding.owns(p):
-                    assert sharding.send_slot(p).data_ptr() == slots[id(p)].data_ptr()
-                    slots[id(p)].copy_(p.detach())
+                    assert sharding.send_slot(p) is None
+                    assert slots[id(p)].data_ptr() == p.data_ptr()
             dist.all_gather_into_tensor(recv, send, group=dist.group.WORLD)
-            with torch.no_grad():
-                for p, src in unpack:
-                    p.copy_(src.view_as(p))
         else:
             # every rank starts from the same weights; each owner subtracts its
             # BF16 delta (a value unique to matrix and owner) and exports it;
