@@ -517,6 +517,13 @@ struct Group {
   float *s = nullptr, *s_inv = nullptr, *gamma = nullptr;
   bool fused_ok = false;  // every matrix fits k_whiten_fused (rows in shared memory)
   int fused_blocks = 0;   // grid x of k_whiten_fused: the most row blocks of a matrix
+  // Untransposed matrices (d_out = r, d_in = c) on the row stream
+  // (k_whiten_rows) when rows_ok; the transposed ones then take
+  // k_whiten_fused alone, with grid x fused_blocks_t.
+  bool rows_ok = false;
+  int rows_count = 0, rows_threads = 0, rows_grid = 0, fused_blocks_t = 0;
+  int* rows_slots = nullptr;  // [rows_count] slots of the untransposed matrices
+  std::vector<int> host_rows_slots;
   float2 *rs_white = nullptr, *rs_map = nullptr;
   int* tmask = nullptr;  // [B] 1 = transposed matrix: its Q is stored in param layout
   unsigned *tk_white = nullptr, *tk_map = nullptr;  // [B] last-CTA tickets (zero between launches)
@@ -595,6 +602,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.rs_map = cv.take<float2>(static_cast<size_t>(g.batch) * g.dmax);
   g.tmask = cv.take<int>(g.batch);
   g.tk_white = cv.take<unsigned>(g.batch);
+  g.rows_slots = cv.take<int>(g.batch);
   g.tk_map = cv.take<unsigned>(g.batch);
 }
 
@@ -979,12 +987,61 @@ static int prepare_front_fused(bool rank1) {
   return SM_OK;
 }
 
-// One launch of the fused front end (k_whiten_fused) for group g.
+// SMB_FRONT_ROWS=0 keeps every matrix of a fused-eligible group on
+// k_whiten_fused (the untransposed row stream off).
+#ifndef SMB_FRONT_ROWS
+#define SMB_FRONT_ROWS 1
+#endif
+constexpr bool kFrontRows = SMB_FRONT_ROWS != 0;
+
+// Sizes the row stream of group g (k_whiten_rows): raises the kernel's
+// dynamic shared-memory limit once per device and instantiation, then takes
+// as many CTAs as fit on the device at once, at most one per row.  At plan
+// creation, outside any capture.
+static int prepare_front_rows(Group& g, int sms) {
+  static std::mutex mutex;
+  static bool done[2][64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  auto kern = g.rank1 ? k_whiten_rows<true> : k_whiten_rows<false>;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    if (!done[g.rank1][dev]) {
+      SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem_bytes(32 * 8 * kRowsKMax * 4)));
+      SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+      done[g.rank1][dev] = true;
+    }
+  }
+  int per_sm = 0;
+  SM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, g.rows_threads,
+                                                        static_cast<size_t>(rows_smem_bytes(g.c))));
+  if (per_sm < 1) {
+    g.rows_ok = false;
+    return SM_OK;
+  }
+  const int64_t rows = static_cast<int64_t>(g.rows_count) * g.r;
+  g.rows_grid = static_cast<int>(std::min<int64_t>(rows, static_cast<int64_t>(per_sm) * sms));
+  return SM_OK;
+}
+
+// One launch of the fused front end (k_whiten_fused) for group g: every
+// matrix, or only the transposed ones when the row stream takes the rest.
 static int launch_front_fused(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, cudaStream_t st) {
   auto kern = g.rank1 ? k_whiten_fused<true> : k_whiten_fused<false>;
-  dim3 grid(static_cast<unsigned>(g.fused_blocks), static_cast<unsigned>(g.batch));
+  const int transposed_only = g.rows_ok ? 1 : 0;
+  dim3 grid(static_cast<unsigned>(transposed_only ? g.fused_blocks_t : g.fused_blocks), static_cast<unsigned>(g.batch));
   return launch_kernel(kern, grid, dim3(256), static_cast<size_t>(kFusedSmemBytes), st, mats, mom_beta, mom_omb,
                        g.rs_white, g.dmax, g.pre, g.rho, g.rho2, g.tk_white, g.xh, g.xl,
+                       static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp), transposed_only);
+}
+
+// One launch of the untransposed row stream (k_whiten_rows) for group g.
+static int launch_front_rows(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, cudaStream_t st) {
+  auto kern = g.rank1 ? k_whiten_rows<true> : k_whiten_rows<false>;
+  return launch_kernel(kern, dim3(static_cast<unsigned>(g.rows_grid)), dim3(static_cast<unsigned>(g.rows_threads)),
+                       static_cast<size_t>(rows_smem_bytes(g.c)), st, mats, g.rows_slots, g.rows_count, g.r, g.c,
+                       mom_beta, mom_omb, g.rs_white, g.dmax, g.pre, g.rho, g.rho2, g.tk_white, g.xh, g.xl,
                        static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp));
 }
 
@@ -1000,6 +1057,11 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
   if (fused && vec4 && g.fused_ok) {
+    if (g.rows_ok) {
+      SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_rows(g, mats, mom_beta, mom_omb, st));
+      *launches += 1;
+      if (g.fused_blocks_t == 0) return SM_OK;
+    }
     SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_fused(g, mats, mom_beta, mom_omb, st));
     *launches += 1;
     return SM_OK;
@@ -1171,6 +1233,21 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     }
     groups[g].fused_ok = fused_ok;
     groups[g].fused_blocks = fused_blocks;
+    // row stream for the untransposed matrices (slot order), k_whiten_fused for the rest
+    groups[g].host_rows_slots.clear();
+    int fused_blocks_t = 0;
+    for (int i = 0; i < nm; ++i) {
+      if (mg[i] != static_cast<int>(g)) continue;
+      const SmMatrixSpec& m = spec->matrices[i];
+      if (m.d_out > m.d_in) fused_blocks_t = std::max(fused_blocks_t, static_cast<int>(cdiv(m.d_out, fused_rows(m.d_in))));
+    }
+    for (int i = 0; i < nm; ++i)  // slots rise with i within a group
+      if (mg[i] == static_cast<int>(g) && spec->matrices[i].d_out <= spec->matrices[i].d_in)
+        groups[g].host_rows_slots.push_back(slot[i]);
+    groups[g].rows_count = static_cast<int>(groups[g].host_rows_slots.size());
+    groups[g].fused_blocks_t = fused_blocks_t;
+    groups[g].rows_ok = kFrontRows && fused_ok && groups[g].rows_count > 0 && rows_stream_fits(groups[g].c);
+    groups[g].rows_threads = 32 * rows_team_warps(groups[g].c);
   }
   choose_tilings(groups, di->sms, pairs);
   MatDev* d_mats = cv.take<MatDev>(nm);
@@ -1749,6 +1826,11 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
       if (rc != SM_OK) break;
       rc = encode_group_maps(g);
       if (rc == SM_OK && g.fused_ok) rc = prepare_front_fused(g.rank1);
+      if (rc == SM_OK && g.rows_ok) {
+        DeviceInfo* di = nullptr;
+        rc = current_device_info(&di);
+        if (rc == SM_OK) rc = prepare_front_rows(g, di->sms);
+      }
     }
     for (size_t gi = 0; gi < p->groups.size() && rc == SM_OK; ++gi) {
       Group& g = p->groups[gi];
@@ -1759,6 +1841,11 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
       e = cudaMemcpyAsync(g.tmask, g.host_tmask.data(), g.batch * sizeof(int), cudaMemcpyHostToDevice,
                           static_cast<cudaStream_t>(stream));
       if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("tmask upload: ") + cudaGetErrorString(e));
+      if (rc == SM_OK && g.rows_count > 0) {
+        e = cudaMemcpyAsync(g.rows_slots, g.host_rows_slots.data(), g.rows_count * sizeof(int),
+                            cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("row slot upload: ") + cudaGetErrorString(e));
+      }
     }
     for (int kind = 0; kind < 3 && rc == SM_OK; ++kind) {
       for (const LaunchSet& set : p->s8.sets[kind]) {

@@ -927,7 +927,7 @@ __global__ void __launch_bounds__(256)
     k_whiten_fused(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs, int ld_rs,
                    float* __restrict__ pre, float* __restrict__ rho, float* __restrict__ rho2,
                    unsigned* __restrict__ tickets, __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl,
-                   int64_t rp, int64_t cp) {
+                   int64_t rp, int64_t cp, int transposed_only) {
   extern __shared__ __align__(128) uint8_t fused_smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ FrontSeg s_seg[8];
@@ -940,7 +940,9 @@ __global__ void __launch_bounds__(256)
   const MatDev md = mats[b];
   const int R = fused_rows(md.d_in);
   const int o0 = blockIdx.x * R;
-  if (o0 >= md.d_out) return;  // whole CTA: it takes no part in the matrix's ticket
+  // whole CTA: it takes no part in the matrix's ticket (with transposed_only,
+  // k_whiten_rows handles the untransposed matrices)
+  if (o0 >= md.d_out || (transposed_only && !md.transposed)) return;
   const int rows = min(R, md.d_out - o0);
   const int n = md.d_in;
   const int n4 = n / 4;
@@ -1121,6 +1123,232 @@ __global__ void __launch_bounds__(256)
       const double placed = norm * scale;
       if (norm > 0.0 && !(placed > 0x1p-60 && placed < 0x1p60)) atomicExch(&g_status, kStatusFrontRange);
       pre[b] = plane_scale_for(norm);
+    }
+  }
+}
+
+// ===================================== N3 in one pass: untransposed row stream
+// The matrices of a group whose param rows are X rows (d_out <= d_in) all
+// have the group's shape r x n (n = d_in).  Their r * count rows form one
+// stream; CTA c of the persistent grid takes the contiguous range
+// [c * total / grid, (c+1) * total / grid) of it.  A CTA is one team of
+// TW = rows_team_warps(n) warps, so every thread holds at most kRowsKMax
+// float4 of a row: thread t owns the float4 columns t, t + 32 TW, ...  and
+// keeps the matrix's inv_a (and z_a) for them in registers.  Rows arrive in
+// a ring of kRowsStages shared-memory buffers (g row, m row) by bulk async
+// copies (cp.async.bulk, no multicast) that thread 0 issues kRowsStages - 1
+// rows ahead; each buffer completes on its own mbarrier (a bounded wait).
+// Per row: (y . z_a, |y|) from registers-held columns (FP64 squares), then m'
+// and the hi/lo planes of x = v * pre[b] at X[o, :] -- the same arithmetic
+// as k_whiten_fused.  No CTA-wide phase separates loading from writing, so
+// copies stay in flight while a row is written.  A matrix's ticket counts
+// rows: a CTA adds its row count once per matrix segment it covers, and the
+// CTA that completes the count reduces the row norms into the stage-1 alphas
+// and the next plane scale.
+constexpr int kRowsKMax = 8;     // float4 per thread per row
+constexpr int kRowsStages = 3;   // row buffers per CTA
+
+__host__ __device__ constexpr int rows_team_warps(int n) {
+  int tw = 1;
+  while (tw < 8 && n / 4 > 32 * tw * kRowsKMax) tw <<= 1;
+  return tw;
+}
+// n that the row stream takes: float4 rows of at most 32 * 8 * kRowsKMax float4
+__host__ __device__ constexpr bool rows_stream_fits(int n) { return n % 4 == 0 && n > 0 && n / 4 <= 32 * 8 * kRowsKMax; }
+__host__ __device__ constexpr int rows_smem_bytes(int n) { return kRowsStages * 2 * n * 4; }
+
+template <bool RANK1>
+__global__ void __launch_bounds__(256)
+    k_whiten_rows(const MatDev* __restrict__ mats, const int* __restrict__ slots, int count, int r, int n,
+                  float mom_beta, float omb, float2* __restrict__ rs, int ld_rs, float* __restrict__ pre,
+                  float* __restrict__ rho, float* __restrict__ rho2, unsigned* __restrict__ tickets,
+                  __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl, int64_t rp, int64_t cp) {
+  extern __shared__ __align__(128) uint8_t rows_smem[];
+  __shared__ __align__(8) uint64_t full[kRowsStages];
+  __shared__ FrontSeg s_part[2][8];
+  __shared__ double sh[8];
+  __shared__ unsigned s_last;
+  __shared__ int s_abort;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int T = blockDim.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, TW = T >> 5;
+  const int64_t total = static_cast<int64_t>(count) * r;
+  const int64_t j0 = total * blockIdx.x / gridDim.x, j1 = total * (blockIdx.x + 1) / gridDim.x;
+  const int rows = static_cast<int>(j1 - j0);
+  if (rows <= 0) return;
+  const int n4 = n / 4;
+  const uint32_t row_bytes = static_cast<uint32_t>(n) * 4u;
+  float* ring = reinterpret_cast<float*>(rows_smem);  // buffer s: g at ring + 2 n s, m after it
+
+  // thread 0: bulk copies of stream row q (0-based in this CTA's range) into buffer q % S
+  auto issue = [&](int q) {
+    const int64_t j = j0 + q;
+    const int k = static_cast<int>(j / r), o = static_cast<int>(j - static_cast<int64_t>(k) * r);
+    const MatDev& m = mats[slots[k]];
+    const int s = q % kRowsStages;
+    const uint32_t bar = smem_u32(&full[s]);
+    float* dst = ring + static_cast<size_t>(2 * s) * n;
+    mbar_arrive_expect_tx(bar, 2u * row_bytes);
+    bulk_load(smem_u32(dst), m.grad + static_cast<int64_t>(o) * n, row_bytes, bar);
+    bulk_load(smem_u32(dst + n), m.mom + static_cast<int64_t>(o) * n, row_bytes, bar);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kRowsStages; ++s) mbar_init(smem_u32(&full[s]), 1);
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int issued = min(kRowsStages, rows);
+  if (tid == 0)
+    for (int q = 0; q < issued; ++q) issue(q);
+
+  float4 a_reg[kRowsKMax], z_reg[kRowsKMax];
+  int cur_k = -1, b = 0, seg = 0;
+  float scale = 1.0f, coef = 0.0f;
+  const float* inv_b = nullptr;
+  float* mom = nullptr;
+  float2* rsb = nullptr;
+  int64_t plane = 0;
+  bool alive = true;
+  int q_fail = rows;  // first row whose copies did not arrive
+
+  // closes this CTA's segment of matrix b: its rows join the matrix's ticket
+  auto close_segment = [&]() {
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const unsigned t = atomicAdd(tickets + b, static_cast<unsigned>(seg));
+      s_last = (t + static_cast<unsigned>(seg) == static_cast<unsigned>(r)) ? 1u : 0u;
+      if (s_last) {
+        __threadfence();
+        tickets[b] = 0u;
+      }
+    }
+    __syncthreads();
+    if (s_last) {
+      const double t = rows_sum_sq_y(rsb, r, sh);
+      if (tid == 0) {
+        const double norm = sqrt(t);
+        set_stage1_alphas(norm, scale, rho, rho2, b);
+        const double placed = norm * scale;
+        if (norm > 0.0 && !(placed > 0x1p-60 && placed < 0x1p60)) atomicExch(&g_status, kStatusFrontRange);
+        pre[b] = plane_scale_for(norm);
+      }
+      __syncthreads();
+    }
+  };
+
+  for (int q = 0; q < rows; ++q) {
+    const int64_t j = j0 + q;
+    const int k = static_cast<int>(j / r), o = static_cast<int>(j - static_cast<int64_t>(k) * r);
+    if (k != cur_k) {
+      if (cur_k >= 0) close_segment();
+      cur_k = k;
+      b = slots[k];
+      const MatDev& m = mats[b];
+      inv_b = m.inv_b;
+      mom = m.mom;
+      coef = RANK1 ? m.scal_a[0] : 0.0f;
+      scale = pre[b];
+      rsb = rs + static_cast<int64_t>(b) * ld_rs;
+      plane = static_cast<int64_t>(b) * rp * cp;
+      seg = 0;
+#pragma unroll
+      for (int kk = 0; kk < kRowsKMax; ++kk) {
+        const int i4 = tid + kk * T;
+        a_reg[kk] = i4 < n4 ? reinterpret_cast<const float4*>(m.inv_a)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        z_reg[kk] = (RANK1 && i4 < n4) ? reinterpret_cast<const float4*>(m.z_a)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    ++seg;
+    const int s = q % kRowsStages;
+    bool ok = alive && mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((q / kRowsStages) & 1), &s_abort,
+                                 kStatusTimeoutFrontLoad);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) {
+      if (alive) q_fail = q;
+      alive = false;
+      continue;
+    }
+    // every thread is past row q - 1: its buffer takes the next row
+    if (tid == 0 && q >= 1 && issued < rows) issue(issued++);
+    const float4* g4 = reinterpret_cast<const float4*>(ring + static_cast<size_t>(2 * s) * n);
+    const float4* m4 = g4 + n4;
+    const float ib = inv_b[o];
+
+    // row statistics
+    float dot = 0.0f;
+    double sq = 0.0;
+#pragma unroll
+    for (int kk = 0; kk < kRowsKMax; ++kk) {
+      const int i4 = tid + kk * T;
+      if (i4 < n4) {
+        const float4 gv = g4[i4], mv = m4[i4];
+        const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float ae[4] = {a_reg[kk].x, a_reg[kk].y, a_reg[kk].z, a_reg[kk].w};
+        const float ze[4] = {z_reg[kk].x, z_reg[kk].y, z_reg[kk].z, z_reg[kk].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mn = mom_beta * me[e] + omb * ge[e];
+          const float src = mom_beta * mn + omb * ge[e];
+          const float y = (src * ib) * ae[e];
+          sq += static_cast<double>(y) * y;
+          if (RANK1) dot += y * ze[e];
+        }
+      }
+    }
+    sq = warp_sum_d(sq);
+    dot = RANK1 ? warp_sum(dot) : 0.0f;
+    if (TW > 1) {
+      if (lane == 0) {
+        s_part[q & 1][warp].dot = dot;
+        s_part[q & 1][warp].sq = sq;
+      }
+      __syncthreads();
+      dot = 0.0f;
+      sq = 0.0;
+      for (int w = 0; w < TW; ++w) {
+        dot += s_part[q & 1][w].dot;
+        sq += s_part[q & 1][w].sq;
+      }
+    }
+    if (tid == 0) rsb[o] = make_float2(dot, static_cast<float>(sqrt(sq)));
+
+    // momentum and planes
+    const float cw = coef * dot;
+    float* mrow = mom + static_cast<int64_t>(o) * n;
+    const int64_t xrow = plane + static_cast<int64_t>(o) * cp;
+#pragma unroll
+    for (int kk = 0; kk < kRowsKMax; ++kk) {
+      const int i4 = tid + kk * T;
+      if (i4 < n4) {
+        const float4 gv = g4[i4], mv = m4[i4];
+        const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float ae[4] = {a_reg[kk].x, a_reg[kk].y, a_reg[kk].z, a_reg[kk].w};
+        const float ze[4] = {z_reg[kk].x, z_reg[kk].y, z_reg[kk].z, z_reg[kk].w};
+        float mn[4], h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          mn[e] = mom_beta * me[e] + omb * ge[e];
+          const float src = mom_beta * mn[e] + omb * ge[e];
+          float v = (src * ib) * ae[e];
+          if (RANK1) v += cw * ze[e];
+          split_hilo(v * scale, h[e], l[e]);
+        }
+        reinterpret_cast<float4*>(mrow)[i4] = make_float4(mn[0], mn[1], mn[2], mn[3]);
+        const int64_t xo = xrow + 4 * i4;
+        *reinterpret_cast<uint2*>(xh + xo) = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+        *reinterpret_cast<uint2*>(xl + xo) = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+      }
+    }
+  }
+  close_segment();
+  if (!alive && tid == 0) {
+    // the copies still in flight land (bounded) before this CTA's shared memory goes
+    for (int q = q_fail; q < issued; ++q) {
+      const int s = q % kRowsStages;
+      mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((q / kRowsStages) & 1), nullptr, kStatusTimeoutFrontLoad);
     }
   }
 }
