@@ -521,9 +521,15 @@ struct Group {
   // (k_whiten_rows) when rows_ok; the transposed ones then take
   // k_whiten_fused alone, with grid x fused_blocks_t.
   bool rows_ok = false;
-  int rows_count = 0, rows_threads = 0, rows_grid = 0, fused_blocks_t = 0;
+  int rows_count = 0, rows_threads = 0, rows_grid = 0, fused_blocks_t = 0, fused_blocks_u = 0;
   int* rows_slots = nullptr;  // [rows_count] slots of the untransposed matrices
   std::vector<int> host_rows_slots;
+  // Transposed matrices (d_out = c, d_in = r) on the block stream
+  // (k_whiten_cols) when cols_ok.
+  bool cols_ok = false;
+  int cols_count = 0, cols_threads = 0, cols_grid = 0;
+  int* cols_slots = nullptr;  // [cols_count] slots of the transposed matrices
+  std::vector<int> host_cols_slots;
   float2 *rs_white = nullptr, *rs_map = nullptr;
   int* tmask = nullptr;  // [B] 1 = transposed matrix: its Q is stored in param layout
   unsigned *tk_white = nullptr, *tk_map = nullptr;  // [B] last-CTA tickets (zero between launches)
@@ -603,6 +609,7 @@ static void carve_group(Carver& cv, Group& g) {
   g.tmask = cv.take<int>(g.batch);
   g.tk_white = cv.take<unsigned>(g.batch);
   g.rows_slots = cv.take<int>(g.batch);
+  g.cols_slots = cv.take<int>(g.batch);
   g.tk_map = cv.take<unsigned>(g.batch);
 }
 
@@ -993,6 +1000,11 @@ static int prepare_front_fused(bool rank1) {
 #define SMB_FRONT_ROWS 1
 #endif
 constexpr bool kFrontRows = SMB_FRONT_ROWS != 0;
+// SMB_FRONT_COLS=0 keeps the transposed matrices on k_whiten_fused.
+#ifndef SMB_FRONT_COLS
+#define SMB_FRONT_COLS 1
+#endif
+constexpr bool kFrontCols = SMB_FRONT_COLS != 0;
 
 // Sizes the row stream of group g (k_whiten_rows): raises the kernel's
 // dynamic shared-memory limit once per device and instantiation, then takes
@@ -1025,15 +1037,54 @@ static int prepare_front_rows(Group& g, int sms) {
   return SM_OK;
 }
 
+// Sizes the block stream of group g (k_whiten_cols): one CTA per SM, at
+// most one per block.  At plan creation, outside any capture.
+static int prepare_front_cols(Group& g, int sms) {
+  static std::mutex mutex;
+  static bool done[2][64] = {};
+  int dev = 0;
+  SM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SM_ERR_UNSUPPORTED, "device ordinal out of range");
+  auto kern = g.rank1 ? k_whiten_cols<true> : k_whiten_cols<false>;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    if (!done[g.rank1][dev]) {
+      SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 196608));
+      SM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+      done[g.rank1][dev] = true;
+    }
+  }
+  int per_sm = 0;
+  SM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, g.cols_threads,
+                                                        static_cast<size_t>(cols_smem_bytes(g.r))));
+  if (per_sm < 1) {
+    g.cols_ok = false;
+    return SM_OK;
+  }
+  const int64_t blocks = static_cast<int64_t>(g.cols_count) * cdiv(g.c, kColsRows);
+  g.cols_grid = static_cast<int>(std::min<int64_t>(blocks, static_cast<int64_t>(per_sm) * sms));
+  return SM_OK;
+}
+
 // One launch of the fused front end (k_whiten_fused) for group g: every
-// matrix, or only the transposed ones when the row stream takes the rest.
-static int launch_front_fused(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, cudaStream_t st) {
+// matrix, or those of one orientation when a stream takes the other.
+static int launch_front_fused(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, int which,
+                              cudaStream_t st) {
   auto kern = g.rank1 ? k_whiten_fused<true> : k_whiten_fused<false>;
-  const int transposed_only = g.rows_ok ? 1 : 0;
-  dim3 grid(static_cast<unsigned>(transposed_only ? g.fused_blocks_t : g.fused_blocks), static_cast<unsigned>(g.batch));
+  const int gx = which == 1 ? g.fused_blocks_t : which == 2 ? g.fused_blocks_u : g.fused_blocks;
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(g.batch));
   return launch_kernel(kern, grid, dim3(256), static_cast<size_t>(kFusedSmemBytes), st, mats, mom_beta, mom_omb,
                        g.rs_white, g.dmax, g.pre, g.rho, g.rho2, g.tk_white, g.xh, g.xl,
-                       static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp), transposed_only);
+                       static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp), which);
+}
+
+// One launch of the transposed block stream (k_whiten_cols) for group g.
+static int launch_front_cols(const Group& g, const MatDev* mats, float mom_beta, float mom_omb, cudaStream_t st) {
+  auto kern = g.rank1 ? k_whiten_cols<true> : k_whiten_cols<false>;
+  return launch_kernel(kern, dim3(static_cast<unsigned>(g.cols_grid)), dim3(static_cast<unsigned>(g.cols_threads)),
+                       static_cast<size_t>(cols_smem_bytes(g.r)), st, mats, g.cols_slots, g.cols_count, g.c, g.r,
+                       mom_beta, mom_omb, g.rs_white, g.dmax, g.pre, g.rho, g.rho2, g.tk_white, g.xh, g.xl,
+                       static_cast<int64_t>(g.rp), static_cast<int64_t>(g.cp));
 }
 
 // One launch of the untransposed row stream (k_whiten_rows) for group g.
@@ -1057,13 +1108,22 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
   if (fused && vec4 && g.fused_ok) {
+    // untransposed matrices: row stream; transposed: block stream; what
+    // neither takes goes through k_whiten_fused
     if (g.rows_ok) {
       SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_rows(g, mats, mom_beta, mom_omb, st));
       *launches += 1;
-      if (g.fused_blocks_t == 0) return SM_OK;
     }
-    SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_fused(g, mats, mom_beta, mom_omb, st));
-    *launches += 1;
+    if (g.cols_ok) {
+      SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_cols(g, mats, mom_beta, mom_omb, st));
+      *launches += 1;
+    }
+    const bool rest_u = g.rows_count > 0 && !g.rows_ok, rest_t = g.cols_count > 0 && !g.cols_ok;
+    if (rest_u || rest_t) {
+      const int which = rest_u && rest_t ? 0 : rest_t ? 1 : 2;
+      SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, launch_front_fused(g, mats, mom_beta, mom_omb, which, st));
+      *launches += 1;
+    }
     return SM_OK;
   }
   SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
@@ -1235,19 +1295,28 @@ static int plan_layout(const SmPlanSpec* spec, void* ws, SmPlan* plan, size_t* b
     groups[g].fused_blocks = fused_blocks;
     // row stream for the untransposed matrices (slot order), k_whiten_fused for the rest
     groups[g].host_rows_slots.clear();
-    int fused_blocks_t = 0;
-    for (int i = 0; i < nm; ++i) {
+    groups[g].host_cols_slots.clear();
+    int fused_blocks_t = 0, fused_blocks_u = 0;
+    for (int i = 0; i < nm; ++i) {  // slots rise with i within a group
       if (mg[i] != static_cast<int>(g)) continue;
       const SmMatrixSpec& m = spec->matrices[i];
-      if (m.d_out > m.d_in) fused_blocks_t = std::max(fused_blocks_t, static_cast<int>(cdiv(m.d_out, fused_rows(m.d_in))));
-    }
-    for (int i = 0; i < nm; ++i)  // slots rise with i within a group
-      if (mg[i] == static_cast<int>(g) && spec->matrices[i].d_out <= spec->matrices[i].d_in)
+      const int nblk = static_cast<int>(cdiv(m.d_out, std::max(1, fused_rows(m.d_in))));
+      if (m.d_out > m.d_in) {
+        fused_blocks_t = std::max(fused_blocks_t, nblk);
+        groups[g].host_cols_slots.push_back(slot[i]);
+      } else {
+        fused_blocks_u = std::max(fused_blocks_u, nblk);
         groups[g].host_rows_slots.push_back(slot[i]);
+      }
+    }
     groups[g].rows_count = static_cast<int>(groups[g].host_rows_slots.size());
+    groups[g].cols_count = static_cast<int>(groups[g].host_cols_slots.size());
     groups[g].fused_blocks_t = fused_blocks_t;
+    groups[g].fused_blocks_u = fused_blocks_u;
     groups[g].rows_ok = kFrontRows && fused_ok && groups[g].rows_count > 0 && rows_stream_fits(groups[g].c);
     groups[g].rows_threads = 32 * rows_team_warps(groups[g].c);
+    groups[g].cols_ok = kFrontCols && fused_ok && groups[g].cols_count > 0 && cols_stream_fits(groups[g].r);
+    groups[g].cols_threads = cols_threads(groups[g].r);
   }
   choose_tilings(groups, di->sms, pairs);
   MatDev* d_mats = cv.take<MatDev>(nm);
@@ -1831,6 +1900,11 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
         rc = current_device_info(&di);
         if (rc == SM_OK) rc = prepare_front_rows(g, di->sms);
       }
+      if (rc == SM_OK && g.cols_ok) {
+        DeviceInfo* di = nullptr;
+        rc = current_device_info(&di);
+        if (rc == SM_OK) rc = prepare_front_cols(g, di->sms);
+      }
     }
     for (size_t gi = 0; gi < p->groups.size() && rc == SM_OK; ++gi) {
       Group& g = p->groups[gi];
@@ -1845,6 +1919,11 @@ int sm_plan_create(const SmPlanSpec* spec, void* workspace, size_t workspace_byt
         e = cudaMemcpyAsync(g.rows_slots, g.host_rows_slots.data(), g.rows_count * sizeof(int),
                             cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
         if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("row slot upload: ") + cudaGetErrorString(e));
+      }
+      if (rc == SM_OK && g.cols_count > 0) {
+        e = cudaMemcpyAsync(g.cols_slots, g.host_cols_slots.data(), g.cols_count * sizeof(int),
+                            cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) rc = fail(SM_ERR_CUDA, std::string("block slot upload: ") + cudaGetErrorString(e));
       }
     }
     for (int kind = 0; kind < 3 && rc == SM_OK; ++kind) {

@@ -927,7 +927,7 @@ __global__ void __launch_bounds__(256)
     k_whiten_fused(const MatDev* __restrict__ mats, float mom_beta, float omb, float2* __restrict__ rs, int ld_rs,
                    float* __restrict__ pre, float* __restrict__ rho, float* __restrict__ rho2,
                    unsigned* __restrict__ tickets, __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl,
-                   int64_t rp, int64_t cp, int transposed_only) {
+                   int64_t rp, int64_t cp, int which) {
   extern __shared__ __align__(128) uint8_t fused_smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ FrontSeg s_seg[8];
@@ -940,9 +940,10 @@ __global__ void __launch_bounds__(256)
   const MatDev md = mats[b];
   const int R = fused_rows(md.d_in);
   const int o0 = blockIdx.x * R;
-  // whole CTA: it takes no part in the matrix's ticket (with transposed_only,
-  // k_whiten_rows handles the untransposed matrices)
-  if (o0 >= md.d_out || (transposed_only && !md.transposed)) return;
+  // whole CTA: it takes no part in the matrix's ticket.  which: 0 every
+  // matrix, 1 only transposed ones, 2 only untransposed ones (the streams
+  // k_whiten_rows / k_whiten_cols take the others)
+  if (o0 >= md.d_out || (which == 1 && !md.transposed) || (which == 2 && md.transposed)) return;
   const int rows = min(R, md.d_out - o0);
   const int n = md.d_in;
   const int n4 = n / 4;
@@ -1349,6 +1350,280 @@ __global__ void __launch_bounds__(256)
     for (int q = q_fail; q < issued; ++q) {
       const int s = q % kRowsStages;
       mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((q / kRowsStages) & 1), nullptr, kStatusTimeoutFrontLoad);
+    }
+  }
+}
+
+// ===================================== N3 in one pass: transposed block stream
+// The transposed matrices of a group (d_out = c > d_in = n = r) have param
+// rows that are X columns.  Their 16-row blocks form one stream; CTA c of the
+// persistent grid (one CTA per SM) takes a contiguous range of blocks.  A
+// block's g rows and m rows are contiguous in memory: one bulk async copy
+// each (cp.async.bulk, no multicast) into a 2-stage ring, thread 0 issuing
+// the next block while the current one is processed (bounded mbarrier waits).
+// Thread = (4 consecutive X rows i..i+3, part p of kColsParts row parts of
+// 16 / kColsParts param rows): the 32 / kColsParts lanes of a part take
+// consecutive float4 columns, so the 16-byte shared loads are conflict-free,
+// and the parts of a warp together write whole 32-byte sectors of their X
+// rows (16 bf16: the block's 16 param rows).  One thread per item, so a
+// thread keeps its columns' inv_a (and z_a) in registers for the whole
+// matrix and its rows' inv_b for the block.
+//   1. per param row: (y . z_a, |y|^2) partial sums over the thread's
+//      columns, reduced over the lanes of a part (shuffles), then over the
+//      warps in warp order (shared memory): deterministic;
+//   2. m' and the hi/lo planes of x = v * pre[b], as k_whiten_fused.
+// A matrix's ticket counts blocks: a CTA adds its block count once per
+// matrix segment; the CTA that completes the count reduces the row norms.
+#ifndef SMB_COLS_PARTS
+#define SMB_COLS_PARTS 4
+#endif
+constexpr int kColsRows = 16;   // param rows per block
+constexpr int kColsStages = 2;
+constexpr int kColsParts = SMB_COLS_PARTS;       // 2 or 4
+constexpr int kColsPartRows = kColsRows / kColsParts;
+constexpr int kColsLanes = 32 / kColsParts;     // lanes per part
+static_assert(kColsParts == 2 || kColsParts == 4, "2 or 4 row parts");
+// 4 parts: up to 24 warps of at most 80 registers; 2 parts: 16 of at most 128
+constexpr int kColsMaxThreads = kColsParts == 4 ? 768 : 512;
+
+__host__ __device__ constexpr int cols_smem_bytes(int n) { return kColsStages * 2 * kColsRows * n * 4; }
+// items (= threads): the float4 columns rounded up to whole parts, times the parts
+__host__ __device__ constexpr int cols_threads(int n) { return ((n / 4 + kColsLanes - 1) / kColsLanes) * 32; }
+__host__ __device__ constexpr bool cols_stream_fits(int n) {
+  return n % 4 == 0 && n > 0 && cols_smem_bytes(n) <= 196608 && cols_threads(n) <= kColsMaxThreads;
+}
+
+template <bool RANK1>
+__global__ void __launch_bounds__(kColsMaxThreads, 1)
+    k_whiten_cols(const MatDev* __restrict__ mats, const int* __restrict__ slots, int count, int c, int n,
+                  float mom_beta, float omb, float2* __restrict__ rs, int ld_rs, float* __restrict__ pre,
+                  float* __restrict__ rho, float* __restrict__ rho2, unsigned* __restrict__ tickets,
+                  __nv_bfloat16* __restrict__ xh, __nv_bfloat16* __restrict__ xl, int64_t rp, int64_t cp) {
+  extern __shared__ __align__(128) uint8_t cols_smem[];
+  __shared__ __align__(8) uint64_t full[kColsStages];
+  __shared__ float s_pdot[32][kColsRows];   // [warp][row] partials
+  __shared__ double s_psq[32][kColsRows];
+  __shared__ float s_dot[kColsRows];
+  __shared__ double sh[32];
+  __shared__ unsigned s_last;
+  __shared__ int s_abort;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, NW = blockDim.x >> 5;
+  const int nb = (c + kColsRows - 1) / kColsRows;  // blocks per matrix
+  const int64_t total = static_cast<int64_t>(count) * nb;
+  const int64_t j0 = total * blockIdx.x / gridDim.x, j1 = total * (blockIdx.x + 1) / gridDim.x;
+  const int blocks = static_cast<int>(j1 - j0);
+  if (blocks <= 0) return;
+  const int n4 = n / 4;
+  float* ring = reinterpret_cast<float*>(cols_smem);  // stage s: g rows at ring + 2 R n s, m rows after
+  const int part = lane / kColsLanes;
+  const int i4 = warp * kColsLanes + (lane % kColsLanes);  // this thread's float4 column
+  const bool has = i4 < n4;
+  const int r0 = part * kColsPartRows;                     // its first row of a block
+
+  auto issue = [&](int q) {
+    const int64_t j = j0 + q;
+    const int k = static_cast<int>(j / nb), blk = static_cast<int>(j - static_cast<int64_t>(k) * nb);
+    const int o0 = blk * kColsRows, rows = min(kColsRows, c - o0);
+    const MatDev& m = mats[slots[k]];
+    const int s = q % kColsStages;
+    const uint32_t bar = smem_u32(&full[s]);
+    float* dst = ring + static_cast<size_t>(2 * s) * kColsRows * n;
+    const uint32_t bytes = static_cast<uint32_t>(rows) * static_cast<uint32_t>(n) * 4u;
+    mbar_arrive_expect_tx(bar, 2u * bytes);
+    bulk_load(smem_u32(dst), m.grad + static_cast<int64_t>(o0) * n, bytes, bar);
+    bulk_load(smem_u32(dst + kColsRows * n), m.mom + static_cast<int64_t>(o0) * n, bytes, bar);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kColsStages; ++s) mbar_init(smem_u32(&full[s]), 1);
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int issued = min(kColsStages, blocks);
+  if (tid == 0)
+    for (int q = 0; q < issued; ++q) issue(q);
+
+  int cur_k = -1, b = 0, seg = 0;
+  float scale = 1.0f, coef = 0.0f;
+  const MatDev* md = nullptr;
+  float2* rsb = nullptr;
+  int64_t plane = 0;
+  float4 av = make_float4(0.f, 0.f, 0.f, 0.f), zv = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool alive = true;
+  int q_fail = blocks;
+
+  auto close_segment = [&]() {
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const unsigned t = atomicAdd(tickets + b, static_cast<unsigned>(seg));
+      s_last = (t + static_cast<unsigned>(seg) == static_cast<unsigned>(nb)) ? 1u : 0u;
+      if (s_last) {
+        __threadfence();
+        tickets[b] = 0u;
+      }
+    }
+    __syncthreads();
+    if (s_last) {
+      const double t = rows_sum_sq_y(rsb, c, sh);
+      if (tid == 0) {
+        const double norm = sqrt(t);
+        set_stage1_alphas(norm, scale, rho, rho2, b);
+        const double placed = norm * scale;
+        if (norm > 0.0 && !(placed > 0x1p-60 && placed < 0x1p60)) atomicExch(&g_status, kStatusFrontRange);
+        pre[b] = plane_scale_for(norm);
+      }
+      __syncthreads();
+    }
+  };
+
+  for (int q = 0; q < blocks; ++q) {
+    const int64_t j = j0 + q;
+    const int k = static_cast<int>(j / nb), blk = static_cast<int>(j - static_cast<int64_t>(k) * nb);
+    if (k != cur_k) {
+      if (cur_k >= 0) close_segment();
+      cur_k = k;
+      b = slots[k];
+      md = mats + b;
+      coef = RANK1 ? md->scal_a[0] : 0.0f;
+      scale = pre[b];
+      rsb = rs + static_cast<int64_t>(b) * ld_rs;
+      plane = static_cast<int64_t>(b) * rp * cp;
+      seg = 0;
+      if (has) {
+        av = reinterpret_cast<const float4*>(md->inv_a)[i4];
+        if (RANK1) zv = reinterpret_cast<const float4*>(md->z_a)[i4];
+      }
+    }
+    ++seg;
+    const int o0 = blk * kColsRows, rows = min(kColsRows, c - o0);
+    float ib[kColsPartRows];
+#pragma unroll
+    for (int r = 0; r < kColsPartRows; ++r) ib[r] = r0 + r < rows ? md->inv_b[o0 + r0 + r] : 0.0f;
+    const int s = q % kColsStages;
+    bool ok = alive && mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((q / kColsStages) & 1), &s_abort,
+                                 kStatusTimeoutFrontLoad);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) {
+      if (alive) q_fail = q;
+      alive = false;
+      continue;
+    }
+    if (tid == 0 && q >= 1 && issued < blocks) issue(issued++);
+    const float* sg = ring + static_cast<size_t>(2 * s) * kColsRows * n;
+    const float* smo = sg + kColsRows * n;
+    const float ae[4] = {av.x, av.y, av.z, av.w}, ze[4] = {zv.x, zv.y, zv.z, zv.w};
+
+    // 1. row statistics of this part's rows over the thread's columns
+    float pdot[kColsPartRows];
+    double psq[kColsPartRows];
+#pragma unroll
+    for (int r = 0; r < kColsPartRows; ++r) {
+      pdot[r] = 0.0f;
+      psq[r] = 0.0;
+      const int rr = r0 + r;
+      if (has && rr < rows) {
+        const float4 gv = reinterpret_cast<const float4*>(sg + static_cast<size_t>(rr) * n)[i4];
+        const float4 mv = reinterpret_cast<const float4*>(smo + static_cast<size_t>(rr) * n)[i4];
+        const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mn = mom_beta * me[e] + omb * ge[e];
+          const float src = mom_beta * mn + omb * ge[e];
+          const float y = (src * ib[r]) * ae[e];
+          psq[r] += static_cast<double>(y) * y;
+          if (RANK1) pdot[r] += y * ze[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kColsPartRows; ++r) {
+#pragma unroll
+      for (int off = kColsLanes / 2; off > 0; off >>= 1) {
+        psq[r] += __shfl_xor_sync(0xffffffffu, psq[r], off);
+        if (RANK1) pdot[r] += __shfl_xor_sync(0xffffffffu, pdot[r], off);
+      }
+    }
+    if (lane % kColsLanes == 0) {
+#pragma unroll
+      for (int r = 0; r < kColsPartRows; ++r) {
+        s_pdot[warp][r0 + r] = pdot[r];
+        s_psq[warp][r0 + r] = psq[r];
+      }
+    }
+    __syncthreads();
+    if (tid < kColsRows) {
+      float dot = 0.0f;
+      double sq = 0.0;
+      for (int w = 0; w < NW; ++w) {
+        dot += s_pdot[w][tid];
+        sq += s_psq[w][tid];
+      }
+      s_dot[tid] = dot;
+      if (tid < rows) rsb[o0 + tid] = make_float2(dot, static_cast<float>(sqrt(sq)));
+    }
+    __syncthreads();
+
+    // 2. momentum and this part's 16 / kColsParts X columns of rows i..i+3
+    if (has) {
+      uint32_t hw[4][kColsPartRows / 2], lw[4][kColsPartRows / 2];  // [X row e][bf16 pair of param rows]
+      float* mom = md->mom + static_cast<int64_t>(o0) * n;
+#pragma unroll
+      for (int w2 = 0; w2 < kColsPartRows / 2; ++w2) {
+        float hv[2][4], lv[2][4];
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int r = 2 * w2 + q2, rr = r0 + r;
+          if (rr < rows) {
+            const float4 gv = reinterpret_cast<const float4*>(sg + static_cast<size_t>(rr) * n)[i4];
+            const float4 mv = reinterpret_cast<const float4*>(smo + static_cast<size_t>(rr) * n)[i4];
+            const float cw = coef * s_dot[rr];
+            const float ge[4] = {gv.x, gv.y, gv.z, gv.w}, me[4] = {mv.x, mv.y, mv.z, mv.w};
+            float mn[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              mn[e] = mom_beta * me[e] + omb * ge[e];
+              const float src = mom_beta * mn[e] + omb * ge[e];
+              float v = (src * ib[r]) * ae[e];
+              if (RANK1) v += cw * ze[e];
+              split_hilo(v * scale, hv[q2][e], lv[q2][e]);
+            }
+            reinterpret_cast<float4*>(mom + static_cast<int64_t>(rr) * n)[i4] = make_float4(mn[0], mn[1], mn[2], mn[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hv[q2][e] = 0.0f;
+              lv[q2][e] = 0.0f;
+            }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hw[e][w2] = pack_bf16x2(hv[0][e], hv[1][e]);
+          lw[e][w2] = pack_bf16x2(lv[0][e], lv[1][e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t xo = plane + static_cast<int64_t>(4 * i4 + e) * cp + o0 + r0;
+        if constexpr (kColsPartRows == 8) {
+          *reinterpret_cast<uint4*>(xh + xo) = make_uint4(hw[e][0], hw[e][1], hw[e][2], hw[e][3]);
+          *reinterpret_cast<uint4*>(xl + xo) = make_uint4(lw[e][0], lw[e][1], lw[e][2], lw[e][3]);
+        } else {
+          *reinterpret_cast<uint2*>(xh + xo) = make_uint2(hw[e][0], hw[e][1]);
+          *reinterpret_cast<uint2*>(xl + xo) = make_uint2(lw[e][0], lw[e][1]);
+        }
+      }
+    }
+  }
+  close_segment();
+  if (!alive && tid == 0) {
+    for (int q = q_fail; q < issued; ++q) {
+      const int s = q % kColsStages;
+      mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>((q / kColsStages) & 1), nullptr, kStatusTimeoutFrontLoad);
     }
   }
 }

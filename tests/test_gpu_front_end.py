@@ -2,7 +2,8 @@
 
 From a plan's second step on, the front end is one pass: the untransposed
 matrices (d_out <= d_in) stream their rows through teams of 1, 2, 4 or 8
-warps (chosen by the row length), the transposed ones take 16-row blocks.
+warps (chosen by the row length), the transposed ones stream 16-row blocks
+whose columns become 32-byte pieces of X rows.
 These runs step several times, so every step after the first goes through
 that pass, and compare every step's update direction, and the final momenta
 and statistic EMAs, with the CPU oracle (bars: direction 1e-2 relative
@@ -10,9 +11,10 @@ Frobenius error and cosine >= 0.999; state 1e-5).
 
 Shapes: row lengths whose float4 count sits just above a team-size boundary
 (257, 513, 1025 float4 -> 2, 4, 8 warps with ragged last columns), a row of
-4 float4 (most of a warp idle), several matrices of one shape (CTA row ranges
-that cross matrix boundaries), a transposed partner in the same shape group,
-and the widest config-4 row (8192).
+6 float4 (most of a warp idle), several matrices of one shape (CTA row ranges
+that cross matrix boundaries), transposed matrices whose row counts leave a
+ragged last block and whose float4 counts leave idle lanes, and the widest
+config-4 row (8192).
 """
 import numpy as np
 import pytest
@@ -91,6 +93,7 @@ def test_row_stream_team_sizes_follow_oracle(variant):
         (60, 2052),                # 513 float4: four warps
         (40, 4100), (40, 4100),    # 1025 float4: eight warps
         (96, 96), (96, 96), (96, 96),
+        (40, 12), (40, 12),        # transposed, 3 float4 per row: most of a half idle, ragged last block
     ]
     run_steps(shapes, variant == "rank1", steps=3, seed=11)
 
