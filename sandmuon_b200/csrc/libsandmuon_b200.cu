@@ -961,14 +961,12 @@ static int run_s8(const std::vector<Group>& groups, const S8Launches& plan, cuda
         const int64_t per = static_cast<int64_t>(g.rp) * g.rp;
         const int blocks = static_cast<int>(std::min<int64_t>(cdiv(per / 4, 1024), 512));
         SM_TIMED(tm, SM_TCLASS_ELEMWISE, 0.0, st, ([&]() -> int {
-                   SM_TRY(launch_kernel(k_reduce_s8scale, dim3(g.batch), dim3(256), 0, st, g.partials, per_mat,
-                                        kS8Margin, g.s, g.s_inv, g.rho, g.px_alpha));
                    SM_TRY(launch_kernel(k_poly_stage1, dim3(blocks, g.batch), dim3(256), 0, st, g.gh, g.gl, g.g2,
-                                        g.s, g.rp, (float)kS8Coeff[0][0], (float)kS8Coeff[0][1],
-                                        (float)kS8Coeff[0][2]));
+                                        g.partials, per_mat, kS8Margin, g.s, g.s_inv, g.rho, g.px_alpha, g.rp,
+                                        (float)kS8Coeff[0][0], (float)kS8Coeff[0][1], (float)kS8Coeff[0][2]));
                    return SM_OK;
                  }()));
-        *launches += 2;
+        *launches += 1;
       }
     }
     SM_TRY(launch_s8_kind(groups, plan, kPX, stage, st, tm, launches));

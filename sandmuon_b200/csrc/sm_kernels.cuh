@@ -4,7 +4,7 @@
 //   N2  k_stats_finish                         : EMA + inverse square roots
 //   N3  k_whiten_rowstats / k_whiten_write     : Nesterov momentum, two-sided
 //                                                whitening, stage-1 hi/lo split
-//   N5  k_poly_stage1                          : first S8 polynomial (hi/lo)
+//   N5  k_poly_stage1                          : stage-1 scale s and first S8 polynomial (hi/lo)
 //   N7  k_mapback_rowstats / k_mapback_apply   : mapback, graft, weight update
 //   N8  k_adamw_multi                          : auxiliary AdamW
 //   --  k_reduce_*                             : per-matrix scalar reductions
@@ -462,6 +462,125 @@ __device__ __forceinline__ double block_sum_d(double v, double* sh) {
 
 constexpr float kFltTiny = 1.17549435e-38f;  // torch.finfo(torch.float32).tiny
 
+// Vectors of up to 256 * kFinishK elements: each thread loads its elements
+// once and the three passes below run from registers (one memory round trip
+// instead of three); the arithmetic and reduction orders are those of the
+// loop path.
+constexpr int kFinishK = 12;
+
+template <bool RANK1_A, bool KIND_B>
+__device__ __forceinline__ void stats_finish_regs(const StatDev& d, int n, float count, float beta, float omb,
+                                                  double* sh) {
+  float sum[kFinishK], ema[kFinishK], first[kFinishK], mema[kFinishK];
+#pragma unroll
+  for (int k = 0; k < kFinishK; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    const bool in = i < n;
+    sum[k] = in ? d.sum[i] : 0.0f;
+    ema[k] = (in && !d.init) ? d.ema[i] : 0.0f;
+    first[k] = (RANK1_A && in) ? d.first_sum[i] : 0.0f;
+    mema[k] = (RANK1_A && in && !d.init) ? d.mean_ema[i] : 0.0f;
+  }
+  if (KIND_B) {
+    // b = sum / count ; b /= max(mean(b), tiny)
+    double acc = 0.0;
+#pragma unroll
+    for (int k = 0; k < kFinishK; ++k)
+      if (threadIdx.x + 256 * k < n) acc += static_cast<double>(sum[k] / count);
+    const float mean_b = static_cast<float>(block_sum_d<256>(acc, sh) / n);
+    const float denom = fmaxf(mean_b, kFltTiny);
+    double acc_e = 0.0;
+#pragma unroll
+    for (int k = 0; k < kFinishK; ++k) {
+      const int i = threadIdx.x + 256 * k;
+      if (i < n) {
+        const float bv = (sum[k] / count) / denom;
+        ema[k] = d.init ? bv : ema[k] * beta + omb * bv;
+        d.ema[i] = ema[k];
+        d.sum[i] = 0.0f;
+        acc_e += ema[k];
+      }
+    }
+    __syncthreads();  // sh reuse
+    const float mean_e = static_cast<float>(block_sum_d<256>(acc_e, sh) / n);
+#pragma unroll
+    for (int k = 0; k < kFinishK; ++k) {
+      const int i = threadIdx.x + 256 * k;
+      if (i < n) {
+        const float nrm = fmaxf(ema[k], mean_e * 1e-6f) / fmaxf(mean_e, kFltTiny);
+        d.inv[i] = 1.0f / sqrtf(fmaxf(nrm, 1e-6f));
+      }
+    }
+    return;
+  }
+  double acc = 0.0;
+#pragma unroll
+  for (int k = 0; k < kFinishK; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      const float second = sum[k] / count;
+      ema[k] = d.init ? second : ema[k] * beta + omb * second;
+      d.ema[i] = ema[k];
+      d.sum[i] = 0.0f;
+      if (RANK1_A) {
+        const float mean = first[k] / count;
+        mema[k] = d.init ? mean : mema[k] * beta + omb * mean;
+        d.mean_ema[i] = mema[k];
+        d.first_sum[i] = 0.0f;
+      }
+      acc += ema[k];
+    }
+  }
+  const float mean_e = static_cast<float>(block_sum_d<256>(acc, sh) / n);
+  if (!RANK1_A) {
+#pragma unroll
+    for (int k = 0; k < kFinishK; ++k) {
+      const int i = threadIdx.x + 256 * k;
+      if (i < n) {
+        const float nrm = fmaxf(ema[k], mean_e * 1e-6f) / fmaxf(mean_e, kFltTiny);
+        d.inv[i] = 1.0f / sqrtf(fmaxf(nrm, 1e-6f));
+      }
+    }
+    if (threadIdx.x == 0) {
+      d.scal[0] = 0.0f;
+      d.scal[1] = 0.0f;
+      d.scal[2] = 0.0f;
+      d.scal[3] = 0.0f;
+    }
+    return;
+  }
+  // rank1_inverse_sqrt (sandmuon/optimizer.py:27-35)
+  const float scale = fmaxf(mean_e, kFltTiny);
+  const float root_scale = sqrtf(scale);
+  double acc_z = 0.0, acc_zeta = 0.0;
+#pragma unroll
+  for (int k = 0; k < kFinishK; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      const float mu = mema[k];
+      const float var = fmaxf(ema[k] - mu * mu, 0.0f);
+      const float inv = 1.0f / sqrtf(fmaxf(var / scale, 1e-6f));
+      const float z = inv * (mu / root_scale);
+      d.inv[i] = inv;
+      d.z[i] = z;
+      d.zeta[i] = inv * z;
+      acc_z += static_cast<double>(z) * z;
+      acc_zeta += static_cast<double>(inv * z) * (inv * z);
+    }
+  }
+  __syncthreads();  // sh reuse
+  const double kz = block_sum_d<256>(acc_z, sh);
+  __syncthreads();
+  const double kzeta = block_sum_d<256>(acc_zeta, sh);
+  if (threadIdx.x == 0) {
+    const float root = sqrtf(1.0f + static_cast<float>(kz));
+    d.scal[0] = -1.0f / (root * (root + 1.0f));
+    d.scal[1] = static_cast<float>(kzeta);
+    d.scal[2] = static_cast<float>(kz);
+    d.scal[3] = 0.0f;
+  }
+}
+
 __global__ void __launch_bounds__(256) k_stats_finish(const StatDev* __restrict__ stats, float beta, float omb) {
   grid_dep_wait();
   grid_dep_launch();
@@ -469,6 +588,12 @@ __global__ void __launch_bounds__(256) k_stats_finish(const StatDev* __restrict_
   const StatDev d = stats[blockIdx.x];
   const int n = d.n;
   const float count = static_cast<float>(d.count_dev != nullptr ? *d.count_dev : d.count);
+  if (n <= 256 * kFinishK) {
+    if (d.kind == SM_STAT_B) stats_finish_regs<false, true>(d, n, count, beta, omb, sh);
+    else if (d.kind == SM_STAT_A_RANK1) stats_finish_regs<true, false>(d, n, count, beta, omb, sh);
+    else stats_finish_regs<false, false>(d, n, count, beta, omb, sh);
+    return;
+  }
 
   if (d.kind == SM_STAT_B) {
     // b = sum / count ; b /= max(mean(b), tiny)
@@ -1630,42 +1755,37 @@ __global__ void __launch_bounds__(kColsMaxThreads, 1)
 
 // ================================================ S8 stage-1 scale and poly
 // s[b] = max(1.35 * |G2_b|_F^(1/4), 1e-30) from the per-tile partial sums of
-// squares written by the G*G epilogue (sandmuon/optimizer.py:81), and the
-// stage-1 P X alpha rho[b] / s[b].
+// squares written by the G*G epilogue (sandmuon/optimizer.py:81), then
+// P = a I + b G / s / s + c G2 / s / s / s / s (sandmuon/optimizer.py:83-84),
+// emitted as hi/lo BF16 planes in place of the G hi/lo planes.  Every CTA of
+// matrix b reduces the matrix's partials itself (a few hundred floats from
+// L2, in one fixed order, so every CTA derives the same s); the matrix's
+// first CTA also stores s, 1/s and the stage-1 P X alpha rho[b] / s[b].
+// Four consecutive elements (one row, rp % 4 == 0) per thread and iteration.
 __global__ void __launch_bounds__(256)
-    k_reduce_s8scale(const float* __restrict__ partials, int per_mat, float margin, float* __restrict__ s,
-                     float* __restrict__ s_inv, const float* __restrict__ rho, float* __restrict__ px_alpha) {
+    k_poly_stage1(__nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ gl, const float* __restrict__ g2,
+                  const float* __restrict__ partials, int per_mat, float margin, float* __restrict__ s,
+                  float* __restrict__ s_inv, const float* __restrict__ rho, float* __restrict__ px_alpha, int rp,
+                  float pa, float pb, float pc) {
   grid_dep_wait();
   grid_dep_launch();
   __shared__ double sh[8];
-  double acc = 0.0;
-  for (int p = threadIdx.x; p < per_mat; p += blockDim.x)
-    acc += partials[static_cast<int64_t>(blockIdx.x) * per_mat + p];
-  const double t = block_sum_d<256>(acc, sh);
-  if (threadIdx.x == 0) {
-    const float nrm = static_cast<float>(sqrt(t));
-    const float sv = fmaxf(margin * powf(nrm, 0.25f), 1e-30f);
-    s[blockIdx.x] = sv;
-    s_inv[blockIdx.x] = 1.0f / sv;
-    // stage-1 P X: (P x) / s with x = rho * (stored planes)
-    px_alpha[blockIdx.x] = rho[blockIdx.x] * (1.0f / sv);
-  }
-}
-
-// P = a I + b G / s / s + c G2 / s / s / s / s (sandmuon/optimizer.py:83-84),
-// emitted as hi/lo BF16 planes in place of the G hi/lo planes.  Four
-// consecutive elements (one row, rp % 4 == 0) per thread and iteration.
-__global__ void __launch_bounds__(256)
-    k_poly_stage1(__nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ gl, const float* __restrict__ g2,
-                  const float* __restrict__ s, int rp, float pa, float pb, float pc) {
-  grid_dep_wait();
-  grid_dep_launch();
   const int b = blockIdx.y;
+  double acc = 0.0;
+  for (int p = threadIdx.x; p < per_mat; p += blockDim.x) acc += partials[static_cast<int64_t>(b) * per_mat + p];
+  const double t = block_sum_d<256>(acc, sh);
+  const float sv = fmaxf(margin * powf(static_cast<float>(sqrt(t)), 0.25f), 1e-30f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    s[b] = sv;
+    s_inv[b] = 1.0f / sv;
+    // stage-1 P X: (P x) / s with x = rho * (stored planes)
+    px_alpha[b] = rho[b] * (1.0f / sv);
+  }
   const int64_t per4 = static_cast<int64_t>(rp) * rp / 4;
   // Multiplications by 1/s, one at a time: for a zero matrix (s = 1e-30, so
   // 1/s = 1e30 while 1/s^2 would overflow) every partial product stays 0 and
   // P = a I exactly; for a normalised input s is O(1).
-  const float is = 1.0f / s[b];
+  const float is = 1.0f / sv;
   const int64_t base = static_cast<int64_t>(b) * rp * rp;
   for (int64_t i4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i4 < per4;
        i4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
