@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--partition", choices=("lpt", "layer"), default="lpt")
+    ap.add_argument("--transport", choices=("auto", "peer", "nccl"), default="auto",
+                    help="how updated weights reach the other ranks at N>1: peer stores from the update kernel "
+                         "(auto: when every rank can map its peers) or an NCCL all-gather")
     ap.add_argument("--exchange", choices=("weights", "bf16_delta"), default="weights",
                     help="N > 1: all-gather FP32 updated weights (default) or BF16 update deltas")
     ap.add_argument("--profile", action="store_true",
@@ -91,7 +94,7 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def workload_config(world, partition, workload="cfg1", exchange="weights"):
+def workload_config(world, partition, workload="cfg1", exchange="weights", transport=None):
     layers, width, hidden, rows = SETS[workload]
     params = layers * (4 * width * width + 2 * width * hidden)
     return {
@@ -101,7 +104,8 @@ def workload_config(world, partition, workload="cfg1", exchange="weights"):
         "params": params,
         "s8_precision": "stages 1-4 compensated bf16 (hi/lo, 3 products), stage 5 bf16, fp32 accumulate",
         "l2": "no flush: each step streams ~1 GB of FP32 state (> 126 MB L2)",
-        "parallelism": (f"matrix-sharded ({partition}, {exchange} exchange) x{world}" if world > 1
+        "parallelism": (f"matrix-sharded ({partition}, {exchange} exchange"
+                        f"{' by ' + transport if transport else ''}) x{world}" if world > 1
                         else "single GPU"),
     }
 
@@ -164,7 +168,15 @@ class ClockSampler:
 
 # -------------------------------------------------------------- workload
 
-def build(device, group, partition, workload="cfg1", exchange="weights"):
+def used_transport(opt) -> str:
+    """How this run's weight exchange travelled: "peer" stores or "nccl"."""
+    sharding = opt.sharding
+    if sharding is None or sharding.exchange_mode != "weights":
+        return "nccl"
+    return "peer" if sharding.peer_bases else "nccl"
+
+
+def build(device, group, partition, workload="cfg1", exchange="weights", transport="auto"):
     from sandmuon_b200 import RankOneAWeightedPE
     from sandmuon_b200.workloads import gpt_matrix_model, synth_gpt_statistics
     layers, width, hidden, rows = SETS[workload]
@@ -175,7 +187,8 @@ def build(device, group, partition, workload="cfg1", exchange="weights"):
         for p in model.parameters():
             p.copy_(torch.from_numpy((rng.standard_normal(tuple(p.shape)) * 0.02).astype(np.float32)))
     model.to(device)
-    opt = RankOneAWeightedPE(model, lr=LR, process_group=group, partition=partition, exchange=exchange)
+    opt = RankOneAWeightedPE(model, lr=LR, process_group=group, partition=partition, exchange=exchange,
+                             transport=transport)
     grads_host = {}
     for n, p in opt.named_matrices.items():
         g = (rng.standard_normal(tuple(p.shape)) * 1e-4).astype(np.float32)
@@ -781,7 +794,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         group = dist.group.WORLD
     model, opt, grads_host, refill, stat_bytes = build(device, group, args.partition, args.workload,
-                                                       args.exchange)
+                                                       args.exchange, args.transport)
     if args.profile:
         for _ in range(args.warmup + args.steps):
             refill()
@@ -883,7 +896,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 tensor cores (stages 1-4 compensated hi/lo) / fp32 state",
             "data": "synthetic (seeded; random-init weights, N(0,1e-4) grads, injected statistics)",
-            "config": workload_config(world, args.partition, args.workload, args.exchange),
+            "config": workload_config(world, args.partition, args.workload, args.exchange,
+                                      used_transport(opt) if world > 1 else None),
             "s8_gemm_tflops": round(achieved, 1),
             "s8_gemm_ms_per_step": round(gemm_ms, 4),
             "s8_gemm_tflop_per_step_executed": round(gemm_flops / 1e12, 4),

@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define SM_ABI_VERSION 2
+#define SM_ABI_VERSION 3
 
 /* status codes */
 #define SM_OK 0
@@ -200,6 +200,30 @@ int sm_plan_step(SmPlan* plan, const SmStepArgs* args, void* stream);
  * issued on a stream that is itself being captured returns
  * SM_ERR_UNSUPPORTED.  enabled = 0 launches every kernel individually. */
 int sm_plan_set_replay(SmPlan* plan, int enabled);
+
+/* Weight exchange by the update kernel itself (a sharded step; no
+ * counterpart in the single-device reference, which has no exchange).  Each
+ * rank keeps the selected matrices in one flat buffer of the same layout;
+ * from the next step on, every weight the plan updates inside
+ * [local_base, local_base + bytes) is also stored at the same offset from
+ * each of the n_peers peer_bases: the other ranks' copies of that buffer,
+ * mapped into this device's address space with sm_ipc_open.  The caller
+ * orders the ranks' steps around it (a collective before the step, which
+ * the statistic reduction is, and one after it, before any rank reads the
+ * buffer).  n_peers = 0 turns it off.  At most 15 peers. */
+int sm_plan_set_peers(SmPlan* plan, const void* local_base, int64_t bytes, const void* const* peer_bases,
+                      int32_t n_peers);
+
+/* CUDA IPC of a device buffer for sm_plan_set_peers.  sm_ipc_export writes
+ * the 64-byte IPC handle of the allocation that holds ptr and ptr's byte
+ * offset inside it; another process calls sm_ipc_open with the handle (on
+ * its own current device: peer access over NVLink) and adds the offset to
+ * the returned base; sm_ipc_close unmaps that base.  The exporter keeps the
+ * allocation alive until every importer has closed it.  No multicast
+ * mapping is made. */
+int sm_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int sm_ipc_open(const void* handle, void** base_out);
+int sm_ipc_close(void* base);
 
 /* Optional per-kernel-class timing with CUDA events (for the benchmark).
  * When enabled, sm_plan_step records an event pair around each launch;

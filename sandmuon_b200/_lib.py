@@ -99,6 +99,10 @@ SIGNATURES = {
     "sm_plan_create": (_c_int, [ctypes.POINTER(SmPlanSpec), _c_void_p, _c_size, _c_void_p, ctypes.POINTER(_c_void_p)]),
     "sm_plan_step": (_c_int, [_c_void_p, ctypes.POINTER(SmStepArgs), _c_void_p]),
     "sm_plan_set_replay": (_c_int, [_c_void_p, _c_int]),
+    "sm_plan_set_peers": (_c_int, [_c_void_p, _c_void_p, _c_i64, ctypes.POINTER(_c_void_p), _c_i32]),
+    "sm_ipc_export": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_i64)]),
+    "sm_ipc_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "sm_ipc_close": (_c_int, [_c_void_p]),
     "sm_plan_set_timing": (_c_int, [_c_void_p, _c_int]),
     "sm_plan_timing_read": (_c_int, [_c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_c_i64),
                                      ctypes.POINTER(ctypes.c_double)]),
@@ -165,6 +169,33 @@ def ensure_device(device: torch.device) -> None:
 
 def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(CUDA IPC handle of the allocation holding t, t's byte offset in it)."""
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    offset = _c_i64(0)
+    with torch.cuda.device(t.device):
+        check(load().sm_ipc_export(_c_void_p(t.data_ptr()), handle, ctypes.byref(offset)), "IPC export")
+    return handle.raw, offset.value
+
+
+def ipc_open(handle: bytes, device: torch.device) -> int:
+    """Maps another process's exported allocation into `device`'s address
+    space (peer access); returns the mapped base address."""
+    base = _c_void_p(0)
+    buf = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        check(load().sm_ipc_open(buf, ctypes.byref(base)), "IPC open")
+    return int(base.value)
+
+
+def ipc_close(base: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        check(load().sm_ipc_close(_c_void_p(base)), "IPC close")
 
 
 def device_status(device: torch.device) -> int:

@@ -1147,8 +1147,8 @@ static int run_front(const Group& g, const MatDev* d_mats, float mom_beta, float
 }
 
 // Mapback + graft + update back end for one group (N7 passes 1 and 2).
-static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cudaStream_t st, Timer* tm,
-                    int64_t* launches) {
+static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, const PeerSet& peers, cudaStream_t st,
+                    Timer* tm, int64_t* launches) {
   const int B = g.batch;
   const int ld = g.dmax;
   const MatDev* mats = d_mats + g.mat_off;
@@ -1167,7 +1167,7 @@ static int run_back(const Group& g, const MatDev* d_mats, bool vec4, int sms, cu
              auto kern = g.rank1 ? (vec4 ? k_mapback_apply<true, true> : k_mapback_apply<true, false>)
                                  : (vec4 ? k_mapback_apply<false, true> : k_mapback_apply<false, false>);
              SM_TRY(launch_kernel(kern, grid, dim3(256), 0, st, mats, g.q, static_cast<int64_t>(g.rp),
-                                  static_cast<int64_t>(g.cp), g.rs_map, ld, g.gamma));
+                                  static_cast<int64_t>(g.cp), g.rs_map, ld, g.gamma, peers));
              return SM_OK;
            }()));
   *launches += 2;
@@ -1215,6 +1215,11 @@ struct SmPlan {
   cudaGraphExec_t exec = nullptr;
   std::vector<uint8_t> exec_vec4;
   int64_t exec_launches = 0;
+  // Peer-mirrored weight range (sm_plan_set_peers): weights inside
+  // [peer_lo, peer_hi) are also stored at each peer's copy.
+  PeerSet peers{};
+  const char* peer_lo = nullptr;
+  const char* peer_hi = nullptr;
 };
 
 namespace smb {
@@ -1978,6 +1983,11 @@ int sm_plan_step(SmPlan* p, const SmStepArgs* args, void* stream) {
     d.weight = m.weight;
     d.export_to = m.export_to;
     d.export_bf16 = (p->export_mode == SM_EXPORT_BF16_DELTA && m.export_to != nullptr) ? 1 : 0;
+    {
+      const char* w = reinterpret_cast<const char*>(m.weight);
+      const int64_t wbytes = static_cast<int64_t>(m.d_out) * m.d_in * 4;
+      d.peer = (p->peers.n > 0 && w >= p->peer_lo && w + wbytes <= p->peer_hi) ? 1 : 0;
+    }
     d.inv_a = p->s_inv[m.a_stat];
     d.z_a = p->s_z[m.a_stat];
     d.zeta_a = p->s_zeta[m.a_stat];
@@ -2087,7 +2097,7 @@ static int launch_step(SmPlan* p, const std::vector<uint8_t>& vec4, bool first, 
   DeviceInfo* di;
   SM_TRY(current_device_info(&di));
   for (size_t gi = 0; gi < p->groups.size(); ++gi)
-    SM_TRY(run_back(p->groups[gi], p->d_mats, vec4[gi] != 0, di->sms, st, tm, &launches));
+    SM_TRY(run_back(p->groups[gi], p->d_mats, vec4[gi] != 0, di->sms, p->peers, st, tm, &launches));
   *out = launches;
   return SM_OK;
 }
@@ -2215,8 +2225,11 @@ int sm_s8_polar(const float* x, float* out, int32_t batch, int32_t rows, int32_t
   {
     const bool out_vec4 = vec4 && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
     dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(per, 1024), 8 * di->sms))), batch);
-    if (out_vec4) k_mapback_apply<false, true><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
-    else k_mapback_apply<false, false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma);
+    const PeerSet none{};  // hm[].peer is 0: no peer stores
+    if (out_vec4)
+      k_mapback_apply<false, true><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma, none);
+    else
+      k_mapback_apply<false, false><<<grid, 256, 0, st>>>(d_mats, g.q, g.rp, g.cp, g.rs_map, g.dmax, g.gamma, none);
     SM_LAUNCHED();
   }
   return SM_OK;
@@ -2415,6 +2428,66 @@ int sm_gemm_bf16(const void* a_hi, const void* a_lo, const void* b_hi, const voi
   const int grid = std::min(L.total_tiles, workers) * cg;
   const int lay = a_mn ? kLayoutMM : (b_kmajor ? kLayoutKK : kLayoutKM);
   return dispatch_gemm(bn, cg, comp, lay, epilogue, L, grid, static_cast<cudaStream_t>(stream));
+}
+
+int sm_plan_set_peers(SmPlan* p, const void* local_base, int64_t bytes, const void* const* peer_bases,
+                      int32_t n_peers) {
+  if (p == nullptr) return fail(SM_ERR_ARG, "null plan");
+  if (n_peers < 0 || n_peers > kMaxPeers) return fail(SM_ERR_ARG, "n_peers must be in [0, 15]");
+  if (n_peers > 0 && (local_base == nullptr || bytes <= 0 || peer_bases == nullptr))
+    return fail(SM_ERR_ARG, "peer delivery needs a local range and the peers' bases");
+  PeerSet ps{};
+  ps.n = n_peers;
+  for (int r = 0; r < n_peers; ++r) {
+    if (peer_bases[r] == nullptr) return fail(SM_ERR_ARG, "null peer base");
+    ps.delta[r] = reinterpret_cast<const char*>(peer_bases[r]) - reinterpret_cast<const char*>(local_base);
+  }
+  p->peers = ps;
+  p->peer_lo = static_cast<const char*>(local_base);
+  p->peer_hi = p->peer_lo + (n_peers > 0 ? bytes : 0);
+  // the peer set is a launch argument: the next replay re-captures the step
+  if (p->exec != nullptr) {
+    SM_CUDA(cudaGraphExecDestroy(p->exec));
+    p->exec = nullptr;
+  }
+  return SM_OK;
+}
+
+static PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+
+int sm_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr) return fail(SM_ERR_ARG, "null argument");
+  if (g_addr_range == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return fail(SM_ERR_UNSUPPORTED, "cuMemGetAddressRange is unavailable");
+    g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(SM_ERR_CUDA, "cuMemGetAddressRange failed: " + std::to_string(r));
+  cudaIpcMemHandle_t h;
+  SM_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return SM_OK;
+}
+
+int sm_ipc_open(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr) return fail(SM_ERR_ARG, "null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  SM_CUDA(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return SM_OK;
+}
+
+int sm_ipc_close(void* base) {
+  if (base == nullptr) return fail(SM_ERR_ARG, "null base");
+  SM_CUDA(cudaIpcCloseMemHandle(base));
+  return SM_OK;
 }
 
 }  // extern "C"

@@ -692,7 +692,7 @@ struct MatDev {
   float lr;
   float sqrt_rows;      // sqrt(d_out): the graft norm
   int32_t export_bf16;  // 1: export_to holds bf16 D = bf16(lr * direction), W -= float(D)
-  int32_t pad1;
+  int32_t peer;         // 1: the weight lies in the plan's peer-mirrored range (PeerSet)
 };
 
 // ========================================== N3 pass 1: whitening row stats
@@ -1921,6 +1921,18 @@ __global__ void __launch_bounds__(256, SMB_MAPBACK_MINB)
   }
 }
 
+// Peer delivery of updated weights (a sharded step's weight exchange done by
+// the update kernel itself): every updated weight of a matrix flagged
+// MatDev::peer is also stored at byte offset delta[r] from its local address,
+// the same position in peer r's copy of the flat weight buffer, mapped into
+// this device's address space (plain stores over NVLink; no multicast).
+constexpr int kMaxPeers = 15;
+struct PeerSet {
+  int32_t n;
+  int32_t pad;
+  int64_t delta[kMaxPeers];
+};
+
 // ======================================== N7 pass 2: mapback + update apply
 // W[o,i] -= lr * gamma * inv_b[o] * inv_a[i] * (Q[o,i] + c t[o] z[i])
 // (sandmuon/optimizer.py:303-315).  Grid-stride over the matrix (blockIdx.y)
@@ -1928,7 +1940,7 @@ __global__ void __launch_bounds__(256, SMB_MAPBACK_MINB)
 template <bool RANK1, bool VEC4>
 __global__ void __launch_bounds__(256)
     k_mapback_apply(const MatDev* __restrict__ mats, const __nv_bfloat16* __restrict__ q, int64_t rp, int64_t cp,
-                    const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma) {
+                    const float2* __restrict__ rs, int ld_rs, const float* __restrict__ gamma, const PeerSet peers) {
   grid_dep_wait();
   grid_dep_launch();
   const int b = blockIdx.y;
@@ -1938,6 +1950,7 @@ __global__ void __launch_bounds__(256)
   const float step = md.lr * gamma[b];
   const float coef = RANK1 ? md.scal_a[0] : 0.0f;
   const int per_row = VEC4 ? md.d_in / 4 : md.d_in;
+  const int n_peers = md.peer ? peers.n : 0;
   const int64_t total = static_cast<int64_t>(md.d_out) * per_row;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -1970,6 +1983,8 @@ __global__ void __launch_bounds__(256)
       w.z = w.z - d.z;
       w.w = w.w - d.w;
       *wp = w;
+      for (int r = 0; r < n_peers; ++r)
+        *reinterpret_cast<float4*>(reinterpret_cast<char*>(wp) + peers.delta[r]) = w;
       if (md.export_to != nullptr && !md.export_bf16)
         *reinterpret_cast<float4*>(md.export_to + static_cast<int64_t>(o) * md.d_in + i) = w;
     } else {
@@ -1986,6 +2001,8 @@ __global__ void __launch_bounds__(256)
       }
       const float w = md.weight[wi] - d;
       md.weight[wi] = w;
+      for (int r = 0; r < n_peers; ++r)
+        *reinterpret_cast<float*>(reinterpret_cast<char*>(md.weight + wi) + peers.delta[r]) = w;
       if (md.export_to != nullptr && !md.export_bf16) md.export_to[wi] = w;
     }
   }

@@ -9,10 +9,17 @@ its own microbatches; at step():
   2. each rank runs momentum -> whitening -> S8 -> mapback -> update only for
      the matrices it owns (partition "lpt": longest-processing-time greedy
      over S8 FLOPs; "layer": contiguous transformer layers per rank);
-  3. exchange: the owners' updated FP32 weights are all-gathered with one
-     padded, in-place all_gather_into_tensor: the selected matrices live in
-     one flat buffer laid out as the gather's output, so nothing is copied
-     before or after it (exchange="weights", the default).
+  3. exchange: every rank keeps the selected matrices in one flat FP32
+     buffer of the same layout (each owner's matrices back to back in its
+     shard).  With exchange="weights" (the default) the owners' updated
+     weights reach the other ranks one of two ways (`transport`):
+       "peer": the update kernel itself stores each updated weight into
+       every rank's copy of the buffer (CUDA IPC mappings of the peers'
+       buffers, plain stores over NVLink), and the exchange is a one-element
+       all-reduce that orders the ranks: no bulk collective at all;
+       "nccl": an in-place all_gather_into_tensor of the buffer.
+     "auto" (the default) takes "peer" when the buffer is on CUDA under an
+     NCCL group and every rank could map every peer, else "nccl".
      exchange="bf16_delta" gathers the
      update deltas lr * direction rounded to BF16 instead (half the NVLink
      bytes); every rank, the owner included, subtracts the same rounded delta,
@@ -63,6 +70,7 @@ def partition_matrices(named_shapes: dict[str, tuple[int, int]], world: int, how
 
 
 EXCHANGES = ("weights", "bf16_delta")
+TRANSPORTS = ("auto", "peer", "nccl")
 
 
 def _copy_pairs(pairs, device) -> None:
@@ -78,9 +86,12 @@ class MatrixSharding:
     rank) the constructor moves the selected matrices' storage into the flat
     all-gather buffer (_rehome_weights)."""
 
-    def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights", copy_fn=None):
+    def __init__(self, opt, group, *, partition: str = "lpt", exchange: str = "weights", copy_fn=None,
+                 transport: str = "auto"):
         if exchange not in EXCHANGES:
             raise ValueError(f"unknown exchange {exchange!r} (expected one of {EXCHANGES})")
+        if transport not in TRANSPORTS:
+            raise ValueError(f"unknown transport {transport!r} (expected one of {TRANSPORTS})")
         self.opt = opt
         self.group = group
         self.exchange_mode = exchange
@@ -94,8 +105,13 @@ class MatrixSharding:
         self._owner = {id(opt.named_matrices[n]): r for n, r in self.owner_by_name.items()}
         self._gather = None
         self._flat_weights = None
+        self.peer_bases: list[int] = []   # the other ranks' flat buffers, mapped here
+        self._opened: list[int] = []      # IPC bases to unmap at close
+        self._token = None
         if exchange == "weights" and self.world > 1:
             self._rehome_weights()
+            if transport != "nccl":
+                self._map_peers(required=transport == "peer")
 
     def owns(self, parameter) -> bool:
         return self._owner[id(parameter)] == self.rank
@@ -246,6 +262,67 @@ class MatrixSharding:
         self._flat_weights = flat
         self._homes = [(p, p.data_ptr()) for p in params]
 
+    def _map_peers(self, required: bool) -> None:
+        """Maps every other rank's flat weight buffer into this device (CUDA
+        IPC; a collective).  All ranks agree: if any rank cannot map every
+        peer, every rank unmaps and keeps the NCCL all-gather (or raises when
+        `required`)."""
+        from . import _lib
+        flat = self._flat_weights
+        device = flat.device
+        usable = flat.is_cuda and dist.get_backend(self.group) == "nccl" and self.world - 1 <= 15
+        entry = None
+        if usable:
+            try:
+                entry = _lib.ipc_export(flat)
+            except RuntimeError:
+                entry = None
+        entries = [None] * self.world
+        dist.all_gather_object(entries, entry, group=self.group)
+        ok = all(e is not None for e in entries)
+        bases = []
+        if ok:
+            try:
+                for r, (handle, offset) in enumerate(entries):
+                    if r == self.rank:
+                        continue
+                    base = _lib.ipc_open(handle, device)
+                    self._opened.append(base)
+                    bases.append(base + offset)
+            except RuntimeError:
+                ok = False
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device if flat.is_cuda else "cpu")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        if int(flag.item()) != 1:
+            self._unmap()
+            if required:
+                raise RuntimeError("transport='peer' needs every rank to map every peer's weight buffer "
+                                   "(CUDA tensors, an NCCL group, at most 16 ranks)")
+            return
+        self.peer_bases = bases
+        self._token = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def _unmap(self) -> None:
+        from . import _lib
+        for base in self._opened:
+            _lib.ipc_close(base, self._flat_weights.device)
+        self._opened = []
+        self.peer_bases = []
+
+    def peer_target(self) -> tuple[int, int, list[int]]:
+        """(local flat buffer address, its bytes, the peers' buffer addresses)
+        for StepPlan.set_peers."""
+        flat = self._flat_weights
+        return flat.data_ptr(), flat.numel() * flat.element_size(), list(self.peer_bases)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers after a barrier, so that no rank still
+        stores into a buffer another rank is about to free (a collective)."""
+        if self._opened:
+            dist.all_reduce(self._token, group=self.group)
+            torch.cuda.synchronize(self._flat_weights.device)
+            self._unmap()
+
     def _layout(self):
         """(send, recv, slots, unpack) of the all-gather.  Weights: send is this
         rank's shard of the flat weight buffer and recv the whole buffer (an
@@ -290,7 +367,8 @@ class MatrixSharding:
         return self._layout()[2][id(parameter)]
 
     def exchange(self, matrix_items) -> None:
-        """All-gathers the owners' updates into all ranks.  Weights: one
+        """Brings the owners' updates to all ranks.  Weights by peer stores:
+        a one-element all-reduce that orders the ranks.  Weights by NCCL: one
         in-place all-gather of the flat weight buffer (the update kernel
         already wrote the owned weights there).  BF16 deltas: the owners' send
         slots were filled by the update kernel; the received deltas of the
@@ -307,6 +385,12 @@ class MatrixSharding:
                     raise RuntimeError("a selected matrix's storage moved after the sharded optimizer was built "
                                        "(for example model.to() or a reassigned .data); build the optimizer "
                                        "after the model is in place")
+        if self.peer_bases:
+            # the update kernel already stored every owner's weights into every
+            # rank's buffer: this all-reduce only orders the ranks (each rank's
+            # update kernel precedes its part of it in stream order)
+            dist.all_reduce(self._token, group=self.group)
+            return
         send, recv, slots, unpack = self._layout()
         dist.all_gather_into_tensor(recv, send, group=self.group)
         if self.exchange_mode == "bf16_delta":

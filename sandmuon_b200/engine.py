@@ -259,6 +259,15 @@ class StepPlan:
         """Graph replay of the step's launches (on by default; identical results)."""
         _lib.check(_lib.load().sm_plan_set_replay(self._handle, int(enabled)), "sm_plan_set_replay")
 
+    def set_peers(self, local_base: int, nbytes: int, peer_bases: list[int]) -> None:
+        """From the next step on, every weight this plan updates inside
+        [local_base, local_base + nbytes) is also stored at the same offset
+        from each peer base (other ranks' copies of the flat weight buffer,
+        mapped into this device); an empty list turns it off."""
+        arr = (ctypes.c_void_p * max(1, len(peer_bases)))(*peer_bases)
+        rc = _lib.load().sm_plan_set_peers(self._handle, ctypes.c_void_p(local_base), nbytes, arr, len(peer_bases))
+        _lib.check(rc, "sm_plan_set_peers")
+
     def set_timing(self, enabled: bool) -> None:
         _lib.check(_lib.load().sm_plan_set_timing(self._handle, int(enabled)), "sm_plan_set_timing")
 

@@ -38,7 +38,9 @@ class DiagonalWeightedPE(Optimizer):
     Extra keywords: `process_group` (torch.distributed group or None) shards
     the S8 work over the group's ranks, `partition` ("lpt" or "layer") picks
     the owners, `exchange` ("weights" or "bf16_delta") what the owners
-    all-gather, and `reduce_gradients=True` makes step() average the
+    exchange, `transport` ("auto", "peer" or "nccl") how updated weights
+    reach the other ranks (peer stores from the update kernel, or an NCCL
+    all-gather), and `reduce_gradients=True` makes step() average the
     gradients over the group itself (reduce-scatter of the matrix gradients
     to their owners, all-reduce of the rest) in place of a data-parallel
     wrapper's all-reduce; see sandmuon_b200.distributed.
@@ -47,7 +49,7 @@ class DiagonalWeightedPE(Optimizer):
     def __init__(self, model: nn.Module, lr: float, *, rank_one_a: bool = False,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
                  process_group=None, partition: str = "lpt", exchange: str = "weights",
-                 reduce_gradients: bool = False):
+                 reduce_gradients: bool = False, transport: str = "auto"):
         choose = module_filter or (lambda name, module: isinstance(module, nn.Linear))
         matrices: dict[str, nn.Parameter] = {}
         modules: dict[str, nn.Module] = {}
@@ -96,7 +98,8 @@ class DiagonalWeightedPE(Optimizer):
         self._reduce_gradients = bool(reduce_gradients)
         if process_group is not None:
             from .distributed import MatrixSharding
-            self._sharding = MatrixSharding(self, process_group, partition=partition, exchange=exchange)
+            self._sharding = MatrixSharding(self, process_group, partition=partition, exchange=exchange,
+                                            transport=transport)
 
         self.handles = []
         for name, module in modules.items():
@@ -378,6 +381,8 @@ class DiagonalWeightedPE(Optimizer):
             plan = engine.StepPlan(device, mats, stat_specs, statistic_beta=self.statistic_beta, momentum=momentum,
                                    export_mode=export_mode)
             self._plans[key] = plan
+            if self._sharding is not None and self._sharding.peer_bases:
+                plan.set_peers(*self._sharding.peer_target())
         device_counts = None
         if self._sharding is not None:
             flat = self._flat_statistics(device, stat_specs)
@@ -426,12 +431,17 @@ class DiagonalWeightedPE(Optimizer):
         return sd
 
     def close(self):
+        """Removes the hooks and frees the plans; a sharded optimizer that
+        delivers weights by peer stores also unmaps its peers' buffers, after
+        a barrier (a collective: call on every rank)."""
         for handle in self.handles:
             handle.remove()
         self.handles.clear()
         for plan in self._plans.values():
             plan.close()
         self._plans.clear()
+        if self._sharding is not None:
+            self._sharding.close()
 
 
 class RankOneAWeightedPE(DiagonalWeightedPE):
@@ -443,10 +453,10 @@ class RankOneAWeightedPE(DiagonalWeightedPE):
     def __init__(self, model: nn.Module, lr: float, *,
                  module_filter: Callable[[str, nn.Module], bool] | None = None,
                  process_group=None, partition: str = "lpt", exchange: str = "weights",
-                 reduce_gradients: bool = False, split_sides: bool = False):
+                 reduce_gradients: bool = False, split_sides: bool = False, transport: str = "auto"):
         super().__init__(model, lr, rank_one_a=True, module_filter=module_filter,
                          process_group=process_group, partition=partition, exchange=exchange,
-                         reduce_gradients=reduce_gradients)
+                         reduce_gradients=reduce_gradients, transport=transport)
         # The historical option of that name (reproduction/odl/optim/
         # diagonal_weighted_pe.py:408-410, 500-543) applies the rank-one
         # whitening and mapback on the activation side only.  The engine's

@@ -2,7 +2,8 @@
 
 Launched by torch.distributed.run (one process per GPU, any world size) with
 the output directory, the partition ("lpt" / "layer"), the exchange
-("weights" / "bf16_delta") and optionally "reduce".  Every rank builds the
+("weights" / "bf16_delta") and optionally "reduce" and "nccl" (the weight
+exchange by NCCL all-gather instead of peer stores from the update kernel).  Every rank builds the
 same mini GPT-named model, injects the same statistics and gradients (with
 "reduce": rank-dependent gradients averaging to them, which the optimizer
 reduces itself), runs STEPS sharded steps (statistic all-reduce, owned-matrix
@@ -60,7 +61,7 @@ def oracle_run():
     return init, weights, oracle.state
 
 
-def main(out_dir: str, partition: str, exchange: str, reduce: bool):
+def main(out_dir: str, partition: str, exchange: str, reduce: bool, transport: str = "auto"):
     from sandmuon_b200 import RankOneAWeightedPE
     from sandmuon_b200.workloads import gpt_matrix_model, inject_statistics
     rank = int(os.environ["RANK"])
@@ -74,7 +75,7 @@ def main(out_dir: str, partition: str, exchange: str, reduce: bool):
         if rank == 0:
             torch.save({n: p.detach().cpu() for n, p in model.named_parameters()}, Path(out_dir) / "init.pt")
         opt = RankOneAWeightedPE(model, lr=LR, process_group=dist.group.WORLD, partition=partition,
-                                 exchange=exchange, reduce_gradients=reduce)
+                                 exchange=exchange, reduce_gradients=reduce, transport=transport)
         rng = np.random.default_rng(SEED)
         world = dist.get_world_size()
         for _ in range(STEPS):
@@ -96,6 +97,7 @@ def main(out_dir: str, partition: str, exchange: str, reduce: bool):
                 out[names[i] + "/momentum"] = st["momentum_buffer"].detach().cpu()
         out["/device_status"] = torch.tensor(_lib.device_status(device))
         out["/owned"] = torch.tensor(sum(opt.sharding.owns(p) for p in opt.named_matrices.values()))
+        out["/peer"] = torch.tensor(1 if opt.sharding.peer_bases else 0)
         torch.save(out, Path(out_dir) / f"rank{rank}.pt")
         opt.close()
         dist.barrier()
@@ -104,5 +106,6 @@ def main(out_dir: str, partition: str, exchange: str, reduce: bool):
 
 
 if __name__ == "__main__":
+    extra = sys.argv[4:]
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "lpt", sys.argv[3] if len(sys.argv) > 3 else "weights",
-         len(sys.argv) > 4 and sys.argv[4] == "reduce")
+         "reduce" in extra, "nccl" if "nccl" in extra else "auto")

@@ -30,14 +30,14 @@ def test_library_loads_and_exports_every_declared_symbol(built_library):
     missing = [n for n in declared_symbols() if not hasattr(lib, n)]
     assert not missing, missing
     lib.sm_version.restype = ctypes.c_int
-    assert lib.sm_version() == 2
+    assert lib.sm_version() == 3
 
 
 def test_binding_signatures_cover_the_header(built_library):
     from sandmuon_b200 import _lib
     assert set(_lib.SIGNATURES) == set(declared_symbols())
     lib = _lib.load()
-    assert lib.sm_version() == 2
+    assert lib.sm_version() == 3
 
 
 STRUCTS = ("SmMatrixSpec", "SmStatSpec", "SmPlanSpec", "SmStepArgs", "SmCopySpec", "SmDeltaSpec", "SmAdamTensor")

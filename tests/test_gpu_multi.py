@@ -1,7 +1,9 @@
 """Sharded optimizer steps on 2, 4 and 8 GPUs (NCCL), against the CPU oracle.
 
 Each run launches one process per GPU (tests/multi_gpu_worker.py), two
-sharded steps of a 3-layer GPT-named matrix set.  Every rank must end with
+sharded steps of a 3-layer GPT-named matrix set.  The FP32 weight exchange
+runs by the update kernel's peer stores (the default on CUDA + NCCL) and, in
+its own case, by an NCCL all-gather.  Every rank must end with
 bitwise identical weights, and every matrix's accumulated update (the sum of
 its two steps' directions times the learning rate) must match the oracle's
 within the parity bar: 1e-2 relative Frobenius error, cosine >= 0.999.
@@ -61,6 +63,19 @@ def test_sharded_step_matches_oracle(tmp_path, world, partition, exchange):
     port = 29500 + 10 * world + {"lpt": 1, "layer": 2}[partition] + (4 if exchange == "bf16_delta" else 0)
     ranks = _launch(tmp_path, world, port, partition, exchange)
     _check_against_oracle(ranks, world)
+    if exchange == "weights":  # delivered by the update kernel's peer stores
+        assert all(int(r["/peer"]) == 1 for r in ranks)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_sharded_step_nccl_weight_gather_matches_oracle(tmp_path, world):
+    """transport="nccl": the weights travel by an in-place NCCL all-gather of
+    the flat buffer instead of the update kernel's peer stores."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ranks = _launch(tmp_path, world, 29700 + world, "lpt", "weights", "nccl")
+    _check_against_oracle(ranks, world)
+    assert all(int(r["/peer"]) == 0 for r in ranks)
 
 
 @pytest.mark.parametrize("world", [2, 8])
