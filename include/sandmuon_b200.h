@@ -123,7 +123,8 @@ int sm_stats_accumulate_noalloc(const void* rows, int dtype, int64_t n_rows, int
 typedef struct {
     float* weight;        /* [d_out, d_in] updated in place                  */
     float* momentum;      /* [d_out, d_in] FP32 momentum_buffer              */
-    float* export_to;     /* NULL, or [d_out, d_in]: the updated weight is also
+    float* export_to;     /* NULL, or [d_out, d_in]: the updated weight (or its
+                             BF16 delta, SM_EXPORT_BF16_DELTA) is also
                              written here (a rank's all-gather send slot)    */
     int32_t d_out;
     int32_t d_in;

@@ -338,3 +338,52 @@ def test_exchange_keeps_weights_of_matrices_without_gradient():
             else:
                 expected = 100.0 * i + 10.0 * step + owners[i]
             assert lo[i] == hi[i] == expected, (step, i, lo[i], hi[i], expected)
+
+
+def test_unknown_transport_is_rejected():
+    with pytest.raises(ValueError):
+        MatrixSharding(None, None, transport="rdma")
+
+
+def _transport_worker(rank, world, port, results):
+    """The weight transport on a gloo group: "auto" keeps the NCCL-style
+    all-gather (peer stores need CUDA buffers under NCCL), and "peer" fails on
+    every rank together instead of leaving one rank in a collective."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        opt = _StubOptimizer(gpt_matrix_model(2, 16, 64))
+        auto = MatrixSharding(opt, dist.group.WORLD, transport="auto")
+        out = {"auto_peers": list(auto.peer_bases)}
+        auto.close()  # nothing mapped: no collective, no error
+        opt2 = _StubOptimizer(gpt_matrix_model(2, 16, 64))
+        try:
+            MatrixSharding(opt2, dist.group.WORLD, transport="peer")
+            out["peer"] = "built"
+        except RuntimeError as e:
+            out["peer"] = "refused" if "transport='peer'" in str(e) else f"other: {e}"
+        # the group is still usable after the refusal: the ranks stayed paired
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        out["after"] = float(t.item())
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_weight_transport_falls_back_or_refuses_together_on_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_transport_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank in range(world):
+        res = results[rank]
+        assert res["auto_peers"] == [] and res["peer"] == "refused" and res["after"] == float(world), res
